@@ -1,0 +1,374 @@
+"""Benchmark: ragged decode tokens/s of the Qwen3-0.6B-architecture forward step
+on B200, with the paged-attention kernel's HBM GB/s against the roofline.
+
+Workload (N=1 and per rank): one continuous-batching decode step of a
+Qwen3-0.6B-architecture model (28 layers, hidden 1024, 16/8 heads x 128,
+vocab 151936, bf16, seeded random-init weights) over 256 sequences whose
+contexts are uniform in [1, 4096] (BASELINE config 2's shapes; the KV pages
+hold seeded N(0,1) data and the block ids are a seeded random permutation of
+the pool).  A "step" = one token for each of the 256 sequences.  Inputs (60 GB
+of KV) are far larger than L2, so no flush is needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Multi-GPU: one process per GPU (torchrun), each rank an independent
+data-parallel replica with its own 256 sequences (weak scaling, no data-path
+collective); rank 0 prints the whole-job aggregate.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "ragged decode tokens/s per GPU (Qwen3-0.6B arch); attn HBM GB/s as % of peak"
+UNIT = "tokens/s"
+BATCH = 256
+MAX_CTX = 4096
+SEED = 20261201
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=BATCH)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-kernel-compare", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def contexts(batch: int, seed: int):
+    import numpy as np
+    rng = np.random.Generator(np.random.PCG64(seed))
+    return rng.integers(1, MAX_CTX + 1, batch)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = max(mx, float(parts[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU leg: the reference's CPU path restated (oracle), on a bounded sample
+
+def cpu_sample(nseq: int, steps: int, warmup: int):
+    """Time the torch-CPU f32 restatement of the reference's batched decode
+    (qwen2.rs:630-764, per-sequence contiguous KV caches) on the first `nseq`
+    sequences of this workload, all host threads.  Returns (tokens/s, cores,
+    sample description)."""
+    import numpy as np
+    import torch
+
+    from oracle.qwen_ref import QwenRef, SeqState, qwen3_0_6b, random_weights
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    cfg = qwen3_0_6b()
+    ctx = [int(c) for c in contexts(BATCH, SEED)[:nseq]]
+    model = QwenRef(cfg, random_weights(cfg, SEED))
+    gen = torch.Generator().manual_seed(SEED)
+    states = []
+    for c in ctx:
+        st = SeqState(cfg, c + warmup + steps + 2)
+        st.preallocate(cfg.num_key_value_heads, cfg.hd())
+        st.fill_random(c - 1, gen)
+        states.append(st)
+    ids = [int(t) for t in np.random.Generator(np.random.PCG64(SEED)).integers(0, cfg.vocab_size, nseq)]
+    pos = [c - 1 for c in ctx]
+    t_total = 0.0
+    for s in range(warmup + steps):
+        t0 = time.perf_counter()
+        logits = model.step_decode_batch(states, ids, pos)
+        ids = [int(x) for x in torch.argmax(logits, dim=-1)]
+        dt = time.perf_counter() - t0
+        if s >= warmup:
+            t_total += dt
+        pos = [p + 1 for p in pos]
+    tps = nseq * steps / t_total
+    desc = (f"{nseq} of the {BATCH} sequences (contexts {min(ctx)}..{max(ctx)}, mean {sum(ctx) / nseq:.0f}), "
+            f"{steps} timed decode steps after {warmup} warm-up, f32 torch-CPU restatement of "
+            f"qwen2.rs step_decode_batch")
+    return tps, cores, desc
+
+
+# ---------------------------------------------------------------------------
+# our arm
+
+def cudart():
+    import ctypes
+    lib = ctypes.CDLL("libcudart.so.12")
+    lib.cudaMemcpy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]
+    lib.cudaMemcpy.restype = ctypes.c_int
+    return lib
+
+
+def fill_pool(eng, cfg, pool_blocks, device, seed):
+    """Seeded N(0,1) bf16 K/V in every page: one random chunk copied over each
+    layer's K and V pool (the contents do not change the kernel's traffic)."""
+    import torch
+    rt = cudart()
+    layer_bytes = pool_blocks * cfg.num_key_value_heads * 16 * cfg.hd() * 2
+    chunk = min(layer_bytes, 512 << 20)
+    g = torch.Generator(device=f"cuda:{device}").manual_seed(seed)
+    src = torch.randn(chunk // 2, generator=g, dtype=torch.bfloat16, device=f"cuda:{device}")
+    torch.cuda.synchronize()
+    for layer in range(cfg.num_hidden_layers):
+        for which in (0, 1):
+            base = eng.pool_ptr(layer, which)
+            off = 0
+            while off < layer_bytes:
+                n = min(chunk, layer_bytes - off)
+                rc = rt.cudaMemcpy(base + off, src.data_ptr(), n, 3)  # device to device
+                if rc != 0:
+                    raise RuntimeError(f"cudaMemcpy failed: {rc}")
+                off += n
+    del src
+
+
+def run_ours(args, rank, world, local):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from mini_serve_rs_b200 import engine as E
+    from mini_serve_rs_b200.config import qwen3_0_6b, random_device_weights
+
+    torch.cuda.set_device(local)
+    cfg = qwen3_0_6b()
+    B, K, W = args.batch, args.steps, args.warmup
+    ctx = contexts(B, SEED + rank)
+    extra = W + 2 * K + 2
+    need = [(int(c) + extra + 15) // 16 for c in ctx]
+    pool_blocks = int(sum(need) * 1.05) + 64
+    mbps = (MAX_CTX + extra + 15) // 16 + 1
+    eng = E.Engine(cfg, device=local, pool_blocks=pool_blocks, max_seqs=B, max_tokens_per_step=max(B, 256),
+                   max_blocks_per_seq=mbps, dtype=E.MS_DTYPE_BF16)
+    eng.load_weights(random_device_weights(cfg, SEED, device=f"cuda:{local}"))
+    fill_pool(eng, cfg, pool_blocks, local, SEED + 17 * rank)
+    rng = np.random.Generator(np.random.PCG64(SEED + rank))
+    perm = rng.permutation(pool_blocks).astype(np.int32)
+    ids = np.arange(1, B + 1, dtype=np.uint64)
+    off = 0
+    for i in range(B):
+        prompt = rng.integers(0, cfg.vocab_size, int(ctx[i])).astype(np.uint32)
+        # the whole prompt is cached (synthetic KV); step 1 replays its last token
+        eng.admit(int(ids[i]), prompt, perm[off:off + need[i]], num_cached=int(ctx[i]))
+        off += need[i]
+    stream = torch.cuda.ExternalStream(eng.stream_ptr())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(W):
+        eng.step_launch(ids, None, None, E.MS_STEP_TOKENS_FROM_DEVICE)
+        toks, _ = eng.step_wait()
+    torch.cuda.synchronize()
+
+    # ---- value: device-resident inputs (decode tokens fed back on the device)
+    eng.profile()  # reset the event log
+    eng.set_profiling(True)
+    launches0 = eng.profile()[0]
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for _ in range(K):
+            eng.step_launch(ids, None, None, E.MS_STEP_TOKENS_FROM_DEVICE)
+            toks, _ = eng.step_wait()
+        e1.record(stream)
+        e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    klaunch, alaunch, attn_ms, attn_bytes = eng.profile()
+    eng.set_profiling(False)
+    gpu_launches = klaunch - launches0
+    torch.cuda.synchronize()
+    barrier()
+
+    # ---- e2e: through the public step call with host token arrays
+    pos = np.array([int(c) + W + K for c in ctx], dtype=np.int32)
+    host_toks = np.asarray(toks, dtype=np.uint32)
+    barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(K):
+        host_toks, _ = eng.step(ids, host_toks, pos)
+        pos += 1
+    f1.record(stream)
+    f1.synchronize()
+    ms_e2e = f0.elapsed_time(f1)
+    barrier()
+
+    t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=f"cuda:{local}")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, ms_e2e = float(t[0]), float(t[1])
+    res = {
+        "ms": ms, "ms_e2e": ms_e2e, "gpu_launches": gpu_launches, "clocks": clk.summary(),
+        "attn_launches": alaunch, "attn_ms": attn_ms, "attn_bytes": attn_bytes,
+        "h2d": (4 * B + 3 * B) * 4, "d2h": B * 4 + 4, "ctx_mean": float(np.mean(ctx)),
+        "memory": eng.memory(),
+    }
+    eng.close()
+    return res
+
+
+def traffic_per_launch():
+    """dram bytes (read + write) per attention launch from the committed ncu
+    summary of this workload, if one exists."""
+    p = ROOT / "profiles" / "k3_attention_traffic.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["dram_bytes_per_launch"])
+        except (KeyError, ValueError):
+            return None
+    return None
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    n = world if world > 1 else args.gpus
+    cfg_desc = {"workload": "Qwen3-0.6B-arch decode step, 256 seqs x ctx U[1,4096] (BASELINE config 2 shapes "
+                            "through the full 28-layer model)",
+                "model": "qwen3-0.6b-arch", "global_batch": args.batch * n, "seqs_per_gpu": args.batch,
+                "ctx": "uniform[1,4096] at admission, +1 per step", "block_size": 16,
+                "parallelism": f"dp{n} (independent replicas)", "l2": "inputs (60 GB KV/GPU) >> L2, no flush"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        steps = max(1, min(args.steps, 5))
+        warm = max(1, min(args.warmup, 1))
+        tps, cores, desc = cpu_sample(8, steps, warm)
+        line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": n,
+                "steps": steps, "warmup": warm, "ms_per_step": 8 / tps * 1000, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg_desc,
+                "cpu_baseline": {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": desc},
+                "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device(f"cuda:{local}"))
+    try:
+        r = run_ours(args, rank, world, local)
+    finally:
+        pass
+    if rank == 0:
+        B, K = args.batch, args.steps
+        value = n * B * K / (r["ms"] / 1000.0)
+        e2e = n * B * K / (r["ms_e2e"] / 1000.0)
+        peak, peak_kind = peaks()
+        per_launch_ms = r["attn_ms"] / max(1, r["attn_launches"])
+        per_launch_bytes = r["attn_bytes"] / max(1, r["attn_launches"])
+        achieved = per_launch_bytes / (per_launch_ms / 1000.0) / 1e9
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n, "steps": K, "warmup": args.warmup,
+                "ms_per_step": r["ms"] / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic (seeded random-init weights, N(0,1) KV)", "config": cfg_desc,
+                "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"],
+                        "ms_per_step": r["ms_e2e"] / K},
+                "gpu_launches": r["gpu_launches"], "clocks": r["clocks"],
+                "roofline": {"kernel": "paged_attention_kernel (K3 split-K GQA decode + combine)", "bound": "hbm",
+                             "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                             "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                             "traffic": traffic_per_launch(), "algorithmic_bytes_per_launch": per_launch_bytes,
+                             "ms_per_launch": per_launch_ms, "launches": r["attn_launches"],
+                             "share_of_step": r["attn_ms"] / r["ms"]},
+                "memory_bytes": r["memory"]}
+        if world <= 1 and not args.no_cpu_baseline:
+            tps, cores, desc = cpu_sample(8, 2, 1)
+            line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": desc}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

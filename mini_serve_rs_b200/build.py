@@ -1,0 +1,82 @@
+"""Build libms_engine.so in-tree for sm_100a (B200).
+
+    python -m mini_serve_rs_b200.build [--force] [--verbose]
+
+Each csrc/*.cu is compiled to an object under _build/ (skipped when newer
+than its sources), then linked with cuBLAS and the CUDA runtime into
+mini_serve_rs_b200/libms_engine.so.  nvcc cross-compiles: no GPU is needed.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+BUILD = ROOT / "_build" / "ms_engine"
+LIB = PKG / "libms_engine.so"
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def nvcc() -> str:
+    for c in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", shutil.which("nvcc")):
+        if c and Path(c).exists():
+            return c
+    raise RuntimeError("nvcc not found")
+
+
+def cuda_home() -> Path:
+    return Path(nvcc()).resolve().parent.parent
+
+
+def _compile(src: Path, verbose: bool, extra: list) -> Path:
+    obj = BUILD / (src.stem + ".o")
+    deps = [src] + list(CSRC.glob("*.h")) + list(CSRC.glob("*.cuh")) + [ROOT / "include" / "ms_engine.h"]
+    if obj.exists() and obj.stat().st_mtime > max(d.stat().st_mtime for d in deps):
+        return obj
+    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O3",
+           "--expt-relaxed-constexpr", "-I", str(ROOT / "include"), "-c", str(src), "-o", str(obj), *extra]
+    if verbose:
+        cmd.append("-Xptxas=-v")
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed on {src.name}:\n{r.stdout}\n{r.stderr}")
+    if verbose and r.stderr:
+        print(r.stderr, file=sys.stderr)
+    return obj
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    BUILD.mkdir(parents=True, exist_ok=True)
+    if force:
+        for o in BUILD.glob("*.o"):
+            o.unlink()
+    srcs = sorted(CSRC.glob("*.cu"))
+    with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
+        objs = list(ex.map(lambda s: _compile(s, verbose, []), srcs))
+    if LIB.exists() and not force and LIB.stat().st_mtime > max(o.stat().st_mtime for o in objs):
+        return LIB
+    lib64 = cuda_home() / "lib64"
+    tmp = LIB.with_suffix(".so.tmp")
+    cmd = [nvcc(), *ARCH, "-shared", "-Xcompiler", "-fPIC", *map(str, objs), "-o", str(tmp),
+           "-L", str(lib64), "-lcublas", "-lcudart", "-Xlinker", f"-rpath,{lib64}"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--verbose", action="store_true")
+    a = ap.parse_args()
+    print(build(a.force, a.verbose))

@@ -1,0 +1,126 @@
+// Shared device helpers for the sm_100a kernels of libms_engine.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ms {
+
+constexpr int kWarp = 32;
+constexpr unsigned kFull = 0xffffffffu;
+
+// ---- element conversion ----------------------------------------------------
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+template <> struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+template <> struct Elem<__half> {
+  static __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
+};
+
+// Round an f32 value to the storage type and back (the "cast to model dtype"
+// points of the reference's Candle ops).
+template <typename T> __device__ __forceinline__ float round_to(float v) {
+  return Elem<T>::to_f(Elem<T>::from_f(v));
+}
+
+// Load / store 4 consecutive elements as f32.
+template <typename T> struct Vec4;
+template <> struct Vec4<float> {
+  static __device__ __forceinline__ void load(const float *p, float (&o)[4]) {
+    float4 v = *reinterpret_cast<const float4 *>(p);
+    o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+  }
+  static __device__ __forceinline__ void store(float *p, const float (&o)[4]) {
+    *reinterpret_cast<float4 *>(p) = make_float4(o[0], o[1], o[2], o[3]);
+  }
+};
+template <> struct Vec4<__nv_bfloat16> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16 *p, float (&o)[4]) {
+    uint2 u = *reinterpret_cast<const uint2 *>(p);
+    o[0] = __uint_as_float(u.x << 16); o[1] = __uint_as_float(u.x & 0xffff0000u);
+    o[2] = __uint_as_float(u.y << 16); o[3] = __uint_as_float(u.y & 0xffff0000u);
+  }
+  static __device__ __forceinline__ void store(__nv_bfloat16 *p, const float (&o)[4]) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(o[0], o[1]);
+    __nv_bfloat162 b = __floats2bfloat162_rn(o[2], o[3]);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t *>(&a);
+    u.y = *reinterpret_cast<uint32_t *>(&b);
+    *reinterpret_cast<uint2 *>(p) = u;
+  }
+};
+template <> struct Vec4<__half> {
+  static __device__ __forceinline__ void load(const __half *p, float (&o)[4]) {
+    uint2 u = *reinterpret_cast<const uint2 *>(p);
+    __half2 a = *reinterpret_cast<__half2 *>(&u.x);
+    __half2 b = *reinterpret_cast<__half2 *>(&u.y);
+    float2 fa = __half22float2(a), fb = __half22float2(b);
+    o[0] = fa.x; o[1] = fa.y; o[2] = fb.x; o[3] = fb.y;
+  }
+  static __device__ __forceinline__ void store(__half *p, const float (&o)[4]) {
+    __half2 a = __floats2half2_rn(o[0], o[1]);
+    __half2 b = __floats2half2_rn(o[2], o[3]);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t *>(&a);
+    u.y = *reinterpret_cast<uint32_t *>(&b);
+    *reinterpret_cast<uint2 *>(p) = u;
+  }
+};
+
+// Load / store 2 consecutive elements as f32.
+template <typename T> struct Vec2;
+template <> struct Vec2<float> {
+  static __device__ __forceinline__ void load(const float *p, float (&o)[2]) {
+    float2 v = *reinterpret_cast<const float2 *>(p);
+    o[0] = v.x; o[1] = v.y;
+  }
+  static __device__ __forceinline__ void store(float *p, const float (&o)[2]) {
+    *reinterpret_cast<float2 *>(p) = make_float2(o[0], o[1]);
+  }
+};
+template <> struct Vec2<__nv_bfloat16> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16 *p, float (&o)[2]) {
+    uint32_t u = *reinterpret_cast<const uint32_t *>(p);
+    o[0] = __uint_as_float(u << 16); o[1] = __uint_as_float(u & 0xffff0000u);
+  }
+  static __device__ __forceinline__ void store(__nv_bfloat16 *p, const float (&o)[2]) {
+    *reinterpret_cast<__nv_bfloat162 *>(p) = __floats2bfloat162_rn(o[0], o[1]);
+  }
+};
+template <> struct Vec2<__half> {
+  static __device__ __forceinline__ void load(const __half *p, float (&o)[2]) {
+    float2 f = __half22float2(*reinterpret_cast<const __half2 *>(p));
+    o[0] = f.x; o[1] = f.y;
+  }
+  static __device__ __forceinline__ void store(__half *p, const float (&o)[2]) {
+    *reinterpret_cast<__half2 *>(p) = __floats2half2_rn(o[0], o[1]);
+  }
+};
+
+// ---- warp reductions ---------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+  return v;
+}
+
+// Device-side status word: kernels record a problem here instead of faulting.
+// Bits: 1 = mbarrier wait gave up, 2 = index out of range.
+constexpr unsigned kStatusWaitTimeout = 1u;
+constexpr unsigned kStatusBadIndex = 2u;
+
+}  // namespace ms

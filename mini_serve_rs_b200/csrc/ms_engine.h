@@ -1,0 +1,142 @@
+// Engine state behind the C ABI of include/ms_engine.h.
+#pragma once
+
+#include <cublas_v2.h>
+#include <cuda_runtime.h>
+
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "ms_internal.h"
+
+namespace ms {
+
+// One admitted request: what CandleBackend keeps per request
+// (src/backends/candle.rs:405-418) minus the contiguous KV clone -- its K/V
+// now live in the shared paged pool at the scheduler's block ids.
+struct Seq {
+  int slot = -1;                  // device block-table row
+  std::vector<uint32_t> prompt;
+  std::vector<int32_t> blocks;    // host mirror of the row
+  int synced = 0;                 // leading entries already on the device
+  int cached = 0;                 // tokens whose K/V sit in the pool
+  bool prefilled = false;
+};
+
+struct LayerW {
+  void *ln1 = nullptr, *ln2 = nullptr;
+  void *w_qkv = nullptr, *b_qkv = nullptr;  // [(Hq+2Hkv)*D, H], [(Hq+2Hkv)*D]
+  void *q_norm = nullptr, *k_norm = nullptr;
+  void *w_o = nullptr;                      // [H, Hq*D]
+  void *w_gu = nullptr;                     // [2I, H]  gate rows then up rows
+  void *w_down = nullptr;                   // [H, I]
+};
+
+struct Engine {
+  ms_model_cfg cfg{};
+  ms_engine_opts opts{};
+  int dev = 0;
+  cudaStream_t stream = nullptr;
+  cublasHandle_t blas = nullptr;
+  void *blas_ws = nullptr;
+  int dtype = MS_DTYPE_BF16;
+  size_t esize = 2;
+  int D = 128, hq = 0, hkv = 0, H = 0, I = 0, V = 0, L = 0;
+  int qkv_dim = 0;
+
+  // weights (one allocation)
+  void *wbuf = nullptr;
+  size_t wbytes = 0;
+  void *embed = nullptr, *lm_head = nullptr, *final_norm = nullptr;
+  std::vector<LayerW> layers;
+  std::unordered_map<std::string, int> loaded;  // name -> times loaded
+  std::vector<std::string> required;
+  bool finalized = false;
+
+  // RoPE tables [rope_len, D/2] in the model dtype
+  void *cos_t = nullptr, *sin_t = nullptr;
+  int rope_len = 0;
+
+  // paged pool [L][2][pool_blocks][hkv][16][D]
+  void *pool = nullptr;
+  size_t pool_bytes = 0;
+  size_t layer_pool_elems = 0;  // pool_blocks * hkv * 16 * D
+
+  // per-slot device state
+  int32_t *d_block_tables = nullptr;  // [max_seqs][max_blocks_per_seq]
+  int32_t *d_slot_last = nullptr;     // [max_seqs]
+  unsigned *d_status = nullptr;
+
+  // step buffers
+  void *sbuf = nullptr;
+  size_t sbytes = 0;
+  int32_t *d_in = nullptr;  // uploaded step description
+  size_t in_cap = 0;        // int32 elements
+  int32_t *d_cu = nullptr, *d_pos = nullptr, *d_row_table = nullptr, *d_row_ctx = nullptr;
+  int32_t *d_last_index = nullptr, *d_next = nullptr;
+  int64_t *d_slots = nullptr;
+  void *x_resid = nullptr, *x_norm = nullptr, *x_tmp = nullptr, *qkv = nullptr, *qbuf = nullptr,
+       *attn = nullptr, *gu = nullptr, *act = nullptr, *last_norm = nullptr;
+  float *logits = nullptr;
+  void *attn_ws = nullptr;
+  size_t attn_ws_bytes = 0;
+
+  // pinned host staging
+  int32_t *h_in = nullptr;
+  int32_t *h_next = nullptr;
+  unsigned *h_status = nullptr;
+  cudaEvent_t done_ev = nullptr;
+
+  // instrumentation
+  int64_t kernel_launches = 0;
+  bool profiling = false;
+  std::vector<cudaEvent_t> prof_ev;  // pairs: start, end
+  size_t prof_used = 0;              // events in use (2 per bracketed launch)
+  double prof_bytes = 0.0;
+
+  // host bookkeeping
+  std::unordered_map<uint64_t, Seq> seqs;
+  std::vector<int> free_slots;
+  bool healthy = true;
+  int inject = 0;
+  std::string err;
+
+  // last step
+  bool pending = false;
+  int last_nseq = 0, last_T = 0, last_max_ctx = 0;
+  std::vector<int> last_slots;
+  std::vector<uint8_t> last_flags;
+  std::vector<uint64_t> last_ids;
+
+  int fail(int code, const std::string &msg) {
+    err = msg;
+    if (code == MS_E_DEVICE || code == MS_E_INJECTED) quarantine();
+    return code;
+  }
+  void quarantine() {
+    // candle.rs:689-696: a BackendError clears every request's state
+    healthy = false;
+    seqs.clear();
+    free_slots.clear();
+    for (int i = opts.max_seqs - 1; i >= 0; --i) free_slots.push_back(i);
+    pending = false;
+  }
+};
+
+// implemented across ms_engine*.cu
+// create_impl fills a caller-allocated Engine; destroy_impl releases its
+// device resources (the caller deletes the object).
+int create_impl(const ms_model_cfg *cfg, const ms_engine_opts *opts, Engine *eng);
+void destroy_impl(Engine *eng);
+int load_weight_impl(Engine *eng, const char *name, const void *data, int64_t numel, int src_dtype,
+                     int src_on_device);
+int finalize_impl(Engine *eng);
+int seq_admit_impl(Engine *eng, uint64_t id, const uint32_t *prompt, int prompt_len, const int32_t *blocks,
+                   int nblocks, int num_cached);
+int seq_append_block_impl(Engine *eng, uint64_t id, int32_t block);
+int seq_release_impl(Engine *eng, uint64_t id);
+int step_launch_impl(Engine *eng, const ms_step_desc *desc);
+int step_wait_impl(Engine *eng, uint32_t *out_tokens, uint8_t *out_flags);
+
+}  // namespace ms

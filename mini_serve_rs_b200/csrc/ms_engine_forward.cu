@@ -1,0 +1,170 @@
+// Engine forward: the device work of one packed step, enqueued on the engine
+// stream.  Order of operations per layer follows DecoderLayer::forward
+// (src/backends/qwen2.rs:414-428) and the batched decode of qwen2.rs:663-757;
+// the final norm and lm_head run on each sequence's last packed row only
+// (qwen2.rs:620-626, 759-763).
+#include <algorithm>
+#include <string>
+
+#include "ms_engine.h"
+
+namespace ms {
+
+#define MS_CUDA_TRY(expr)                                                                    \
+  do {                                                                                       \
+    cudaError_t _e = (expr);                                                                 \
+    if (_e != cudaSuccess)                                                                   \
+      return eng->fail(MS_E_DEVICE, std::string(#expr) + ": " + cudaGetErrorString(_e));     \
+  } while (0)
+
+#define MS_BLAS_TRY(expr)                                                                    \
+  do {                                                                                       \
+    cublasStatus_t _s = (expr);                                                              \
+    if (_s != CUBLAS_STATUS_SUCCESS)                                                         \
+      return eng->fail(MS_E_DEVICE, std::string(#expr) + ": cublas status " + std::to_string(int(_s))); \
+  } while (0)
+
+namespace {
+
+cudaDataType_t cuda_type(int dt) { return dt == MS_DTYPE_F32 ? CUDA_R_32F : CUDA_R_16BF; }
+
+// Y[T, out] = X[T, in] * W[out, in]^T (candle_nn::Linear, no bias): a
+// column-major GEMM Y^T = W^T(op T) * X^T with f32 accumulation.
+cublasStatus_t linear(Engine *eng, const void *W, const void *X, void *Y, int out, int T, int in,
+                      bool f32_out = false) {
+  const float one = 1.f, zero = 0.f;
+  const cudaDataType_t t = cuda_type(eng->dtype);
+  return cublasGemmEx(eng->blas, CUBLAS_OP_T, CUBLAS_OP_N, out, T, in, &one, W, t, in, X, t, in, &zero, Y,
+                      f32_out ? CUDA_R_32F : t, out, CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT);
+}
+
+}  // namespace
+
+namespace {
+// Records the next profiling event on the engine stream (created on first use).
+cudaError_t prof_mark(Engine *eng) {
+  if (eng->prof_used == eng->prof_ev.size()) {
+    cudaEvent_t e;
+    cudaError_t err = cudaEventCreate(&e);
+    if (err != cudaSuccess) return err;
+    eng->prof_ev.push_back(e);
+  }
+  return cudaEventRecord(eng->prof_ev[eng->prof_used++], eng->stream);
+}
+}  // namespace
+
+int enqueue_forward(Engine *eng, int S, int T, int max_ctx, long long total_blocks, int nd, double total_ctx) {
+  cudaStream_t st = eng->stream;
+  const int dt = eng->dtype;
+  const float eps = float(eng->cfg.rms_norm_eps);
+  const size_t es = eng->esize;
+
+  MS_CUDA_TRY(cudaMemsetAsync(eng->d_status, 0, sizeof(unsigned), st));
+
+  // ---- K1: pack ----
+  int32_t *d = eng->d_in;
+  PackArgs pa{};
+  pa.seq_row = d;
+  pa.seq_ntok = d + S;
+  pa.seq_start = d + 2 * S;
+  pa.num_seqs = S;
+  pa.tokens = d + 3 * S;
+  pa.delta_row = pa.tokens + T;
+  pa.delta_idx = pa.delta_row + nd;
+  pa.delta_block = pa.delta_idx + nd;
+  pa.num_deltas = nd;
+  pa.block_tables = eng->d_block_tables;
+  pa.max_blocks_per_seq = eng->opts.max_blocks_per_seq;
+  pa.block_size = eng->opts.block_size;
+  pa.cu_seqlens = eng->d_cu;
+  pa.positions = eng->d_pos;
+  pa.slot_mapping = eng->d_slots;
+  pa.row_table = eng->d_row_table;
+  pa.row_ctx = eng->d_row_ctx;
+  pa.last_index = eng->d_last_index;
+  pa.slot_last_tok = eng->d_slot_last;
+  pa.tokens_from_device = 1;
+  pa.status = eng->d_status;
+  pa.pool_blocks = eng->opts.pool_blocks;
+  MS_CUDA_TRY(launch_pack(pa, st));
+  const int32_t *tokens = pa.tokens;
+
+  // attention partitioning: enough CTAs to fill the GPU, workspace bounded
+  int part = choose_partition_blocks(T, eng->hkv, max_ctx, total_blocks);
+  while (attention_workspace_bytes(T, eng->hq, max_ctx, part) > int64_t(eng->attn_ws_bytes)) part *= 2;
+
+  // ---- layer 0 input: embedding gather + input norm (K4 without residual) ----
+  MS_CUDA_TRY(launch_add_rmsnorm(eng->embed, nullptr, tokens, eng->layers[0].ln1, eng->x_resid, eng->x_norm, T,
+                                 eng->H, eps, dt, st));
+  const size_t pool_layer_bytes = eng->layer_pool_elems * es;
+  for (int l = 0; l < eng->L; ++l) {
+    const LayerW &w = eng->layers[l];
+    char *kp = static_cast<char *>(eng->pool) + size_t(2 * l) * pool_layer_bytes;
+    char *vp = kp + pool_layer_bytes;
+    // QKV projection, then bias / QK-norm / RoPE / paged append
+    MS_BLAS_TRY(linear(eng, w.w_qkv, eng->x_norm, eng->qkv, eng->qkv_dim, T, eng->H));
+    MS_CUDA_TRY(launch_qk_norm_rope_append(eng->qkv, w.b_qkv, w.q_norm, w.k_norm, eng->cos_t, eng->sin_t, eng->d_pos,
+                                           eng->d_slots, eng->qbuf, kp, vp, T, eng->hq, eng->hkv, eng->D,
+                                           eng->opts.block_size, eps, dt, st));
+    // paged attention over each row's causal context
+    AttnArgs a{};
+    a.q = eng->qbuf;
+    a.k_pool = kp;
+    a.v_pool = vp;
+    a.block_tables = eng->d_block_tables;
+    a.max_blocks_per_seq = eng->opts.max_blocks_per_seq;
+    a.row_table = eng->d_row_table;
+    a.row_ctx = eng->d_row_ctx;
+    a.num_rows = T;
+    a.max_ctx = max_ctx;
+    a.out = eng->attn;
+    a.num_heads = eng->hq;
+    a.num_kv_heads = eng->hkv;
+    a.head_dim = eng->D;
+    a.block_size = eng->opts.block_size;
+    a.scale = 1.0f / std::sqrt(float(eng->D));
+    a.part_blocks = part;
+    a.workspace = eng->attn_ws;
+    a.workspace_bytes = int64_t(eng->attn_ws_bytes);
+    a.dtype = dt;
+    a.status = eng->d_status;
+    if (eng->profiling) MS_CUDA_TRY(prof_mark(eng));
+    MS_CUDA_TRY(launch_paged_attention(a, st));
+    if (eng->profiling) {
+      MS_CUDA_TRY(prof_mark(eng));
+      // K and V rows read, q in, out written, one table entry per page, one ctx per row
+      eng->prof_bytes += total_ctx * eng->hkv * eng->D * 2.0 * es + 2.0 * T * eng->hq * eng->D * es +
+                         double(total_blocks) * 4.0 + 4.0 * T;
+    }
+    // o_proj, residual add + post-attention norm
+    MS_BLAS_TRY(linear(eng, w.w_o, eng->attn, eng->x_tmp, eng->H, T, eng->hq * eng->D));
+    MS_CUDA_TRY(launch_add_rmsnorm(eng->x_tmp, eng->x_resid, nullptr, w.ln2, eng->x_resid, eng->x_norm, T, eng->H,
+                                   eps, dt, st));
+    // MLP
+    MS_BLAS_TRY(linear(eng, w.w_gu, eng->x_norm, eng->gu, 2 * eng->I, T, eng->H));
+    MS_CUDA_TRY(launch_silu_mul(eng->gu, eng->act, T, eng->I, dt, st));
+    MS_BLAS_TRY(linear(eng, w.w_down, eng->act, eng->x_tmp, eng->H, T, eng->I));
+    if (l + 1 < eng->L) {
+      MS_CUDA_TRY(launch_add_rmsnorm(eng->x_tmp, eng->x_resid, nullptr, eng->layers[l + 1].ln1, eng->x_resid,
+                                     eng->x_norm, T, eng->H, eps, dt, st));
+    } else {
+      // last layer: residual add + final norm on each sequence's last row only
+      MS_CUDA_TRY(launch_add_rmsnorm(eng->x_tmp, eng->x_resid, eng->d_last_index, eng->final_norm, nullptr,
+                                     eng->last_norm, S, eng->H, eps, dt, st));
+    }
+  }
+  // lm_head in f32 output, greedy argmax, tokens back to the host
+  MS_BLAS_TRY(linear(eng, eng->lm_head, eng->last_norm, eng->logits, eng->V, S, eng->H, true));
+  MS_CUDA_TRY(launch_argmax(eng->logits, S, eng->V, eng->d_next, pa.seq_row, eng->d_slot_last, st));
+  {
+    const int max_blk = (max_ctx + 15) / 16;
+    const int parts = (max_blk + part - 1) / part;
+    eng->kernel_launches += 3 + int64_t(eng->L) * (5 + (parts > 1 ? 1 : 0));
+  }
+  MS_CUDA_TRY(cudaMemcpyAsync(eng->h_next, eng->d_next, size_t(S) * 4, cudaMemcpyDeviceToHost, st));
+  MS_CUDA_TRY(cudaMemcpyAsync(eng->h_status, eng->d_status, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+  MS_CUDA_TRY(cudaEventRecord(eng->done_ev, st));
+  return MS_OK;
+}
+
+}  // namespace ms

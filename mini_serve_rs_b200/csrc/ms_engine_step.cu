@@ -1,0 +1,190 @@
+// Engine step: one continuous-batching iteration (ModelBackend::step_batch,
+// src/backends/traits.rs:196-199; CandleBackend::step_batch,
+// src/backends/candle.rs:377-698).
+//
+// The reference runs every new sequence's prefill alone and then one batched
+// decode; here all of them go into one packed ragged batch: prefill rows
+// carry their whole (uncached) prompt, decode rows one token at
+// prompt + outputs - 1 (candle.rs:622-628).  Each sequence gets its greedy
+// token from the f32 logits of its last packed row (candle.rs:737-751).
+#include <algorithm>
+#include <string>
+
+#include "ms_engine.h"
+
+namespace ms {
+
+#define MS_CUDA_TRY(expr)                                                                    \
+  do {                                                                                       \
+    cudaError_t _e = (expr);                                                                 \
+    if (_e != cudaSuccess)                                                                   \
+      return eng->fail(MS_E_DEVICE, std::string(#expr) + ": " + cudaGetErrorString(_e));     \
+  } while (0)
+
+namespace {
+
+struct RowPlan {
+  Seq *seq;
+  int ntok, start;
+  bool prefill;
+};
+
+int grow_staging(Engine *eng, size_t elems) {
+  if (elems <= eng->in_cap) return MS_OK;
+  size_t cap = std::max<size_t>(elems, eng->in_cap * 2);
+  cap = std::max<size_t>(cap, 1 << 16);
+  if (eng->h_in) cudaFreeHost(eng->h_in);
+  if (eng->d_in) cudaFree(eng->d_in);
+  eng->h_in = nullptr;
+  eng->d_in = nullptr;
+  eng->in_cap = 0;
+  MS_CUDA_TRY(cudaMallocHost(&eng->h_in, cap * 4));
+  MS_CUDA_TRY(cudaMalloc(&eng->d_in, cap * 4));
+  eng->in_cap = cap;
+  return MS_OK;
+}
+
+}  // namespace
+
+int enqueue_forward(Engine *eng, int S, int T, int max_ctx, long long total_blocks, int nd, double total_ctx);
+
+int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
+  if (!eng->healthy) {
+    eng->err = "Backend quarantined; restart required";
+    return MS_E_QUARANTINED;
+  }
+  if (!eng->finalized) return eng->fail(MS_E_INVALID, "engine not finalized (weights missing)");
+  if (eng->pending) return eng->fail(MS_E_INVALID, "ms_step_launch called twice without ms_step_wait");
+  if (!desc) return eng->fail(MS_E_INVALID, "null step description");
+  if (eng->inject) {
+    eng->inject = 0;
+    return eng->fail(MS_E_INJECTED, "injected fault");
+  }
+  const int S = desc->num_seqs;
+  if (S < 0 || S > eng->opts.max_seqs) return eng->fail(MS_E_INVALID, "num_seqs out of range");
+  if (S == 0) {  // candle.rs:381-383: an empty batch is a no-op
+    eng->pending = true;
+    eng->last_nseq = 0;
+    eng->last_T = 0;
+    return MS_OK;
+  }
+  if (!desc->seq_ids) return eng->fail(MS_E_INVALID, "null seq_ids");
+  eng->last_ids.assign(desc->seq_ids, desc->seq_ids + S);
+  const bool from_dev = (desc->flags & MS_STEP_TOKENS_FROM_DEVICE) != 0;
+
+  // ---- plan (validate everything before touching state) ----
+  std::vector<RowPlan> plan(S);
+  std::unordered_map<uint64_t, int> seen;
+  int T = 0, nd = 0, max_ctx = 0;
+  long long total_blocks = 0;
+  double total_ctx = 0.0;  // sum over packed rows of the keys each row attends to
+  for (int i = 0; i < S; ++i) {
+    const uint64_t id = desc->seq_ids[i];
+    auto it = eng->seqs.find(id);
+    if (it == eng->seqs.end()) return eng->fail(MS_E_NOT_FOUND, "unknown sequence id " + std::to_string(id));
+    if (!seen.emplace(id, i).second) return eng->fail(MS_E_INVALID, "sequence listed twice in one step");
+    Seq &s = it->second;
+    RowPlan &r = plan[i];
+    r.seq = &s;
+    r.prefill = !s.prefilled;
+    const int plen = int(s.prompt.size());
+    if (r.prefill) {
+      if (s.cached >= plen) {  // exact cached prefix: replay the last prompt token (candle.rs:447-455)
+        r.start = plen - 1;
+        r.ntok = 1;
+      } else {
+        r.start = s.cached;
+        r.ntok = plen - s.cached;
+      }
+    } else {
+      r.start = s.cached;
+      r.ntok = 1;
+      if (desc->positions && desc->positions[i] != s.cached)
+        return eng->fail(MS_E_INVALID, "decode position " + std::to_string(desc->positions[i]) +
+                                           " does not match the engine's " + std::to_string(s.cached));
+      if (!from_dev) {
+        if (!desc->input_tokens) return eng->fail(MS_E_INVALID, "null input_tokens");
+        if (desc->input_tokens[i] >= uint32_t(eng->V)) return eng->fail(MS_E_INVALID, "input token outside the vocabulary");
+      }
+    }
+    const int end = r.start + r.ntok;
+    if (end > eng->rope_len) return eng->fail(MS_E_TOKEN_LIMIT, "position beyond max_position_embeddings");
+    if (int64_t(end) > int64_t(s.blocks.size()) * eng->opts.block_size)
+      return eng->fail(MS_E_INVALID, "block table too short for position " + std::to_string(end - 1));
+    T += r.ntok;
+    nd += int(s.blocks.size()) - s.synced;
+    max_ctx = std::max(max_ctx, end);
+    for (int j = 0; j < r.ntok; ++j) {
+      total_ctx += double(r.start + j + 1);
+      total_blocks += (r.start + j + 1 + 15) / 16;
+    }
+  }
+  if (T > eng->opts.max_tokens_per_step)
+    return eng->fail(MS_E_PRESSURE, "step needs " + std::to_string(T) + " tokens, engine holds " +
+                                        std::to_string(eng->opts.max_tokens_per_step));
+
+  // ---- stage the step description: one pinned buffer, one upload ----
+  const size_t need = size_t(3) * S + T + size_t(3) * nd;
+  int rc = grow_staging(eng, need);
+  if (rc != MS_OK) return rc;
+  int32_t *h = eng->h_in;
+  int32_t *h_row = h, *h_ntok = h + S, *h_start = h + 2 * S, *h_tok = h + 3 * S;
+  int32_t *h_drow = h_tok + T, *h_didx = h_drow + nd, *h_dblk = h_didx + nd;
+  int t = 0, d = 0;
+  for (int i = 0; i < S; ++i) {
+    const RowPlan &r = plan[i];
+    Seq &s = *r.seq;
+    h_row[i] = s.slot;
+    h_ntok[i] = r.ntok;
+    h_start[i] = r.start;
+    if (r.prefill) {
+      for (int j = 0; j < r.ntok; ++j) h_tok[t++] = int32_t(s.prompt[r.start + j]);
+    } else {
+      h_tok[t++] = from_dev ? -1 : int32_t(desc->input_tokens[i]);
+    }
+    for (int b = s.synced; b < int(s.blocks.size()); ++b, ++d) {
+      h_drow[d] = s.slot;
+      h_didx[d] = b;
+      h_dblk[d] = s.blocks[b];
+    }
+  }
+  MS_CUDA_TRY(cudaSetDevice(eng->dev));
+  MS_CUDA_TRY(cudaMemcpyAsync(eng->d_in, eng->h_in, need * 4, cudaMemcpyHostToDevice, eng->stream));
+  rc = enqueue_forward(eng, S, T, max_ctx, total_blocks, nd, total_ctx);
+  if (rc != MS_OK) return rc;
+
+  // ---- commit host state ----
+  eng->last_slots.resize(S);
+  eng->last_flags.assign(S, 0);
+  for (int i = 0; i < S; ++i) {
+    RowPlan &r = plan[i];
+    eng->last_slots[i] = r.seq->slot;
+    if (r.prefill) eng->last_flags[i] = MS_FLAG_PREFILLED;
+    r.seq->cached = r.start + r.ntok;
+    r.seq->prefilled = true;
+    r.seq->synced = int(r.seq->blocks.size());
+  }
+  eng->last_nseq = S;
+  eng->last_T = T;
+  eng->last_max_ctx = max_ctx;
+  eng->pending = true;
+  return MS_OK;
+}
+
+int step_wait_impl(Engine *eng, uint32_t *out_tokens, uint8_t *out_flags) {
+  if (!eng->pending) return eng->fail(MS_E_INVALID, "ms_step_wait without a launched step");
+  eng->pending = false;
+  const int S = eng->last_nseq;
+  if (S == 0) return MS_OK;
+  MS_CUDA_TRY(cudaEventSynchronize(eng->done_ev));
+  if (*eng->h_status != 0)
+    return eng->fail(MS_E_DEVICE, "device status word " + std::to_string(*eng->h_status) +
+                                      " (1 = bounded wait gave up, 2 = index out of range)");
+  if (out_tokens)
+    for (int i = 0; i < S; ++i) out_tokens[i] = uint32_t(eng->h_next[i]);
+  if (out_flags)
+    for (int i = 0; i < S; ++i) out_flags[i] = eng->last_flags[i];
+  return MS_OK;
+}
+
+}  // namespace ms

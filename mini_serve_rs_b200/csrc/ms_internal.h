@@ -1,0 +1,86 @@
+// Internal launcher interfaces shared by the kernel files and the engine.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/ms_engine.h"
+
+namespace ms {
+
+struct AttnArgs {
+  const void *q;
+  const void *k_pool;
+  const void *v_pool;
+  const int32_t *block_tables;
+  int max_blocks_per_seq;
+  const int32_t *row_table;
+  const int32_t *row_ctx;
+  int num_rows;
+  int max_ctx;
+  void *out;
+  int num_heads;
+  int num_kv_heads;
+  int head_dim;
+  int block_size;
+  float scale;
+  int part_blocks;
+  void *workspace;
+  int64_t workspace_bytes;
+  int dtype;
+  unsigned *status;  // device status word (may be null)
+};
+
+cudaError_t launch_paged_attention(const AttnArgs &a, cudaStream_t stream);
+int choose_partition_blocks(int num_rows, int num_kv_heads, int max_ctx, long long total_blocks);
+int64_t attention_workspace_bytes(int num_rows, int num_heads, int max_ctx, int part_blocks);
+
+cudaError_t launch_add_rmsnorm(const void *x, const void *r, const int32_t *row_index, const void *w,
+                               void *resid_out, void *norm_out, int rows, int hidden, float eps,
+                               int dtype, cudaStream_t stream);
+
+cudaError_t launch_qk_norm_rope_append(const void *qkv, const void *bias, const void *q_norm_w,
+                                       const void *k_norm_w, const void *cos_table,
+                                       const void *sin_table, const int32_t *positions,
+                                       const int64_t *slot_mapping, void *q_out, void *k_pool,
+                                       void *v_pool, int num_tokens, int num_heads, int num_kv_heads,
+                                       int head_dim, int block_size, float eps, int dtype,
+                                       cudaStream_t stream);
+
+cudaError_t launch_silu_mul(const void *gate_up, void *out, int rows, int inter, int dtype,
+                            cudaStream_t stream);
+cudaError_t launch_argmax(const float *logits, int rows, int vocab, int32_t *out,
+                          const int32_t *row_slot, int32_t *slot_last_token, cudaStream_t stream);
+cudaError_t launch_embedding(const int32_t *tokens, const void *table, void *out, int rows,
+                             int hidden, int dtype, cudaStream_t stream);
+cudaError_t launch_convert(const void *src, int src_dtype, void *dst, int dst_dtype, int64_t n,
+                           cudaStream_t stream);
+
+struct PackArgs {
+  const int32_t *seq_row;    // [nseq] block-table row (engine slot) of each sequence
+  const int32_t *seq_ntok;   // [nseq] tokens this step
+  const int32_t *seq_start;  // [nseq] position of the first token
+  int num_seqs;
+  const int32_t *delta_row;
+  const int32_t *delta_idx;
+  const int32_t *delta_block;
+  int num_deltas;
+  int32_t *block_tables;  // [rows][max_blocks_per_seq]
+  int max_blocks_per_seq;
+  int block_size;
+  int32_t *cu_seqlens;    // [nseq+1]
+  int32_t *positions;     // [T]
+  int64_t *slot_mapping;  // [T]
+  int32_t *row_table;     // [T]
+  int32_t *row_ctx;       // [T]
+  // optional engine extras
+  int32_t *last_index;          // [nseq] packed index of each sequence's last token
+  int32_t *tokens;              // [T] input tokens (rewritten for device-fed decode rows)
+  const int32_t *slot_last_tok; // [rows] last token produced per slot (device-fed decode)
+  int tokens_from_device;
+  unsigned *status;
+  int64_t pool_blocks;
+};
+cudaError_t launch_pack(const PackArgs &a, cudaStream_t stream);
+
+}  // namespace ms

@@ -1,0 +1,288 @@
+// K4 fused residual-add + RMSNorm, K6 glue (SiLU-mul, argmax), dtype conversion.
+//
+// K4 restates RmsNorm::forward (src/backends/qwen2.rs:68-75) fused with the
+// residual adds of DecoderLayer::forward (qwen2.rs:420-427) and of the batched
+// decode (qwen2.rs:751-756): the sum is rounded to the model dtype, the
+// variance is taken in f32 from the rounded sum, the row is divided by
+// sqrt(var + eps), rounded, then multiplied by the weight and rounded again.
+// One CTA per row, 16-byte vector loads, warp-shuffle + shared-memory reduce.
+#include "ms_common.cuh"
+#include "ms_internal.h"
+
+namespace ms {
+namespace {
+
+template <typename T> struct V16;  // 16 bytes of T
+template <> struct V16<float> {
+  static constexpr int N = 4;
+  static __device__ __forceinline__ void load(const float *p, float (&o)[4]) { Vec4<float>::load(p, o); }
+  static __device__ __forceinline__ void store(float *p, const float (&o)[4]) { Vec4<float>::store(p, o); }
+};
+template <typename T> struct V16Half {
+  static constexpr int N = 8;
+  static __device__ __forceinline__ void load(const T *p, float (&o)[8]) {
+    float a[4], b[4];
+    Vec4<T>::load(p, a);
+    Vec4<T>::load(p + 4, b);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { o[i] = a[i]; o[4 + i] = b[i]; }
+  }
+  static __device__ __forceinline__ void store(T *p, const float (&o)[8]) {
+    float a[4], b[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { a[i] = o[i]; b[i] = o[4 + i]; }
+    Vec4<T>::store(p, a);
+    Vec4<T>::store(p + 4, b);
+  }
+};
+template <> struct V16<__nv_bfloat16> : V16Half<__nv_bfloat16> {};
+template <> struct V16<__half> : V16Half<__half> {};
+
+__device__ __forceinline__ float block_sum(float v, float *red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float t = (lane < nw) ? red[lane] : 0.f;
+  t = warp_sum(t);
+  return t;
+}
+
+template <typename T>
+__global__ void add_rmsnorm_kernel(const T *__restrict__ x, const T *__restrict__ r,
+                                   const int32_t *__restrict__ row_index, const T *__restrict__ w,
+                                   T *__restrict__ resid_out, T *__restrict__ norm_out, int hidden,
+                                   float eps) {
+  constexpr int N = V16<T>::N;
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const size_t src = row_index ? size_t(row_index[row]) : size_t(row);
+  const int c = threadIdx.x;  // chunk of N elements
+  const bool active = c * N < hidden;
+  float s[N];
+  float sq = 0.f;
+  if (active) {
+    V16<T>::load(x + src * hidden + c * N, s);
+    if (r) {
+      float rr[N];
+      V16<T>::load(r + src * hidden + c * N, rr);
+#pragma unroll
+      for (int i = 0; i < N; ++i) s[i] = round_to<T>(s[i] + rr[i]);
+    }
+    if (resid_out) V16<T>::store(resid_out + size_t(row) * hidden + c * N, s);
+#pragma unroll
+    for (int i = 0; i < N; ++i) sq = fmaf(s[i], s[i], sq);
+  }
+  const float total = block_sum(sq, red);
+  const float norm = sqrtf(total / float(hidden) + eps);
+  if (active) {
+    float ww[N], y[N];
+    V16<T>::load(w + c * N, ww);
+#pragma unroll
+    for (int i = 0; i < N; ++i) y[i] = round_to<T>(round_to<T>(s[i] / norm) * ww[i]);
+    V16<T>::store(norm_out + size_t(row) * hidden + c * N, y);
+  }
+}
+
+// act = silu(gate).to(dtype) * up, gate_up = [gate | up] per row (qwen2.rs:169-174).
+template <typename T>
+__global__ void silu_mul_kernel(const T *__restrict__ gu, T *__restrict__ out, int rows, int inter) {
+  constexpr int N = V16<T>::N;
+  const int chunks = inter / N;
+  const long long total = (long long)rows * chunks;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / chunks;
+    const int c = int(i % chunks);
+    float g[N], u[N], y[N];
+    V16<T>::load(gu + row * 2 * inter + c * N, g);
+    V16<T>::load(gu + row * 2 * inter + inter + c * N, u);
+#pragma unroll
+    for (int k = 0; k < N; ++k) {
+      const float a = round_to<T>(g[k] / (1.0f + expf(-g[k])));
+      y[k] = round_to<T>(a * u[k]);
+    }
+    V16<T>::store(out + row * inter + c * N, y);
+  }
+}
+
+// Row-wise argmax of f32 logits; ties resolve to the lowest index.
+__global__ void argmax_kernel(const float *__restrict__ logits, int vocab, int32_t *__restrict__ out,
+                              const int32_t *__restrict__ row_slot, int32_t *__restrict__ slot_last) {
+  const int row = blockIdx.x;
+  const float *l = logits + size_t(row) * vocab;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  if ((vocab & 3) == 0) {
+    const int n4 = vocab >> 2;
+    const float4 *l4 = reinterpret_cast<const float4 *>(l);
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+      const float4 v = l4[i];
+      const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (vv[k] > best) { best = vv[k]; bi = 4 * i + k; }
+    }
+  } else {
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x)
+      if (l[i] > best) { best = l[i]; bi = i; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(kFull, best, o);
+    const int oi = __shfl_xor_sync(kFull, bi, o);
+    if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+  }
+  __shared__ float sb[32];
+  __shared__ int si[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) { sb[warp] = best; si[warp] = bi; }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    best = lane < nw ? sb[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(kFull, best, o);
+      const int oi = __shfl_xor_sync(kFull, bi, o);
+      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    if (lane == 0) {
+      if (bi == 0x7fffffff) bi = 0;  // all NaN / -inf
+      out[row] = bi;
+      if (row_slot && slot_last) slot_last[row_slot[row]] = bi;
+    }
+  }
+}
+
+template <typename S, typename D>
+__global__ void convert_kernel(const S *__restrict__ src, D *__restrict__ dst, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    dst[i] = Elem<D>::from_f(Elem<S>::to_f(src[i]));
+}
+
+template <typename S>
+cudaError_t convert_from(const S *src, void *dst, int dst_dtype, int64_t n, cudaStream_t st) {
+  const int threads = 256;
+  const int64_t blocks = std::min<int64_t>((n + threads - 1) / threads, 148 * 32);
+  switch (dst_dtype) {
+    case MS_DTYPE_F32: convert_kernel<S, float><<<blocks, threads, 0, st>>>(src, (float *)dst, n); break;
+    case MS_DTYPE_BF16: convert_kernel<S, __nv_bfloat16><<<blocks, threads, 0, st>>>(src, (__nv_bfloat16 *)dst, n); break;
+    case MS_DTYPE_F16: convert_kernel<S, __half><<<blocks, threads, 0, st>>>(src, (__half *)dst, n); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_add_rmsnorm(const void *x, const void *r, const int32_t *row_index, const void *w,
+                               void *resid_out, void *norm_out, int rows, int hidden, float eps,
+                               int dtype, cudaStream_t st) {
+  if (rows == 0) return cudaSuccess;
+  if (rows < 0 || hidden <= 0) return cudaErrorInvalidValue;
+  const int n = dtype == MS_DTYPE_F32 ? 4 : 8;
+  if (hidden % n != 0 || hidden / n > 1024) return cudaErrorInvalidValue;
+  const int threads = ((hidden / n + 31) / 32) * 32;
+  switch (dtype) {
+    case MS_DTYPE_F32:
+      add_rmsnorm_kernel<float><<<rows, threads, 0, st>>>((const float *)x, (const float *)r, row_index,
+                                                          (const float *)w, (float *)resid_out,
+                                                          (float *)norm_out, hidden, eps);
+      break;
+    case MS_DTYPE_BF16:
+      add_rmsnorm_kernel<__nv_bfloat16><<<rows, threads, 0, st>>>(
+          (const __nv_bfloat16 *)x, (const __nv_bfloat16 *)r, row_index, (const __nv_bfloat16 *)w,
+          (__nv_bfloat16 *)resid_out, (__nv_bfloat16 *)norm_out, hidden, eps);
+      break;
+    case MS_DTYPE_F16:
+      add_rmsnorm_kernel<__half><<<rows, threads, 0, st>>>((const __half *)x, (const __half *)r, row_index,
+                                                           (const __half *)w, (__half *)resid_out,
+                                                           (__half *)norm_out, hidden, eps);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_silu_mul(const void *gu, void *out, int rows, int inter, int dtype, cudaStream_t st) {
+  if (rows == 0) return cudaSuccess;
+  const int n = dtype == MS_DTYPE_F32 ? 4 : 8;
+  if (rows < 0 || inter % n != 0) return cudaErrorInvalidValue;
+  const long long total = (long long)rows * (inter / n);
+  const int threads = 256;
+  const long long blocks = std::min<long long>((total + threads - 1) / threads, 148LL * 16);
+  switch (dtype) {
+    case MS_DTYPE_F32: silu_mul_kernel<float><<<blocks, threads, 0, st>>>((const float *)gu, (float *)out, rows, inter); break;
+    case MS_DTYPE_BF16: silu_mul_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>((const __nv_bfloat16 *)gu, (__nv_bfloat16 *)out, rows, inter); break;
+    case MS_DTYPE_F16: silu_mul_kernel<__half><<<blocks, threads, 0, st>>>((const __half *)gu, (__half *)out, rows, inter); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(const float *logits, int rows, int vocab, int32_t *out, const int32_t *row_slot,
+                          int32_t *slot_last_token, cudaStream_t st) {
+  if (rows == 0) return cudaSuccess;
+  if (rows < 0 || vocab <= 0) return cudaErrorInvalidValue;
+  argmax_kernel<<<rows, 1024, 0, st>>>(logits, vocab, out, row_slot, slot_last_token);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_convert(const void *src, int src_dtype, void *dst, int dst_dtype, int64_t n,
+                           cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  switch (src_dtype) {
+    case MS_DTYPE_F32: return convert_from<float>((const float *)src, dst, dst_dtype, n, st);
+    case MS_DTYPE_BF16: return convert_from<__nv_bfloat16>((const __nv_bfloat16 *)src, dst, dst_dtype, n, st);
+    case MS_DTYPE_F16: return convert_from<__half>((const __half *)src, dst, dst_dtype, n, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace ms
+
+// ---- C ABI --------------------------------------------------------------------
+extern "C" int ms_launch_add_rmsnorm(const void *x, const void *r, const int32_t *row_index, const void *w,
+                                     void *resid_out, void *norm_out, int32_t rows, int32_t hidden,
+                                     float eps, int32_t dtype, void *stream) {
+  return int(ms::launch_add_rmsnorm(x, r, row_index, w, resid_out, norm_out, rows, hidden, eps, dtype,
+                                    static_cast<cudaStream_t>(stream)));
+}
+
+extern "C" int ms_launch_silu_mul(const void *gate_up, void *out, int32_t rows, int32_t inter,
+                                  int32_t dtype, void *stream) {
+  return int(ms::launch_silu_mul(gate_up, out, rows, inter, dtype, static_cast<cudaStream_t>(stream)));
+}
+
+extern "C" int ms_launch_argmax(const float *logits, int32_t rows, int32_t vocab, int32_t *out,
+                                void *stream) {
+  return int(ms::launch_argmax(logits, rows, vocab, out, nullptr, nullptr, static_cast<cudaStream_t>(stream)));
+}
+
+// prototype-compatible RMSNorm (mini_serve_kernels.cu:247-265): same checks,
+// default stream, cudaError_t as int.  The f16 prototype rounds x*inv_rms to
+// f16 before the weight multiply (.cu:183-184), as this kernel does.
+extern "C" int launch_rmsnorm_f32(const float *d_x, const float *d_w, float *d_out, int num_rows,
+                                  int hidden_size, float eps) {
+  if (num_rows <= 0 || hidden_size <= 0) return int(cudaErrorInvalidValue);
+  return int(ms::launch_add_rmsnorm(d_x, nullptr, nullptr, d_w, nullptr, d_out, num_rows, hidden_size,
+                                    eps, MS_DTYPE_F32, 0));
+}
+
+extern "C" int launch_rmsnorm_f16(const void *d_x, const void *d_w, void *d_out, int num_rows,
+                                  int hidden_size, float eps) {
+  if (num_rows <= 0 || hidden_size <= 0) return int(cudaErrorInvalidValue);
+  return int(ms::launch_add_rmsnorm(d_x, nullptr, nullptr, d_w, nullptr, d_out, num_rows, hidden_size,
+                                    eps, MS_DTYPE_F16, 0));
+}
+
+extern "C" int launch_rmsnorm_bf16(const void *d_x, const void *d_w, void *d_out, int num_rows,
+                                   int hidden_size, float eps) {
+  if (num_rows <= 0 || hidden_size <= 0) return int(cudaErrorInvalidValue);
+  return int(ms::launch_add_rmsnorm(d_x, nullptr, nullptr, d_w, nullptr, d_out, num_rows, hidden_size,
+                                    eps, MS_DTYPE_BF16, 0));
+}

@@ -1,0 +1,329 @@
+"""ctypes binding of include/ms_engine.h (libms_engine.so, sm_100a).
+
+The library is required: importing this module without the built .so raises
+immediately, so no code path can silently fall back to a CPU implementation.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+from typing import Dict, Iterable, Optional, Sequence
+
+import numpy as np
+
+LIB_PATH = Path(__file__).resolve().parent / "libms_engine.so"
+
+MS_OK, MS_E_INVALID, MS_E_PRESSURE, MS_E_DEVICE, MS_E_INJECTED, MS_E_QUARANTINED, MS_E_TOKEN_LIMIT, \
+    MS_E_NOT_FOUND = range(8)
+MS_DTYPE_F32, MS_DTYPE_BF16, MS_DTYPE_F16 = 0, 1, 2
+MS_STEP_TOKENS_FROM_DEVICE = 1
+MS_STEP_KEEP_LOGITS = 2
+MS_FLAG_PREFILLED = 1
+
+
+class MsModelCfg(C.Structure):
+    _fields_ = [("vocab_size", C.c_int32), ("hidden_size", C.c_int32), ("intermediate_size", C.c_int32),
+                ("num_layers", C.c_int32), ("num_heads", C.c_int32), ("num_kv_heads", C.c_int32),
+                ("head_dim", C.c_int32), ("max_position_embeddings", C.c_int32), ("rope_theta", C.c_double),
+                ("rms_norm_eps", C.c_double), ("qk_norm", C.c_int32), ("attn_bias", C.c_int32),
+                ("tie_word_embeddings", C.c_int32), ("dtype", C.c_int32)]
+
+
+class MsEngineOpts(C.Structure):
+    _fields_ = [("device", C.c_int32), ("tp_rank", C.c_int32), ("tp_size", C.c_int32), ("nccl_comm", C.c_void_p),
+                ("pool_blocks", C.c_int64), ("block_size", C.c_int32), ("max_seqs", C.c_int32),
+                ("max_tokens_per_step", C.c_int32), ("max_blocks_per_seq", C.c_int32)]
+
+
+class MsStepDesc(C.Structure):
+    _fields_ = [("num_seqs", C.c_int32), ("seq_ids", C.POINTER(C.c_uint64)),
+                ("input_tokens", C.POINTER(C.c_uint32)), ("positions", C.POINTER(C.c_int32)),
+                ("flags", C.c_uint32)]
+
+
+_P = C.c_void_p
+_I32 = C.c_int32
+_SIGS = {
+    "ms_engine_create": ([C.POINTER(MsModelCfg), C.POINTER(MsEngineOpts), C.POINTER(_P)], C.c_int),
+    "ms_engine_destroy": ([_P], C.c_int),
+    "ms_engine_load_weight": ([_P, C.c_char_p, _P, C.c_int64, _I32, _I32], C.c_int),
+    "ms_engine_finalize": ([_P], C.c_int),
+    "ms_engine_memory": ([_P, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(C.c_int64)], C.c_int),
+    "ms_seq_admit": ([_P, C.c_uint64, C.POINTER(C.c_uint32), _I32, C.POINTER(_I32), _I32, _I32], C.c_int),
+    "ms_seq_append_block": ([_P, C.c_uint64, _I32], C.c_int),
+    "ms_seq_release": ([_P, C.c_uint64], C.c_int),
+    "ms_seq_cached_tokens": ([_P, C.c_uint64, C.POINTER(_I32)], C.c_int),
+    "ms_step": ([_P, C.POINTER(MsStepDesc), C.POINTER(C.c_uint32), C.POINTER(C.c_uint8)], C.c_int),
+    "ms_step_launch": ([_P, C.POINTER(MsStepDesc)], C.c_int),
+    "ms_step_wait": ([_P, C.POINTER(C.c_uint32), C.POINTER(C.c_uint8)], C.c_int),
+    "ms_engine_stream": ([_P, C.POINTER(_P)], C.c_int),
+    "ms_engine_set_profiling": ([_P, _I32], C.c_int),
+    "ms_engine_profile": ([_P, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(C.c_double),
+                           C.POINTER(C.c_double)], C.c_int),
+    "ms_is_healthy": ([_P], C.c_int),
+    "ms_mark_unhealthy": ([_P], C.c_int),
+    "ms_inject_fault": ([_P, _I32], C.c_int),
+    "ms_last_error": ([_P, C.c_char_p, _I32], C.c_int),
+    "ms_debug_dump_tables": ([_P, C.POINTER(_I32), C.POINTER(_I32), C.POINTER(_I32), C.POINTER(C.c_int64),
+                              C.POINTER(_I32)], C.c_int),
+    "ms_debug_logits": ([_P, C.POINTER(C.c_float), C.c_int64], C.c_int),
+    "ms_debug_pool_ptr": ([_P, _I32, _I32, C.POINTER(_P)], C.c_int),
+    "ms_launch_pack": ([_P, _P, _P, _I32, _P, _P, _P, _I32, _P, _I32, _I32, _P, _P, _P, _P, _P, _P], C.c_int),
+    "ms_launch_add_rmsnorm": ([_P, _P, _P, _P, _P, _P, _I32, _I32, C.c_float, _I32, _P], C.c_int),
+    "ms_launch_qk_norm_rope_append": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
+                                       C.c_float, _I32, _P], C.c_int),
+    "ms_attention_workspace_bytes": ([_I32, _I32, _I32, _I32, _I32], C.c_int64),
+    "ms_launch_paged_attention": ([_P, _P, _P, _P, _I32, _P, _P, _I32, _I32, _P, _I32, _I32, _I32, _I32, C.c_float,
+                                   _I32, _P, C.c_int64, _I32, _P], C.c_int),
+    "ms_launch_silu_mul": ([_P, _P, _I32, _I32, _I32, _P], C.c_int),
+    "ms_launch_argmax": ([_P, _I32, _I32, _P, _P], C.c_int),
+    "launch_rmsnorm_f32": ([_P, _P, _P, C.c_int, C.c_int, C.c_float], C.c_int),
+    "launch_rmsnorm_f16": ([_P, _P, _P, C.c_int, C.c_int, C.c_float], C.c_int),
+    "launch_rmsnorm_bf16": ([_P, _P, _P, C.c_int, C.c_int, C.c_float], C.c_int),
+    "launch_paged_gqa_decode_tiled_f32": ([_P] * 6 + [C.c_int] * 4 + [C.c_float], C.c_int),
+    "launch_paged_gqa_decode_tiled_f16": ([_P] * 6 + [C.c_int] * 4 + [C.c_float], C.c_int),
+    "launch_paged_gqa_decode_tiled_bf16": ([_P] * 6 + [C.c_int] * 4 + [C.c_float], C.c_int),
+}
+
+
+def load_library(path: Optional[os.PathLike] = None) -> C.CDLL:
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise RuntimeError(f"{p} is missing: build it with `python -m mini_serve_rs_b200.build` "
+                           "(this package has no CPU fallback)")
+    lib = C.CDLL(str(p))
+    for name, (args, res) in _SIGS.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    return lib
+
+
+_LIB: Optional[C.CDLL] = None
+
+
+def lib() -> C.CDLL:
+    global _LIB
+    if _LIB is None:
+        _LIB = load_library()
+    return _LIB
+
+
+def exported_symbols() -> Iterable[str]:
+    return tuple(_SIGS)
+
+
+# ---- errors (src/core/errors.rs:8-17) -------------------------------------------
+
+
+class EngineError(RuntimeError):
+    code = -1
+
+
+class CachePressure(EngineError):
+    code = MS_E_PRESSURE
+
+
+class BackendError(EngineError):
+    code = MS_E_DEVICE
+
+
+class NoHealthyWorkers(EngineError):
+    code = MS_E_QUARANTINED
+
+
+class TokenLimitExceeded(EngineError):
+    code = MS_E_TOKEN_LIMIT
+
+
+def error_for(code: int, msg: str) -> EngineError:
+    if code == MS_E_PRESSURE:
+        return CachePressure(msg)
+    if code == MS_E_QUARANTINED:
+        return NoHealthyWorkers(msg)
+    if code == MS_E_TOKEN_LIMIT:
+        return TokenLimitExceeded(msg)
+    e = BackendError(msg)
+    e.code = code
+    return e
+
+
+def _u32p(a: np.ndarray):
+    return a.ctypes.data_as(C.POINTER(C.c_uint32))
+
+
+def _i32p(a: np.ndarray):
+    return a.ctypes.data_as(C.POINTER(C.c_int32))
+
+
+def torch_dtype_code(t) -> int:
+    import torch
+    return {torch.float32: MS_DTYPE_F32, torch.bfloat16: MS_DTYPE_BF16, torch.float16: MS_DTYPE_F16}[t.dtype]
+
+
+class Engine:
+    """One engine per GPU: weights, paged KV pool and the step (ms_engine_*)."""
+
+    def __init__(self, cfg, *, device: int = 0, pool_blocks: int, max_seqs: int = 256,
+                 max_tokens_per_step: int = 8192, max_blocks_per_seq: int | None = None,
+                 dtype: int = MS_DTYPE_BF16):
+        """cfg: any object with the fields of oracle-style Config (vocab_size,
+        hidden_size, intermediate_size, num_hidden_layers, num_attention_heads,
+        num_key_value_heads, head_dim or hd(), max_position_embeddings,
+        rope_theta, rms_norm_eps, qk_norm, attention_bias, tie_word_embeddings)."""
+        self.lib = lib()
+        self.cfg = cfg
+        hd = cfg.hd() if hasattr(cfg, "hd") else cfg.head_dim
+        self.c_cfg = MsModelCfg(cfg.vocab_size, cfg.hidden_size, cfg.intermediate_size, cfg.num_hidden_layers,
+                                cfg.num_attention_heads, cfg.num_key_value_heads, hd, cfg.max_position_embeddings,
+                                float(cfg.rope_theta), float(cfg.rms_norm_eps), int(cfg.qk_norm),
+                                int(cfg.attention_bias), int(cfg.tie_word_embeddings), dtype)
+        if max_blocks_per_seq is None:
+            max_blocks_per_seq = (cfg.max_position_embeddings + 15) // 16
+        self.opts = MsEngineOpts(device, 0, 1, None, pool_blocks, 16, max_seqs, max_tokens_per_step,
+                                 max_blocks_per_seq)
+        self.dtype = dtype
+        self.max_seqs = max_seqs
+        self.max_blocks_per_seq = max_blocks_per_seq
+        h = C.c_void_p()
+        rc = self.lib.ms_engine_create(C.byref(self.c_cfg), C.byref(self.opts), C.byref(h))
+        if rc != MS_OK:
+            raise error_for(rc, "ms_engine_create: " + self._err(None))
+        self.h = h
+        self._out_tok = np.zeros(max_seqs, np.uint32)
+        self._out_flags = np.zeros(max_seqs, np.uint8)
+
+    # -- plumbing
+    def _err(self, h=...) -> str:
+        buf = C.create_string_buffer(1024)
+        self.lib.ms_last_error(self.h if h is ... else h, buf, 1024)
+        return buf.value.decode(errors="replace")
+
+    def _check(self, rc: int, what: str):
+        if rc != MS_OK:
+            raise error_for(rc, f"{what}: {self._err()}")
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.ms_engine_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- weights
+    def load_weights(self, weights: Dict[str, "object"]):
+        """weights: name -> torch tensor (CPU or on this engine's device)."""
+        import torch
+        for name, t in weights.items():
+            t = t.contiguous()
+            on_dev = 1 if t.is_cuda else 0
+            if not on_dev and t.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+                t = t.to(torch.float32)
+            self._check(self.lib.ms_engine_load_weight(self.h, name.encode(), C.c_void_p(t.data_ptr()), t.numel(),
+                                                       torch_dtype_code(t), on_dev), f"load {name}")
+        self._check(self.lib.ms_engine_finalize(self.h), "finalize")
+
+    def memory(self):
+        w, p, s = C.c_int64(), C.c_int64(), C.c_int64()
+        self._check(self.lib.ms_engine_memory(self.h, C.byref(w), C.byref(p), C.byref(s)), "memory")
+        return {"weights": w.value, "pool": p.value, "workspace": s.value}
+
+    # -- sequences
+    def admit(self, seq_id: int, prompt: Sequence[int], blocks: Sequence[int], num_cached: int = 0):
+        pr = np.ascontiguousarray(prompt, dtype=np.uint32)
+        bl = np.ascontiguousarray(blocks, dtype=np.int32)
+        self._check(self.lib.ms_seq_admit(self.h, seq_id, _u32p(pr), len(pr), _i32p(bl), len(bl), num_cached),
+                    "admit")
+
+    def append_block(self, seq_id: int, block: int):
+        self._check(self.lib.ms_seq_append_block(self.h, seq_id, block), "append_block")
+
+    def release(self, seq_id: int):
+        self._check(self.lib.ms_seq_release(self.h, seq_id), "release")
+
+    def cached_tokens(self, seq_id: int) -> int:
+        v = C.c_int32()
+        self._check(self.lib.ms_seq_cached_tokens(self.h, seq_id, C.byref(v)), "cached_tokens")
+        return v.value
+
+    # -- step
+    def _desc(self, seq_ids, input_tokens, positions, flags):
+        ids = np.ascontiguousarray(seq_ids, dtype=np.uint64)
+        toks = None if input_tokens is None else np.ascontiguousarray(input_tokens, dtype=np.uint32)
+        pos = None if positions is None else np.ascontiguousarray(positions, dtype=np.int32)
+        d = MsStepDesc(len(ids), ids.ctypes.data_as(C.POINTER(C.c_uint64)),
+                       None if toks is None else _u32p(toks), None if pos is None else _i32p(pos), flags)
+        return d, (ids, toks, pos)
+
+    def step(self, seq_ids, input_tokens=None, positions=None, flags: int = 0):
+        d, keep = self._desc(seq_ids, input_tokens, positions, flags)
+        n = len(keep[0])
+        rc = self.lib.ms_step(self.h, C.byref(d), _u32p(self._out_tok),
+                              self._out_flags.ctypes.data_as(C.POINTER(C.c_uint8)))
+        self._check(rc, "step")
+        return self._out_tok[:n].copy(), self._out_flags[:n].copy()
+
+    def step_launch(self, seq_ids, input_tokens=None, positions=None, flags: int = 0):
+        d, keep = self._desc(seq_ids, input_tokens, positions, flags)
+        self._pending_n = len(keep[0])
+        self._check(self.lib.ms_step_launch(self.h, C.byref(d)), "step_launch")
+
+    def step_wait(self):
+        rc = self.lib.ms_step_wait(self.h, _u32p(self._out_tok), self._out_flags.ctypes.data_as(C.POINTER(C.c_uint8)))
+        self._check(rc, "step_wait")
+        n = self._pending_n
+        return self._out_tok[:n].copy(), self._out_flags[:n].copy()
+
+    def stream_ptr(self) -> int:
+        s = C.c_void_p()
+        self._check(self.lib.ms_engine_stream(self.h, C.byref(s)), "stream")
+        return s.value or 0
+
+    # -- instrumentation
+    def set_profiling(self, on: bool):
+        self._check(self.lib.ms_engine_set_profiling(self.h, 1 if on else 0), "set_profiling")
+
+    def profile(self):
+        """(kernel_launches, attention launches, attention ms, attention algorithmic bytes)."""
+        kl, al, ms, by = C.c_int64(), C.c_int64(), C.c_double(), C.c_double()
+        self._check(self.lib.ms_engine_profile(self.h, C.byref(kl), C.byref(al), C.byref(ms), C.byref(by)),
+                    "profile")
+        return kl.value, al.value, ms.value, by.value
+
+    # -- health
+    def is_healthy(self) -> bool:
+        return bool(self.lib.ms_is_healthy(self.h))
+
+    def mark_unhealthy(self):
+        self._check(self.lib.ms_mark_unhealthy(self.h), "mark_unhealthy")
+
+    def inject_fault(self):
+        self._check(self.lib.ms_inject_fault(self.h, 1), "inject_fault")
+
+    # -- debugging
+    def dump_tables(self, num_seqs: int):
+        n = C.c_int32()
+        self._check(self.lib.ms_debug_dump_tables(self.h, C.byref(n), None, None, None, None), "dump")
+        T = n.value
+        cu = np.zeros(num_seqs + 1, np.int32)
+        pos = np.zeros(T, np.int32)
+        slots = np.zeros(T, np.int64)
+        bt = np.zeros((num_seqs, self.max_blocks_per_seq), np.int32)
+        self._check(self.lib.ms_debug_dump_tables(self.h, C.byref(n), _i32p(cu), _i32p(pos),
+                                                  slots.ctypes.data_as(C.POINTER(C.c_int64)), _i32p(bt)), "dump")
+        return {"cu_seqlens": cu, "positions": pos, "slot_mapping": slots, "block_tables": bt}
+
+    def logits(self, num_seqs: int) -> np.ndarray:
+        out = np.zeros((num_seqs, self.cfg.vocab_size), np.float32)
+        self._check(self.lib.ms_debug_logits(self.h, out.ctypes.data_as(C.POINTER(C.c_float)), out.size), "logits")
+        return out
+
+    def pool_ptr(self, layer: int, which: int) -> int:
+        p = C.c_void_p()
+        self._check(self.lib.ms_debug_pool_ptr(self.h, layer, which, C.byref(p)), "pool_ptr")
+        return p.value

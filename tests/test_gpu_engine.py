@@ -1,0 +1,272 @@
+"""End-to-end parity of the engine (libms_engine) on the B200.
+
+* BASELINE config 1 in f32 mode: greedy tokens of 4 requests x 32 steps under
+  the reference's continuous-batching order equal the CPU oracle's
+  (tests/golden/config1.json), and after every step the engine's device block
+  tables, positions and slot mappings equal the restated packer bit for bit.
+* Small Qwen3 / Qwen2.5 architectures against Hugging Face transformers
+  goldens (logits and greedy tokens), prefills packed into one ragged step.
+* bf16 serving mode against the f32 oracle with the reference's own GPU
+  tolerances (tests/test_pretrained_numerics.rs:180-184: max 0.25, RMS 0.04).
+* Device-fed decode, cached-prefix admission, error and quarantine paths.
+"""
+import json
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from mini_serve_rs_b200 import engine as E
+from mini_serve_rs_b200.backend import CudaBackend
+from oracle.kv_cache_ref import KVCacheRef
+from oracle.packer_ref import pack
+from oracle.qwen_ref import QwenRef, SeqState, qwen3_0_6b, random_weights
+from oracle.scheduler_ref import Request, SchedulerRef
+from tests.golden.golden_cases import MODEL_CASES
+from tests.golden.load import golden
+from tests.gpu_util import need_gpu
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _gpu():
+    need_gpu()
+
+
+def _compare(a, b, max_abs, rms):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    assert np.all(np.isfinite(a))
+    err = np.abs(a - b)
+    assert err.max() <= max_abs, f"max_abs {err.max()}"
+    assert math.sqrt((err ** 2).mean()) <= rms, f"rms {math.sqrt((err ** 2).mean())}"
+
+
+def _engine(cfg, dtype, pool_blocks=1024, max_seqs=16, max_tokens=1024, weights=None):
+    eng = E.Engine(cfg, pool_blocks=pool_blocks, max_seqs=max_seqs, max_tokens_per_step=max_tokens,
+                   max_blocks_per_seq=64, dtype=dtype)
+    eng.load_weights(weights)
+    return eng
+
+
+@pytest.fixture(scope="module")
+def config1():
+    d = json.loads((GOLDEN / "config1.json").read_text())
+    cfg = qwen3_0_6b()
+    return d, cfg, random_weights(cfg, d["seed_weights"])
+
+
+def test_config1_f32_greedy_tokens_and_tables_match_oracle(config1):
+    d, cfg, w = config1
+    eng = _engine(cfg, E.MS_DTYPE_F32, pool_blocks=d["pool_blocks"], weights=w)
+    backend = CudaBackend(eng)
+    checked = []
+
+    def step(seqs):
+        plan = []
+        for s in seqs:
+            if not s.is_prefilled:
+                plan.append((len(s.prompt_tokens), 0, list(s.kv_blocks)))
+            else:
+                plan.append((1, len(s.prompt_tokens) + len(s.output_tokens) - 1, list(s.kv_blocks)))
+        toks = backend.step_batch(seqs)
+        got = eng.dump_tables(len(seqs))
+        want = pack(plan, 16, eng.max_blocks_per_seq)
+        assert np.array_equal(got["cu_seqlens"], want["cu_seqlens"])
+        assert np.array_equal(got["positions"], want["positions"])
+        assert np.array_equal(got["slot_mapping"], want["slot_mapping"])
+        for i, (_, _, blocks) in enumerate(plan):
+            assert np.array_equal(got["block_tables"][i, :len(blocks)], np.asarray(blocks, np.int32))
+        checked.append(len(seqs))
+        return toks
+
+    sched = SchedulerRef(KVCacheRef(d["pool_blocks"], 16), step, backend.cancel_sequence, max_batch_size=8)
+    for i, p in enumerate(d["prompts"]):
+        sched.submit(Request(f"req-{i}", p, d["max_tokens"]))
+    out = sched.run()
+    assert len(checked) == len(d["steps"])
+    for rid, want in d["tokens"].items():
+        got = out[rid]
+        first_bad = next((k for k in range(len(want)) if got[k] != want[k]), None)
+        assert first_bad is None, (rid, first_bad, d["margins"][rid][first_bad], got, want)
+    eng.close()
+
+
+def test_config1_bf16_prefill_and_decode_logits_within_reference_gpu_tolerance(config1):
+    d, cfg, w = config1
+    prompts = [p[:40] for p in d["prompts"]]
+    model = QwenRef(cfg, w)
+    eng = _engine(cfg, E.MS_DTYPE_BF16, weights=w)
+    ids = list(range(1, len(prompts) + 1))
+    blocks = 0
+    states = []
+    for sid, p in zip(ids, prompts):
+        eng.admit(sid, p, list(range(blocks, blocks + 4)))
+        blocks += 4
+        states.append(SeqState(cfg, 64))
+    toks, flags = eng.step(ids, flags=E.MS_STEP_KEEP_LOGITS)
+    assert (flags & E.MS_FLAG_PREFILLED).all()
+    lg = eng.logits(len(ids))
+    for i, p in enumerate(prompts):
+        want = model.forward(p, states[i], 0).numpy()
+        _compare(lg[i], want, 0.25, 0.04)
+    # two decode steps, teacher-forced with the oracle's argmax
+    inputs = [int(t) for t in toks]
+    for k in range(2):
+        pos = [len(p) + k for p in prompts]
+        toks, flags = eng.step(ids, inputs, pos, flags=E.MS_STEP_KEEP_LOGITS)
+        assert not flags.any()
+        lg = eng.logits(len(ids))
+        for i in range(len(ids)):
+            want = model.forward([inputs[i]], states[i], pos[i]).numpy()
+            _compare(lg[i], want, 0.25, 0.04)
+        inputs = [int(t) for t in toks]
+    eng.close()
+
+
+@pytest.mark.parametrize("case", [c for c in MODEL_CASES if c["cfg"].hd() in (64, 128)],
+                         ids=lambda c: c["name"])
+def test_small_models_match_transformers_goldens_f32(case):
+    """All prompts prefilled in ONE packed ragged step, then teacher-forced
+    batched decode; logits vs the transformers goldens, greedy tokens equal."""
+    g = golden()
+    cfg = case["cfg"]
+    w = random_weights(cfg, case["seed"], norm_std=case.get("norm_std", 0.0))
+    eng = _engine(cfg, E.MS_DTYPE_F32, pool_blocks=256, weights=w)
+    prompts = case["prompts"]
+    ids = list(range(10, 10 + len(prompts)))
+    nb = 0
+    for sid, p in zip(ids, prompts):
+        need = (len(p) + case["decode_steps"] + 16) // 16 + 1
+        eng.admit(sid, p, list(range(nb, nb + need)))
+        nb += need
+    want_tok = [g[f"{case['name']}/p{i}/tokens"] for i in range(len(prompts))]
+    want_lg = [g[f"{case['name']}/p{i}/logits"] for i in range(len(prompts))]
+    toks, _ = eng.step(ids, flags=E.MS_STEP_KEEP_LOGITS)
+    lg = eng.logits(len(ids))
+    for i in range(len(prompts)):
+        _compare(lg[i], want_lg[i][0], 2e-4, 2e-5)
+        assert int(toks[i]) == int(want_tok[i][0])
+    for s in range(case["decode_steps"]):
+        inputs = [int(want_tok[i][s]) for i in range(len(prompts))]
+        pos = [len(p) + s for p in prompts]
+        toks, _ = eng.step(ids, inputs, pos, flags=E.MS_STEP_KEEP_LOGITS)
+        lg = eng.logits(len(ids))
+        for i in range(len(prompts)):
+            _compare(lg[i], want_lg[i][s + 1], 2e-4, 2e-5)
+            assert int(toks[i]) == int(want_tok[i][s + 1])
+    eng.close()
+
+
+def _small_engine(dtype=E.MS_DTYPE_BF16):
+    case = MODEL_CASES[1]
+    cfg = case["cfg"]
+    w = random_weights(cfg, case["seed"], norm_std=0.1)
+    return _engine(cfg, dtype, pool_blocks=256, weights=w), cfg
+
+
+def test_device_fed_decode_equals_host_fed():
+    eng_a, cfg = _small_engine()
+    eng_b, _ = _small_engine()
+    rng = np.random.Generator(np.random.PCG64(9))
+    prompts = [[int(t) for t in rng.integers(0, cfg.vocab_size, n)] for n in (5, 40, 17)]
+    ids = [1, 2, 3]
+    for e in (eng_a, eng_b):
+        for k, (sid, p) in enumerate(zip(ids, prompts)):
+            e.admit(sid, p, list(range(8 * k, 8 * k + 8)))
+    ta, _ = eng_a.step(ids)
+    tb, _ = eng_b.step(ids)
+    assert np.array_equal(ta, tb)
+    for s in range(6):
+        pos = [len(p) + s for p in prompts]
+        ta, _ = eng_a.step(ids, ta, pos)
+        tb, _ = eng_b.step(ids, None, pos, flags=E.MS_STEP_TOKENS_FROM_DEVICE)
+        assert np.array_equal(ta, tb), s
+    eng_a.close()
+    eng_b.close()
+
+
+def test_cached_prefix_admission_matches_full_prefill():
+    """A second request whose first 32 prompt tokens are already in the pool
+    (shared pages, as a prefix-cache hit) reuses those pages and gives the
+    same tokens as prefilling everything; an exact full hit replays the last
+    prompt token (src/backends/candle.rs:447-455)."""
+    eng, cfg = _small_engine(E.MS_DTYPE_F32)
+    rng = np.random.Generator(np.random.PCG64(10))
+    prompt = [int(t) for t in rng.integers(0, cfg.vocab_size, 45)]
+    eng.admit(1, prompt, [0, 1, 2, 3])
+    full, _ = eng.step([1])
+    # shares pages 0 and 1 (tokens 0..31) with request 1
+    eng.admit(2, prompt, [0, 1, 6, 7], num_cached=32)
+    part, flags = eng.step([2])
+    assert flags[0] & E.MS_FLAG_PREFILLED and part[0] == full[0]
+    assert eng.cached_tokens(2) == 45
+    # exact hit: all 40 prompt tokens cached -> the last one is replayed
+    eng.admit(6, prompt[:40], [20, 21, 22])
+    ref, _ = eng.step([6])
+    eng.admit(7, prompt[:40], [20, 21, 22], num_cached=40)
+    hit, flags = eng.step([7])
+    assert flags[0] & E.MS_FLAG_PREFILLED and hit[0] == ref[0]
+    assert eng.cached_tokens(7) == 40
+    # both continue identically
+    a, _ = eng.step([1, 2], [full[0], part[0]], [45, 45])
+    assert a[0] == a[1]
+    eng.close()
+
+
+def test_error_paths_and_quarantine():
+    eng, cfg = _small_engine()
+    backend = CudaBackend(eng)
+    with pytest.raises(E.BackendError, match="unknown sequence"):
+        eng.step([99], [1], [0])
+    eng.admit(1, [1, 2, 3], [0])
+    with pytest.raises(E.BackendError, match="outside the pool"):
+        eng.append_block(1, 10 ** 6)
+    with pytest.raises(E.BackendError, match="already admitted"):
+        eng.admit(1, [1], [1])
+    with pytest.raises(E.TokenLimitExceeded):
+        eng.admit(2, [], [1])
+    eng.step([1])
+    # position 16 needs a second page the scheduler has not given yet
+    eng.admit(3, list(range(16)), [2])
+    eng.step([3])
+    with pytest.raises(E.BackendError, match="block table too short"):
+        eng.step([3], [5], [16])
+    assert eng.is_healthy()  # contract errors do not quarantine the engine
+    # injected device-side failure (host-injected, no GPU fault): quarantine
+    eng.inject_fault()
+    with pytest.raises(E.BackendError, match="injected"):
+        eng.step([1], [4], [3])
+    assert not eng.is_healthy()
+    with pytest.raises(E.NoHealthyWorkers):
+        eng.step([1], [4], [3])
+    with pytest.raises(E.NoHealthyWorkers):
+        backend.reserve_sequence("x", 3, 4)
+    eng.close()
+
+
+def test_backend_quarantine_clears_state_like_the_reference():
+    eng, cfg = _small_engine()
+    backend = CudaBackend(eng)
+
+    class S:  # the ActiveSequence fields step_batch reads
+        def __init__(self, rid, prompt, blocks):
+            self.request_id, self.prompt_tokens, self.output_tokens = rid, prompt, []
+            self.is_prefilled, self.kv_blocks, self.max_tokens = False, blocks, 8
+
+    seqs = [S("a", [1, 2, 3], [0]), S("b", [4, 5], [1])]
+    out = backend.step_batch(seqs)
+    assert len(out) == 2 and all(s.is_prefilled for s in seqs)
+    eng.inject_fault()
+    for s, t in zip(seqs, out):
+        s.output_tokens.append(t)
+    with pytest.raises(E.BackendError):
+        backend.step_batch(seqs)
+    assert not backend.is_healthy()
+    with pytest.raises(E.NoHealthyWorkers):
+        backend.step_batch(seqs)
+    eng.close()
