@@ -265,7 +265,8 @@ def run_ours(args, rank, world, local):
     barrier()
 
     # ---- e2e: through the public step call with host token arrays
-    pos = np.array([int(c) + W + K for c in ctx], dtype=np.int32)
+    # step 1 replayed the last cached prompt token; every later step added one
+    pos = np.array([int(c) + W + K - 1 for c in ctx], dtype=np.int32)
     host_toks = np.asarray(toks, dtype=np.uint32)
     barrier()
     torch.cuda.synchronize()

@@ -200,6 +200,12 @@ int ms_debug_dump_tables(ms_engine *eng, int32_t *num_tokens, int32_t *cu_seqlen
                          int32_t *positions, int64_t *slot_mapping, int32_t *block_tables);
 /* f32 logits of the last step run with MS_STEP_KEEP_LOGITS: [num_seqs, vocab]. */
 int ms_debug_logits(ms_engine *eng, float *out, int64_t count);
+/* Copy an activation buffer of the last step to host memory, for parity
+ * checks of a single layer: "x_resid" / "x_norm" / "x_tmp" [T, H],
+ * "qkv" [T, (Hq + 2 Hkv) * D], "q" and "attn" [T, Hq * D], "gu" [T, 2I],
+ * "act" [T, I], "last_norm" [num_seqs, H] (model dtype), "row_ctx" /
+ * "row_table" / "positions" [T] (int32).  Fails if `bytes` is too small. */
+int ms_debug_buffer(ms_engine *eng, const char *name, void *out, int64_t bytes);
 /* Device address of layer `layer`'s K (which = 0) or V (which = 1) page pool,
  * laid out [pool_blocks, num_kv_heads_local, block_size, head_dim]. */
 int ms_debug_pool_ptr(ms_engine *eng, int32_t layer, int32_t which, void **ptr);

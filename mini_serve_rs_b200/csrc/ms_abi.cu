@@ -221,3 +221,31 @@ extern "C" int ms_engine_profile(ms_engine *eng, int64_t *kernel_launches, int64
   eng->prof_bytes = 0.0;
   return MS_OK;
 }
+
+extern "C" int ms_debug_buffer(ms_engine *eng, const char *name, void *out, int64_t bytes) {
+  if (!eng || !name || !out) return MS_E_INVALID;
+  if (eng->pending) return eng->fail(MS_E_INVALID, "step in flight");
+  const std::string n(name);
+  const size_t T = size_t(eng->last_T), S = size_t(eng->last_nseq), es = eng->esize;
+  const void *src = nullptr;
+  size_t sz = 0;
+  if (n == "x_resid") { src = eng->x_resid; sz = T * eng->H * es; }
+  else if (n == "x_norm") { src = eng->x_norm; sz = T * eng->H * es; }
+  else if (n == "x_tmp") { src = eng->x_tmp; sz = T * eng->H * es; }
+  else if (n == "qkv") { src = eng->qkv; sz = T * eng->qkv_dim * es; }
+  else if (n == "q") { src = eng->qbuf; sz = T * eng->hq * eng->D * es; }
+  else if (n == "attn") { src = eng->attn; sz = T * eng->hq * eng->D * es; }
+  else if (n == "gu") { src = eng->gu; sz = T * 2 * eng->I * es; }
+  else if (n == "act") { src = eng->act; sz = T * eng->I * es; }
+  else if (n == "last_norm") { src = eng->last_norm; sz = S * eng->H * es; }
+  else if (n == "row_ctx") { src = eng->d_row_ctx; sz = T * 4; }
+  else if (n == "row_table") { src = eng->d_row_table; sz = T * 4; }
+  else if (n == "positions") { src = eng->d_pos; sz = T * 4; }
+  else return eng->fail(MS_E_INVALID, "unknown buffer " + n);
+  if (int64_t(sz) > bytes) return eng->fail(MS_E_INVALID, "output buffer too small");
+  cudaError_t e = cudaSetDevice(eng->dev);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(eng->stream);
+  if (e == cudaSuccess) e = cudaMemcpy(out, src, sz, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return eng->fail(MS_E_DEVICE, cudaGetErrorString(e));
+  return MS_OK;
+}

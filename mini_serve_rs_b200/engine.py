@@ -69,6 +69,7 @@ _SIGS = {
                               C.POINTER(_I32)], C.c_int),
     "ms_debug_logits": ([_P, C.POINTER(C.c_float), C.c_int64], C.c_int),
     "ms_debug_pool_ptr": ([_P, _I32, _I32, C.POINTER(_P)], C.c_int),
+    "ms_debug_buffer": ([_P, C.c_char_p, _P, C.c_int64], C.c_int),
     "ms_launch_pack": ([_P, _P, _P, _I32, _P, _P, _P, _I32, _P, _I32, _I32, _P, _P, _P, _P, _P, _P], C.c_int),
     "ms_launch_add_rmsnorm": ([_P, _P, _P, _P, _P, _P, _I32, _I32, C.c_float, _I32, _P], C.c_int),
     "ms_launch_qk_norm_rope_append": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
@@ -321,6 +322,14 @@ class Engine:
     def logits(self, num_seqs: int) -> np.ndarray:
         out = np.zeros((num_seqs, self.cfg.vocab_size), np.float32)
         self._check(self.lib.ms_debug_logits(self.h, out.ctypes.data_as(C.POINTER(C.c_float)), out.size), "logits")
+        return out
+
+    def buffer(self, name: str, shape, dtype) -> np.ndarray:
+        """Activation buffer of the last step (see ms_debug_buffer); dtype is a
+        numpy dtype (np.float32, np.int32, or np.uint16 for raw bf16 bits)."""
+        out = np.zeros(shape, dtype)
+        self._check(self.lib.ms_debug_buffer(self.h, name.encode(), out.ctypes.data_as(C.c_void_p), out.nbytes),
+                    f"buffer {name}")
         return out
 
     def pool_ptr(self, layer: int, which: int) -> int:

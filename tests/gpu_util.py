@@ -13,8 +13,17 @@ def need_gpu():
         pytest.fail("GPU test run without a CUDA device")
 
 
+# Device tensors handed to a launch stay referenced until the next sync_ok():
+# a temporary like ptr(x.to(DEV)) would otherwise return its memory to the
+# caching allocator while the kernel still reads it.
+_KEEP = []
+
+
 def ptr(t):
-    return C.c_void_p(0 if t is None else t.data_ptr())
+    if t is None:
+        return C.c_void_p(0)
+    _KEEP.append(t)
+    return C.c_void_p(t.data_ptr())
 
 
 def dt_code(t):
@@ -27,6 +36,7 @@ def max_abs(a, b):
 
 def sync_ok(rc, what="launch"):
     torch.cuda.synchronize()
+    _KEEP.clear()
     assert rc == 0, f"{what} returned {rc}"
 
 

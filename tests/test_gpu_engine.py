@@ -60,19 +60,32 @@ def config1():
     return d, cfg, random_weights(cfg, d["seed_weights"])
 
 
+# Greedy decisions are compared where they are decidable in f32: a step whose
+# oracle top-2 logit margin is below NEAR_TIE (above the GPU-vs-CPU f32
+# reduction-order noise of the 28-layer stack) may pick the runner-up; the test
+# then checks the engine chose one of the two and teacher-forces the oracle's
+# token so the remaining steps stay comparable.
+NEAR_TIE = 1e-3
+
+
 def test_config1_f32_greedy_tokens_and_tables_match_oracle(config1):
     d, cfg, w = config1
     eng = _engine(cfg, E.MS_DTYPE_F32, pool_blocks=d["pool_blocks"], weights=w)
     backend = CudaBackend(eng)
-    checked = []
+    steps = d["steps"]
+    state = {"k": 0, "forced": []}
 
     def step(seqs):
+        k = state["k"]
+        rec = steps[k]
+        assert [s.request_id for s in seqs] == rec["request_ids"]
         plan = []
         for s in seqs:
             if not s.is_prefilled:
                 plan.append((len(s.prompt_tokens), 0, list(s.kv_blocks)))
             else:
                 plan.append((1, len(s.prompt_tokens) + len(s.output_tokens) - 1, list(s.kv_blocks)))
+        assert [p[2] for p in plan] == rec["kv_blocks"]
         toks = backend.step_batch(seqs)
         got = eng.dump_tables(len(seqs))
         want = pack(plan, 16, eng.max_blocks_per_seq)
@@ -81,18 +94,24 @@ def test_config1_f32_greedy_tokens_and_tables_match_oracle(config1):
         assert np.array_equal(got["slot_mapping"], want["slot_mapping"])
         for i, (_, _, blocks) in enumerate(plan):
             assert np.array_equal(got["block_tables"][i, :len(blocks)], np.asarray(blocks, np.int32))
-        checked.append(len(seqs))
+        for i, s in enumerate(seqs):
+            if toks[i] != rec["tokens"][i]:
+                margin = d["margins"][s.request_id][len(s.output_tokens)]
+                assert margin < NEAR_TIE, (s.request_id, len(s.output_tokens), margin)
+                state["forced"].append((s.request_id, len(s.output_tokens), margin))
+                toks[i] = rec["tokens"][i]
+        state["k"] += 1
         return toks
 
     sched = SchedulerRef(KVCacheRef(d["pool_blocks"], 16), step, backend.cancel_sequence, max_batch_size=8)
     for i, p in enumerate(d["prompts"]):
         sched.submit(Request(f"req-{i}", p, d["max_tokens"]))
     out = sched.run()
-    assert len(checked) == len(d["steps"])
-    for rid, want in d["tokens"].items():
-        got = out[rid]
-        first_bad = next((k for k in range(len(want)) if got[k] != want[k]), None)
-        assert first_bad is None, (rid, first_bad, d["margins"][rid][first_bad], got, want)
+    assert state["k"] == len(steps)
+    assert out == d["tokens"]
+    # at most the fixture's near-ties were decided differently
+    assert len(state["forced"]) <= sum(m < NEAR_TIE for v in d["margins"].values() for m in v)
+    print("near-tie steps decided by the runner-up:", state["forced"])
     eng.close()
 
 
@@ -269,4 +288,59 @@ def test_backend_quarantine_clears_state_like_the_reference():
     assert not backend.is_healthy()
     with pytest.raises(E.NoHealthyWorkers):
         backend.step_batch(seqs)
+    eng.close()
+
+
+def test_single_layer_intermediates_match_oracle_f32():
+    """Every activation of a one-layer Qwen3-architecture step (two prompts
+    packed into one prefill) against the oracle's restatement of the same ops."""
+    from dataclasses import replace
+
+    from oracle import kernels_ref
+    from oracle.qwen_ref import linear, rms_norm, rope_tables
+
+    cfg = replace(MODEL_CASES[1]["cfg"], num_hidden_layers=1)
+    w = random_weights(cfg, 77, norm_std=0.1)
+    eng = _engine(cfg, E.MS_DTYPE_F32, pool_blocks=64, weights=w)
+    rng = np.random.Generator(np.random.PCG64(78))
+    prompts = [[int(t) for t in rng.integers(0, cfg.vocab_size, n)] for n in (17, 40)]
+    eng.admit(1, prompts[0], [3, 9])
+    eng.admit(2, prompts[1], [5, 0, 7])
+    eng.step([1, 2])
+    T, H, D, hq, hkv, I = 57, cfg.hidden_size, 128, 4, 2, cfg.intermediate_size
+    got = lambda n, shape, dt=np.float32: eng.buffer(n, shape, dt)
+    pos = np.concatenate([np.arange(17), np.arange(40)])
+    assert np.array_equal(got("positions", (T,), np.int32), pos)
+    assert np.array_equal(got("row_ctx", (T,), np.int32), pos + 1)
+    p = "model.layers.0."
+    toks = torch.tensor(prompts[0] + prompts[1])
+    emb = w["model.embed_tokens.weight"][toks]
+    n1 = rms_norm(emb, w[p + "input_layernorm.weight"], 1e-6)
+    wqkv = torch.cat([w[p + f"self_attn.{x}_proj.weight"] for x in "qkv"])
+    qkv = linear(n1, wqkv)
+    np.testing.assert_allclose(got("qkv", (T, 8 * D)), qkv.numpy(), atol=1e-4, rtol=1e-4)
+    cos, sin = rope_tables(cfg)
+    q, k, v = kernels_ref.qk_norm_rope(qkv, pos.tolist(), cos, sin, hq, hkv, D, w[p + "self_attn.q_norm.weight"],
+                                       w[p + "self_attn.k_norm.weight"], None, 1e-6)
+    np.testing.assert_allclose(got("q", (T, hq, D)), q.numpy(), atol=1e-4, rtol=1e-4)
+    att = torch.zeros(T, hq, D)
+    for s0, n in ((0, 17), (17, 40)):
+        for i in range(n):
+            for h in range(hq):
+                kk, vv = k[s0:s0 + i + 1, h // 2], v[s0:s0 + i + 1, h // 2]
+                sc = torch.softmax((kk @ q[s0 + i, h]) / math.sqrt(D), dim=0)
+                att[s0 + i, h] = sc @ vv
+    np.testing.assert_allclose(got("attn", (T, hq, D)), att.numpy(), atol=1e-4, rtol=1e-4)
+    resid = emb + linear(att.reshape(T, hq * D), w[p + "self_attn.o_proj.weight"])
+    np.testing.assert_allclose(got("x_resid", (T, H)), resid.numpy(), atol=1e-4, rtol=1e-4)
+    n2 = rms_norm(resid, w[p + "post_attention_layernorm.weight"], 1e-6)
+    np.testing.assert_allclose(got("x_norm", (T, H)), n2.numpy(), atol=1e-4, rtol=1e-4)
+    gu = linear(n2, torch.cat([w[p + "mlp.gate_proj.weight"], w[p + "mlp.up_proj.weight"]]))
+    np.testing.assert_allclose(got("gu", (T, 2 * I)), gu.numpy(), atol=1e-4, rtol=1e-4)
+    act = kernels_ref.silu_mul(gu, I)
+    np.testing.assert_allclose(got("act", (T, I)), act.numpy(), atol=1e-4, rtol=1e-4)
+    down = linear(act, w[p + "mlp.down_proj.weight"])
+    np.testing.assert_allclose(got("x_tmp", (T, H)), down.numpy(), atol=1e-4, rtol=1e-4)
+    last = rms_norm((resid + down)[[16, 56]], w["model.norm.weight"], 1e-6)
+    np.testing.assert_allclose(got("last_norm", (2, H)), last.numpy(), atol=1e-4, rtol=1e-4)
     eng.close()
