@@ -45,7 +45,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batch", type=int, default=BATCH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-kernel-compare", action="store_true")
+    ap.add_argument("--kernel", choices=["attention"], default=None,
+                    help="time one kernel in isolation (BASELINE config 2 for attention) instead of the step")
     return ap.parse_args()
 
 
@@ -200,6 +201,7 @@ def fill_pool(eng, cfg, pool_blocks, device, seed):
                 if rc != 0:
                     raise RuntimeError(f"cudaMemcpy failed: {rc}")
                 off += n
+    torch.cuda.synchronize()  # D2D cudaMemcpy may return early; the engine stream does not wait on it
     del src
 
 
@@ -294,6 +296,74 @@ def run_ours(args, rank, world, local):
     return res
 
 
+def attention_config2(device: int, seed: int = 2, pool: int = 40000):
+    """BASELINE config 2's isolated op: 256 rows, ctx ~ U[1,4096], 16/8 heads x
+    128, bf16, block tables a seeded random permutation of the page pool."""
+    import numpy as np
+    import torch
+    dev = f"cuda:{device}"
+    rng = np.random.Generator(np.random.PCG64(seed))
+    B, hq, hkv, D = BATCH, 16, 8, 128
+    ctx = rng.integers(1, MAX_CTX + 1, B).astype(np.int32)
+    nblk = (ctx + 15) // 16
+    perm = rng.permutation(pool).astype(np.int32)
+    tables = np.zeros((B, 256), np.int32)
+    off = 0
+    for b in range(B):
+        tables[b, :nblk[b]] = perm[off:off + nblk[b]]
+        off += nblk[b]
+    g = torch.Generator(device=dev).manual_seed(seed)
+    kp = torch.randn(pool, hkv, 16, D, generator=g, device=dev, dtype=torch.bfloat16)
+    vp = torch.randn(pool, hkv, 16, D, generator=g, device=dev, dtype=torch.bfloat16)
+    q = torch.randn(B, hq, D, generator=g, device=dev, dtype=torch.bfloat16)
+    return {"q": q, "k": kp, "v": vp, "tables": torch.from_numpy(tables).to(dev),
+            "ctx": torch.from_numpy(ctx).to(dev), "sum_ctx": int(ctx.sum()), "sum_blocks": int(nblk.sum())}
+
+
+def run_attention_kernel(args, local):
+    """Time ms_launch_paged_attention alone on config 2 (CUDA events on the
+    launching stream; inputs 4.6 GB >> L2)."""
+    import ctypes as C
+    import torch
+    from mini_serve_rs_b200 import engine as E
+    torch.cuda.set_device(local)
+    d = attention_config2(local)
+    lib = E.lib()
+    B, hq, hkv, D = BATCH, 16, 8, 128
+    part = 0
+    ws_bytes = B * hq * 256 * (D * 4 + 8) + 256
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=f"cuda:{local}")
+    out = torch.empty_like(d["q"])
+    st = torch.cuda.current_stream()
+    p = lambda t: C.c_void_p(t.data_ptr())
+
+    def launch():
+        rc = lib.ms_launch_paged_attention(p(d["q"]), p(d["k"]), p(d["v"]), p(d["tables"]), 256, None, p(d["ctx"]),
+                                           B, MAX_CTX, p(out), hq, hkv, D, 16, 1.0 / math.sqrt(D), part, p(ws),
+                                           ws_bytes, E.MS_DTYPE_BF16, C.c_void_p(st.cuda_stream))
+        assert rc == 0, rc
+
+    for _ in range(args.warmup):
+        launch()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        launch()
+        e1.record(st)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1))
+    times.sort()
+    ms = times[len(times) // 2]
+    algo = d["sum_ctx"] * hkv * D * 2 * 2 + 2 * B * hq * D * 2 + d["sum_blocks"] * 4 + B * 4
+    peak, kind = peaks()
+    gbs = algo / (ms / 1000) / 1e9
+    print(json.dumps({"kernel": "paged_attention (K3 + combine)", "workload": "BASELINE config 2 isolated op",
+                      "ms_median": ms, "ms_all": times, "algorithmic_bytes": algo, "achieved_gbs": gbs,
+                      "peak_gbs": peak, "frac": gbs / peak, "peak_source": kind}), flush=True)
+
+
 def traffic_per_launch():
     """dram bytes (read + write) per attention launch from the committed ncu
     summary of this workload, if one exists."""
@@ -315,6 +385,10 @@ def main():
                 "model": "qwen3-0.6b-arch", "global_batch": args.batch * n, "seqs_per_gpu": args.batch,
                 "ctx": "uniform[1,4096] at admission, +1 per step", "block_size": 16,
                 "parallelism": f"dp{n} (independent replicas)", "l2": "inputs (60 GB KV/GPU) >> L2, no flush"}
+
+    if args.kernel == "attention":
+        run_attention_kernel(args, local)
+        return
 
     if args.impl == "reference":
         if rank != 0:

@@ -227,6 +227,9 @@ int create_impl(const ms_model_cfg *cfg, const ms_engine_opts *opts, Engine *eng
 
   MS_CUDA_TRY(cudaMallocHost(&eng->h_next, S * 4));
   MS_CUDA_TRY(cudaMallocHost(&eng->h_status, 4));
+  // the memsets and table uploads above ran on the legacy stream; the engine
+  // stream is non-blocking, so finish them before any step can be enqueued
+  MS_CUDA_TRY(cudaDeviceSynchronize());
   return MS_OK;
 }
 

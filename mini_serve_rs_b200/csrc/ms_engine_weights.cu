@@ -74,13 +74,18 @@ int load_weight_impl(Engine *eng, const char *cname, const void *data, int64_t n
     return eng->fail(MS_E_INVALID, "tensor " + name + ": expected " + std::to_string(d.numel) + " elements, got " +
                                        std::to_string(numel));
   cudaError_t e = cudaSetDevice(eng->dev);
+  // Order against everything already issued on the device (a device-resident
+  // source may come from another stream); the engine stream is non-blocking.
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return eng->fail(MS_E_DEVICE, cudaGetErrorString(e));
   const size_t sbytes = size_t(numel) * (src_dtype == MS_DTYPE_F32 ? 4 : 2);
   const void *src = data;
   void *tmp = nullptr;
   if (!src_on_device) {
+    // stream-ordered upload: a plain cudaMemcpy from pageable memory may return
+    // before its DMA lands, and the copy below runs on the engine stream
     e = cudaMalloc(&tmp, sbytes);
-    if (e == cudaSuccess) e = cudaMemcpy(tmp, data, sbytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(tmp, data, sbytes, cudaMemcpyHostToDevice, eng->stream);
     if (e != cudaSuccess) {
       if (tmp) cudaFree(tmp);
       return eng->fail(MS_E_DEVICE, std::string("weight upload: ") + cudaGetErrorString(e));

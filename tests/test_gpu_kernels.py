@@ -3,8 +3,9 @@ vectors (reference validator functions) and the CPU oracle on the same seeded
 inputs.  Tolerances: f32 atol 1e-5 / rtol 1e-4 and f16 5e-3 (the reference
 validator's, scripts/validate_cuda_kernels.py:126-129); bf16 vs the fp32
 reference 2e-2 max-abs for attention, and for norms 2e-2
-relative to max(1, |ref|) since bf16 storage alone is 2^-8 relative; bit-exact
-for integer outputs."""
+relative to max(1, |ref|) since bf16 storage alone is 2^-8 relative; for
+QK-norm + RoPE (five bf16 roundings, cancelling sums) max-abs 0.06 and 1%
+relative RMS; bit-exact for integer outputs."""
 import math
 
 import numpy as np
@@ -273,8 +274,13 @@ def test_qk_norm_rope_append_config3(dt, qk_norm, bias):
                                              hq, hkv, D, None if qn is None else qn.float(),
                                              None if kn is None else kn.float(), None if b is None else b.float(),
                                              1e-6)
-        rel = lambda a, w: ((a.float() - w).abs() / w.abs().clamp(min=1.0)).max().item()
-        assert rel(qo.cpu(), fq) <= 2e-2 and rel(got_k, fk) <= 2e-2
+        # bf16 storage at the reference's five rounding points (norm, x weight,
+        # x cos, x sin, sum): max error a few bf16 ulps of the operands, where a
+        # cancelling sum makes the result small; the bulk stays at bf16 precision
+        for a, w_ in ((qo.cpu().float(), fq), (got_k.float(), fk)):
+            err = (a - w_).abs()
+            assert err.max().item() <= 0.06
+            assert (err.pow(2).mean().sqrt() / w_.pow(2).mean().sqrt()).item() <= 1e-2
 
 
 # ---- packer ---------------------------------------------------------------------------
