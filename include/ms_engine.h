@@ -295,6 +295,24 @@ int launch_paged_gqa_decode_tiled_bf16(const void *d_q, const void *d_k_pool,
                                        int num_heads, int num_kv_heads, int max_blocks_per_seq,
                                        float scale);
 
+/* No counterpart in the reference.  Same arguments, checks and result as
+ * launch_paged_gqa_decode_tiled_bf16, for callers that must not allocate
+ * device memory (their allocator already owns the HBM budget, or they cannot
+ * afford the device-wide synchronisation of cudaMalloc/cudaFree on the hot
+ * path): it calls no allocation routine and keeps its split-K scratch in a
+ * fixed 16 MiB buffer inside the library, which every GPU that loads the
+ * library holds until exit.  A call whose scratch would exceed 16 MiB
+ * (batch_size * num_heads * partitions * 520 bytes) returns
+ * cudaErrorMemoryAllocation without launching anything.  The first call on a
+ * device looks the buffer's address up (make it before any stream capture).
+ * Calls share the buffer: calls that may overlap on the GPU race and must be
+ * serialised by the caller. */
+int launch_paged_gqa_decode_tiled_bf16_noalloc(const void *d_q, const void *d_k_pool,
+                                               const void *d_v_pool, const int *d_block_tables,
+                                               const int *d_seq_lens, void *d_out, int batch_size,
+                                               int num_heads, int num_kv_heads,
+                                               int max_blocks_per_seq, float scale);
+
 #ifdef __cplusplus
 }
 #endif

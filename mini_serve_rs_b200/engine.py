@@ -85,6 +85,7 @@ _SIGS = {
     "launch_paged_gqa_decode_tiled_f32": ([_P] * 6 + [C.c_int] * 4 + [C.c_float], C.c_int),
     "launch_paged_gqa_decode_tiled_f16": ([_P] * 6 + [C.c_int] * 4 + [C.c_float], C.c_int),
     "launch_paged_gqa_decode_tiled_bf16": ([_P] * 6 + [C.c_int] * 4 + [C.c_float], C.c_int),
+    "launch_paged_gqa_decode_tiled_bf16_noalloc": ([_P] * 6 + [C.c_int] * 4 + [C.c_float], C.c_int),
 }
 
 
