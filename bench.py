@@ -364,13 +364,14 @@ def run_attention_kernel(args, local):
                       "peak_gbs": peak, "frac": gbs / peak, "peak_source": kind}), flush=True)
 
 
-def traffic_per_launch():
-    """dram bytes (read + write) per attention launch from the committed ncu
-    summary of this workload, if one exists."""
+def traffic_per_launch(algorithmic_bytes: float):
+    """dram bytes (read + write) per attention launch: the committed ncu ratio of
+    dram bytes to algorithmic bytes (profiles/k3_attention_traffic.json, from a
+    capture of the config-2 launch) times this launch's algorithmic bytes."""
     p = ROOT / "profiles" / "k3_attention_traffic.json"
     if p.exists():
         try:
-            return float(json.loads(p.read_text())["dram_bytes_per_launch"])
+            return float(json.loads(p.read_text())["dram_bytes_per_algorithmic_byte"]) * algorithmic_bytes
         except (KeyError, ValueError):
             return None
     return None
@@ -432,7 +433,7 @@ def main():
                 "roofline": {"kernel": "paged_attention_kernel (K3 split-K GQA decode + combine)", "bound": "hbm",
                              "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                              "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
-                             "traffic": traffic_per_launch(), "algorithmic_bytes_per_launch": per_launch_bytes,
+                             "traffic": traffic_per_launch(per_launch_bytes), "algorithmic_bytes_per_launch": per_launch_bytes,
                              "ms_per_launch": per_launch_ms, "launches": r["attn_launches"],
                              "share_of_step": r["attn_ms"] / r["ms"]},
                 "memory_bytes": r["memory"]}
