@@ -20,57 +20,10 @@
 #include <algorithm>
 #include <mutex>
 
-#include "ms_common.cuh"
-#include "ms_internal.h"
+#include "ms_attention_common.cuh"
 
 namespace ms {
 namespace attn {
-
-constexpr int kBS = 16;          // tokens per KV page (kv_cache.rs block_size)
-constexpr int kWarps = 4;        // warps per CTA
-constexpr float kLog2e = 1.4426950408889634f;
-constexpr int kWaitLimit = 1 << 22;  // bounded mbarrier polling
-
-// ---- PTX wrappers (mbarrier + bulk async copy) --------------------------------
-__device__ __forceinline__ uint32_t smem_addr(const void *p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
-}
-__device__ __forceinline__ void fence_barrier_init() {
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
-               "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_addr(dst)),
-      "l"(src), "r"(bytes), "r"(smem_addr(bar))
-      : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Polls with an iteration limit; returns false when it gave up.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
-  for (int i = 0; i < kWaitLimit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
-}
 
 // ---- transposed butterfly: NVP partial values per lane -> NVP/32 totals ------
 // After the call, lane L holds in v[j] the warp-wide sum of original index
@@ -102,23 +55,6 @@ template <typename T, int D> struct TileLoad {
   }
 };
 
-struct Params {
-  const void *q;
-  const void *k_pool;
-  const void *v_pool;
-  const int32_t *block_tables;
-  const int32_t *row_table;
-  const int32_t *row_ctx;
-  void *out;
-  float *ws_o;   // [rows][Hkv][max_parts][G][D]
-  float2 *ws_ml; // [rows][Hkv][max_parts][G]
-  unsigned *status;
-  int max_blocks_per_seq;
-  int num_kv_heads;
-  int part_blocks;  // pages per partition
-  int max_parts;
-  float qscale;  // softmax scale * log2(e)
-};
 
 template <typename T, int D, int G, int NSTAGE>
 __global__ void __launch_bounds__(kWarps * 32) paged_attention_kernel(Params p) {
@@ -355,55 +291,7 @@ __global__ void __launch_bounds__(kWarps * 32) paged_attention_kernel(Params p) 
   int any_failed = __syncthreads_or(failed ? 1 : 0);
   if (any_failed) return;
 
-  const bool single = (nparts == 1);
-  for (int i = threadIdx.x; i < G * D; i += kWarps * 32) {
-    const int h = i / D, d = i % D;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, mm[w * G + h]);
-    float L = 0.f, O = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-      const float mw = mm[w * G + h];
-      const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
-      L += f * ml[w * G + h];
-      O += f * mo[(w * G + h) * D + d];
-    }
-    const size_t qh = size_t(row) * p.num_kv_heads * G + size_t(kvh) * G + h;
-    if (single) {
-      static_cast<T *>(p.out)[qh * D + d] = Elem<T>::from_f(L > 0.f ? O / L : 0.f);
-    } else {
-      const size_t slot = (size_t(row) * p.num_kv_heads + kvh) * p.max_parts + part;
-      p.ws_o[(slot * G + h) * D + d] = O;
-      if (d == 0) p.ws_ml[slot * G + h] = make_float2(M, L);
-    }
-  }
-}
-
-// Merge the partitions of rows that needed more than one (log-sum-exp).
-template <typename T, int D, int G>
-__global__ void combine_kernel(Params p) {
-  const int row = blockIdx.x;
-  const int kvh = blockIdx.y;
-  const int ctx = p.row_ctx[row];
-  const int nblk = max(0, (ctx + kBS - 1) / kBS);
-  const int nparts = min(p.max_parts, (nblk + p.part_blocks - 1) / p.part_blocks);
-  if (nparts <= 1) return;
-  const size_t base = (size_t(row) * p.num_kv_heads + kvh) * p.max_parts;
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
-    const int h = i / D, d = i % D;
-    float M = -INFINITY;
-    for (int s = 0; s < nparts; ++s) M = fmaxf(M, p.ws_ml[(base + s) * G + h].x);
-    float L = 0.f, O = 0.f;
-    for (int s = 0; s < nparts; ++s) {
-      const float2 ml = p.ws_ml[(base + s) * G + h];
-      const float f = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
-      L += f * ml.y;
-      O += f * p.ws_o[((base + s) * G + h) * D + d];
-    }
-    const size_t qh = size_t(row) * p.num_kv_heads * G + size_t(kvh) * G + h;
-    static_cast<T *>(p.out)[qh * D + d] = Elem<T>::from_f(L > 0.f ? O / L : 0.f);
-  }
+  merge_warps_store<T, D, G>(p, mo, mm, ml, row, kvh, part, nparts == 1);
 }
 
 template <typename T, int D, int G>
@@ -436,12 +324,7 @@ cudaError_t launch_t(const Params &p, int num_rows, cudaStream_t stream) {
   kern<<<grid, kWarps * 32, smem, stream>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  if (p.max_parts > 1) {
-    dim3 g2(num_rows, p.num_kv_heads);
-    combine_kernel<T, D, G><<<g2, std::min(1024, G * D), 0, stream>>>(p);
-    e = cudaGetLastError();
-  }
-  return e;
+  return launch_combine<T, D, G>(p, num_rows, stream);
 }
 
 template <typename T, int D>
@@ -528,6 +411,8 @@ cudaError_t launch_paged_attention(const AttnArgs &a, cudaStream_t stream) {
     p.ws_ml = reinterpret_cast<float2 *>(static_cast<char *>(a.workspace) +
                                          n_slots * group * a.head_dim * sizeof(float));
   }
+  if (attn::attention_tc_supported(a.dtype, a.head_dim, group))
+    return attn::launch_attention_tc(p, a, group, stream);
   switch (a.dtype) {
     case 0: return attn::dispatch_dim<float>(p, a.head_dim, group, a.num_rows, stream);
     case 1: return attn::dispatch_dim<__nv_bfloat16>(p, a.head_dim, group, a.num_rows, stream);

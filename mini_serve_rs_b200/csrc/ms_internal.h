@@ -29,7 +29,18 @@ struct AttnArgs {
   int64_t workspace_bytes;
   int dtype;
   unsigned *status;  // device status word (may be null)
+  // Tensor maps (CUtensorMap, host memory) describing k_pool / v_pool for the
+  // 16-bit tensor-core build; null -> encoded per call.  pool_tiles = pages x
+  // kv heads held by the pools (0 -> unknown).
+  const void *k_map = nullptr;
+  const void *v_map = nullptr;
+  int64_t pool_tiles = 0;
 };
+
+// Encode the TMA tensor map of one paged pool for the tensor-core attention
+// build (64-element inner boxes, 128-byte swizzle).  Returns false if the
+// driver entry point is unavailable or the encode fails.
+bool encode_pool_tensor_map(void *map_out, const void *pool, int dtype, int head_dim, int64_t pool_tiles);
 
 cudaError_t launch_paged_attention(const AttnArgs &a, cudaStream_t stream);
 int choose_partition_blocks(int num_rows, int num_kv_heads, int max_ctx, long long total_blocks);
