@@ -262,6 +262,25 @@ int ms_launch_paged_attention(const void *q, const void *k_pool, const void *v_p
                               float scale, int32_t partition_blocks, void *workspace,
                               int64_t workspace_bytes, int32_t dtype, void *stream);
 
+/* K3p: ragged causal prefill attention over the paged pool, bf16 / f16 on
+ * tensor cores (the prefill branch of qwen2.rs:329-345 with the causal mask
+ * of :476-503, including the offset columns of a cached prefix).  A tile is
+ * up to ms_prefill_tiles' tile size of consecutive tokens of one sequence:
+ * tiles[num_tiles][4] (device) = first packed row, rows, position of the
+ * first row, block-table row.  Row t attends to keys 0..position(t) of its
+ * table row; q / out as for ms_launch_paged_attention. */
+int ms_launch_paged_prefill(const void *q, const void *k_pool, const void *v_pool,
+                            const int32_t *block_tables, int32_t max_blocks_per_seq,
+                            const int32_t *tiles, int32_t num_tiles, void *out, int32_t num_heads,
+                            int32_t num_kv_heads, int32_t head_dim, int32_t block_size, float scale,
+                            int32_t dtype, void *stream);
+/* Host helper: cut per-sequence prompt chunks (first packed row, tokens,
+ * first position, block-table row) into prefill tiles.  Returns the number
+ * of tiles written to tiles_out, or -1 if capacity (in tiles) is too small. */
+int ms_prefill_tiles(const int32_t *seq_row0, const int32_t *seq_ntok, const int32_t *seq_start,
+                     const int32_t *seq_table_row, int32_t num_seqs, int32_t num_heads,
+                     int32_t num_kv_heads, int32_t *tiles_out, int32_t capacity);
+
 /* K6 glue. */
 int ms_launch_silu_mul(const void *gate_up, void *out, int32_t rows, int32_t inter,
                        int32_t dtype, void *stream);

@@ -73,7 +73,8 @@ __global__ void __launch_bounds__(kWarps * 32) paged_attention_kernel(Params p) 
   T *stages = reinterpret_cast<T *>(smem_raw);  // [kWarps][NSTAGE][2][TILE]
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw + size_t(kWarps) * NSTAGE * 2 * TILE_BYTES);
 
-  const int row = blockIdx.x;
+  const int ri = blockIdx.x;
+  const int row = p.row_index ? p.row_index[ri] : ri;
   const int kvh = blockIdx.y;
   const int part = blockIdx.z;
   const int warp = threadIdx.x >> 5;
@@ -291,7 +292,7 @@ __global__ void __launch_bounds__(kWarps * 32) paged_attention_kernel(Params p) 
   int any_failed = __syncthreads_or(failed ? 1 : 0);
   if (any_failed) return;
 
-  merge_warps_store<T, D, G>(p, mo, mm, ml, row, kvh, part, nparts == 1);
+  merge_warps_store<T, D, G>(p, mo, mm, ml, row, ri, kvh, part, nparts == 1);
 }
 
 template <typename T, int D, int G>
@@ -386,6 +387,7 @@ cudaError_t launch_paged_attention(const AttnArgs &a, cudaStream_t stream) {
   p.block_tables = a.block_tables;
   p.row_table = a.row_table;
   p.row_ctx = a.row_ctx;
+  p.row_index = a.row_index;
   p.out = a.out;
   p.max_blocks_per_seq = a.max_blocks_per_seq;
   p.num_kv_heads = a.num_kv_heads;

@@ -24,8 +24,9 @@ struct Params {
   const int32_t *block_tables;
   const int32_t *row_table;
   const int32_t *row_ctx;
+  const int32_t *row_index;  // launch row -> packed row (null: identity)
   void *out;
-  float *ws_o;    // [rows][Hkv][max_parts][G][D]
+  float *ws_o;    // [launch rows][Hkv][max_parts][G][D]
   float2 *ws_ml;  // [rows][Hkv][max_parts][G]
   unsigned *status;
   int max_blocks_per_seq;
@@ -122,7 +123,8 @@ __device__ __forceinline__ void mma_16816<__half>(float (&d)[4], const uint32_t 
 // memory and visible to the whole CTA when this is called.
 template <typename T, int D, int G>
 __device__ __forceinline__ void merge_warps_store(const Params &p, const float *mo, const float *mm,
-                                                  const float *ml, int row, int kvh, int part, bool single) {
+                                                  const float *ml, int row, int ri, int kvh, int part,
+                                                  bool single) {
   for (int i = threadIdx.x; i < G * D; i += kWarps * 32) {
     const int h = i / D, d = i % D;
     float M = -INFINITY;
@@ -140,7 +142,7 @@ __device__ __forceinline__ void merge_warps_store(const Params &p, const float *
     if (single) {
       static_cast<T *>(p.out)[qh * D + d] = Elem<T>::from_f(L > 0.f ? O / L : 0.f);
     } else {
-      const size_t slot = (size_t(row) * p.num_kv_heads + kvh) * p.max_parts + part;
+      const size_t slot = (size_t(ri) * p.num_kv_heads + kvh) * p.max_parts + part;
       p.ws_o[(slot * G + h) * D + d] = O;
       if (d == 0) p.ws_ml[slot * G + h] = make_float2(M, L);
     }
@@ -150,13 +152,14 @@ __device__ __forceinline__ void merge_warps_store(const Params &p, const float *
 // Merge the partitions of rows that needed more than one (log-sum-exp).
 template <typename T, int D, int G>
 __global__ void combine_kernel(Params p) {
-  const int row = blockIdx.x;
+  const int ri = blockIdx.x;
+  const int row = p.row_index ? p.row_index[ri] : ri;
   const int kvh = blockIdx.y;
   const int ctx = p.row_ctx[row];
   const int nblk = max(0, (ctx + kBS - 1) / kBS);
   const int nparts = min(p.max_parts, (nblk + p.part_blocks - 1) / p.part_blocks);
   if (nparts <= 1) return;
-  const size_t base = (size_t(row) * p.num_kv_heads + kvh) * p.max_parts;
+  const size_t base = (size_t(ri) * p.num_kv_heads + kvh) * p.max_parts;
   for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
     const int h = i / D, d = i % D;
     float M = -INFINITY;

@@ -67,7 +67,8 @@ __global__ void __launch_bounds__(kWarps * 32)
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + size_t(kWarps) * NSTAGE * STAGE_BYTES);
 
-  const int row = blockIdx.x;
+  const int ri = blockIdx.x;
+  const int row = p.row_index ? p.row_index[ri] : ri;
   const int kvh = blockIdx.y;
   const int part = blockIdx.z;
   const int warp = threadIdx.x >> 5;
@@ -132,8 +133,8 @@ __global__ void __launch_bounds__(kWarps * 32)
   for (int nd = 0; nd < NTD; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
   float m_run = -INFINITY, l_run = 0.f;
 
-  // ldmatrix lane roles: matrix mi = lane / 8, row ri = lane % 8
-  const int mi = lane >> 3, ri = lane & 7;
+  // ldmatrix lane roles: matrix mi = lane / 8, row lr = lane % 8
+  const int mi = lane >> 3, lr = lane & 7;
 
   bool failed = false;
   int issued = 0, kfail = 0;
@@ -173,7 +174,7 @@ __global__ void __launch_bounds__(kWarps * 32)
 #pragma unroll
     for (int kk = 0; kk < KSTEPS; ++kk) {
       uint32_t b[4];
-      const int token = (mi >> 1) * 8 + ri;
+      const int token = (mi >> 1) * 8 + lr;
       ldmatrix_x4(b, kb + tile_off(token, kk * 16 + (mi & 1) * 8));
       const uint32_t a[4] = {qa[kk][0], 0u, qa[kk][1], 0u};
       mma_16816<T>(sc[0], a, b[0], b[1]);
@@ -211,7 +212,7 @@ __global__ void __launch_bounds__(kWarps * 32)
 #pragma unroll
     for (int ndp = 0; ndp < NTD / 2; ++ndp) {
       uint32_t b[4];
-      const int token = (mi & 1) * 8 + ri;
+      const int token = (mi & 1) * 8 + lr;
       ldmatrix_x4_trans(b, vb + tile_off(token, (2 * ndp + (mi >> 1)) * 8));
       mma_16816<T>(o[2 * ndp], pa, b[0], b[1]);
       mma_16816<T>(o[2 * ndp + 1], pa, b[2], b[3]);
@@ -252,7 +253,7 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
   __syncthreads();
   if (__syncthreads_or(failed ? 1 : 0)) return;
-  merge_warps_store<T, D, G>(p, mo, mm, ml, row, kvh, part, nparts == 1);
+  merge_warps_store<T, D, G>(p, mo, mm, ml, row, ri, kvh, part, nparts == 1);
 }
 
 // ---- host side ------------------------------------------------------------------------
@@ -359,6 +360,10 @@ cudaError_t launch_attention_tc(const Params &p, const AttnArgs &a, int group, c
 }
 
 }  // namespace attn
+
+bool attention_tc_available(int dtype, int head_dim, int group) {
+  return attn::attention_tc_supported(dtype, head_dim, group);
+}
 
 bool encode_pool_tensor_map(void *map_out, const void *pool, int dtype, int head_dim, int64_t pool_tiles) {
   auto fn = attn::encode_fn();

@@ -182,6 +182,21 @@ int create_impl(const ms_model_cfg *cfg, const ms_engine_opts *opts, Engine *eng
   eng->pool_bytes = eng->layer_pool_elems * 2 * eng->L * es;
   MS_CUDA_TRY(cudaMalloc(&eng->pool, eng->pool_bytes));
 
+  // ---- tensor maps for the tensor-core attention kernels ----
+  eng->use_tc = attention_tc_available(eng->dtype, eng->D, eng->hq / eng->hkv);
+  if (eng->use_tc) {
+    eng->kmaps.resize(eng->L);
+    eng->vmaps.resize(eng->L);
+    const int64_t tiles = opts->pool_blocks * eng->hkv;
+    for (int l = 0; l < eng->L; ++l) {
+      char *kp = static_cast<char *>(eng->pool) + size_t(2 * l) * eng->layer_pool_elems * es;
+      char *vp = kp + eng->layer_pool_elems * es;
+      if (!encode_pool_tensor_map(&eng->kmaps[l], kp, eng->dtype, eng->D, tiles) ||
+          !encode_pool_tensor_map(&eng->vmaps[l], vp, eng->dtype, eng->D, tiles))
+        return eng->fail(MS_E_DEVICE, "cuTensorMapEncodeTiled failed for the KV pool");
+    }
+  }
+
   // ---- per-slot state ----
   MS_CUDA_TRY(cudaMalloc(&eng->d_block_tables, size_t(opts->max_seqs) * opts->max_blocks_per_seq * 4));
   MS_CUDA_TRY(cudaMemset(eng->d_block_tables, 0, size_t(opts->max_seqs) * opts->max_blocks_per_seq * 4));

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cublas_v2.h>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <string>
@@ -62,6 +63,10 @@ struct Engine {
   void *pool = nullptr;
   size_t pool_bytes = 0;
   size_t layer_pool_elems = 0;  // pool_blocks * hkv * 16 * D
+
+  // tensor-core attention: TMA tensor maps of each layer's K and V pool
+  bool use_tc = false;
+  std::vector<CUtensorMap> kmaps, vmaps;
 
   // per-slot device state
   int32_t *d_block_tables = nullptr;  // [max_seqs][max_blocks_per_seq]
@@ -137,6 +142,18 @@ int seq_admit_impl(Engine *eng, uint64_t id, const uint32_t *prompt, int prompt_
 int seq_append_block_impl(Engine *eng, uint64_t id, int32_t block);
 int seq_release_impl(Engine *eng, uint64_t id);
 int step_launch_impl(Engine *eng, const ms_step_desc *desc);
+
+// What one step's device work needs to know (host-computed, uploaded rows).
+struct StepPlan {
+  int S = 0, T = 0, nd = 0;  // sequences, packed tokens, block-table deltas
+  int n_dec = 0;             // rows run by the decode kernel (row list uploaded when tiles are used)
+  int n_tiles = 0;           // prefill tiles (tensor-core path only)
+  int max_ctx_dec = 0;
+  long long blocks_dec = 0;  // sum over decode rows of pages read
+  double ctx_dec = 0.0;      // sum over decode rows of keys read
+  bool split = false;        // decode rows via row list + prefill tiles
+};
+int enqueue_forward(Engine *eng, const StepPlan &plan);
 int step_wait_impl(Engine *eng, uint32_t *out_tokens, uint8_t *out_flags);
 
 }  // namespace ms

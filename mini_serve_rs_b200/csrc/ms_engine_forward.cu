@@ -53,7 +53,8 @@ cudaError_t prof_mark(Engine *eng) {
 }
 }  // namespace
 
-int enqueue_forward(Engine *eng, int S, int T, int max_ctx, long long total_blocks, int nd, double total_ctx) {
+int enqueue_forward(Engine *eng, const StepPlan &plan) {
+  const int S = plan.S, T = plan.T, nd = plan.nd;
   cudaStream_t st = eng->stream;
   const int dt = eng->dtype;
   const float eps = float(eng->cfg.rms_norm_eps);
@@ -89,9 +90,16 @@ int enqueue_forward(Engine *eng, int S, int T, int max_ctx, long long total_bloc
   MS_CUDA_TRY(launch_pack(pa, st));
   const int32_t *tokens = pa.tokens;
 
-  // attention partitioning: enough CTAs to fill the GPU, workspace bounded
-  int part = choose_partition_blocks(T, eng->hkv, max_ctx, total_blocks);
-  while (attention_workspace_bytes(T, eng->hq, max_ctx, part) > int64_t(eng->attn_ws_bytes)) part *= 2;
+  const int32_t *dec_rows = plan.split ? pa.delta_block + nd : nullptr;
+  const int32_t *tiles = plan.split ? pa.delta_block + nd + plan.n_dec : nullptr;
+  // decode attention partitioning: enough CTAs to fill the GPU, workspace bounded
+  int part = 1;
+  if (plan.n_dec > 0) {
+    part = choose_partition_blocks(plan.n_dec, eng->hkv, plan.max_ctx_dec, plan.blocks_dec);
+    while (attention_workspace_bytes(plan.n_dec, eng->hq, plan.max_ctx_dec, part) > int64_t(eng->attn_ws_bytes))
+      part *= 2;
+  }
+  const int64_t pool_tiles = eng->opts.pool_blocks * eng->hkv;
 
   // ---- layer 0 input: embedding gather + input norm (K4 without residual) ----
   MS_CUDA_TRY(launch_add_rmsnorm(eng->embed, nullptr, tokens, eng->layers[0].ln1, eng->x_resid, eng->x_norm, T,
@@ -106,35 +114,65 @@ int enqueue_forward(Engine *eng, int S, int T, int max_ctx, long long total_bloc
     MS_CUDA_TRY(launch_qk_norm_rope_append(eng->qkv, w.b_qkv, w.q_norm, w.k_norm, eng->cos_t, eng->sin_t, eng->d_pos,
                                            eng->d_slots, eng->qbuf, kp, vp, T, eng->hq, eng->hkv, eng->D,
                                            eng->opts.block_size, eps, dt, st));
-    // paged attention over each row's causal context
-    AttnArgs a{};
-    a.q = eng->qbuf;
-    a.k_pool = kp;
-    a.v_pool = vp;
-    a.block_tables = eng->d_block_tables;
-    a.max_blocks_per_seq = eng->opts.max_blocks_per_seq;
-    a.row_table = eng->d_row_table;
-    a.row_ctx = eng->d_row_ctx;
-    a.num_rows = T;
-    a.max_ctx = max_ctx;
-    a.out = eng->attn;
-    a.num_heads = eng->hq;
-    a.num_kv_heads = eng->hkv;
-    a.head_dim = eng->D;
-    a.block_size = eng->opts.block_size;
-    a.scale = 1.0f / std::sqrt(float(eng->D));
-    a.part_blocks = part;
-    a.workspace = eng->attn_ws;
-    a.workspace_bytes = int64_t(eng->attn_ws_bytes);
-    a.dtype = dt;
-    a.status = eng->d_status;
-    if (eng->profiling) MS_CUDA_TRY(prof_mark(eng));
-    MS_CUDA_TRY(launch_paged_attention(a, st));
-    if (eng->profiling) {
-      MS_CUDA_TRY(prof_mark(eng));
-      // K and V rows read, q in, out written, one table entry per page, one ctx per row
-      eng->prof_bytes += total_ctx * eng->hkv * eng->D * 2.0 * es + 2.0 * T * eng->hq * eng->D * es +
-                         double(total_blocks) * 4.0 + 4.0 * T;
+    // paged attention: one-token rows through split-K decode, prompt chunks through prefill tiles
+    if (plan.n_dec > 0) {
+      AttnArgs a{};
+      a.q = eng->qbuf;
+      a.k_pool = kp;
+      a.v_pool = vp;
+      a.block_tables = eng->d_block_tables;
+      a.max_blocks_per_seq = eng->opts.max_blocks_per_seq;
+      a.row_table = eng->d_row_table;
+      a.row_ctx = eng->d_row_ctx;
+      a.row_index = dec_rows;
+      a.num_rows = plan.n_dec;
+      a.max_ctx = plan.max_ctx_dec;
+      a.out = eng->attn;
+      a.num_heads = eng->hq;
+      a.num_kv_heads = eng->hkv;
+      a.head_dim = eng->D;
+      a.block_size = eng->opts.block_size;
+      a.scale = 1.0f / std::sqrt(float(eng->D));
+      a.part_blocks = part;
+      a.workspace = eng->attn_ws;
+      a.workspace_bytes = int64_t(eng->attn_ws_bytes);
+      a.dtype = dt;
+      a.status = eng->d_status;
+      if (eng->use_tc) {
+        a.k_map = &eng->kmaps[l];
+        a.v_map = &eng->vmaps[l];
+        a.pool_tiles = pool_tiles;
+      }
+      if (eng->profiling) MS_CUDA_TRY(prof_mark(eng));
+      MS_CUDA_TRY(launch_paged_attention(a, st));
+      if (eng->profiling) {
+        MS_CUDA_TRY(prof_mark(eng));
+        // K and V rows read, q in, out written, one table entry per page, one ctx per row
+        eng->prof_bytes += plan.ctx_dec * eng->hkv * eng->D * 2.0 * es + 2.0 * plan.n_dec * eng->hq * eng->D * es +
+                           double(plan.blocks_dec) * 4.0 + 4.0 * plan.n_dec;
+      }
+    }
+    if (plan.n_tiles > 0) {
+      PrefillArgs pf{};
+      pf.q = eng->qbuf;
+      pf.k_pool = kp;
+      pf.v_pool = vp;
+      pf.block_tables = eng->d_block_tables;
+      pf.max_blocks_per_seq = eng->opts.max_blocks_per_seq;
+      pf.tiles = tiles;
+      pf.num_tiles = plan.n_tiles;
+      pf.out = eng->attn;
+      pf.num_heads = eng->hq;
+      pf.num_kv_heads = eng->hkv;
+      pf.head_dim = eng->D;
+      pf.block_size = eng->opts.block_size;
+      pf.scale = 1.0f / std::sqrt(float(eng->D));
+      pf.dtype = dt;
+      pf.status = eng->d_status;
+      pf.k_map = &eng->kmaps[l];
+      pf.v_map = &eng->vmaps[l];
+      pf.pool_tiles = pool_tiles;
+      MS_CUDA_TRY(launch_paged_prefill(pf, st));
     }
     // o_proj, residual add + post-attention norm
     MS_BLAS_TRY(linear(eng, w.w_o, eng->attn, eng->x_tmp, eng->H, T, eng->hq * eng->D));
@@ -157,9 +195,10 @@ int enqueue_forward(Engine *eng, int S, int T, int max_ctx, long long total_bloc
   MS_BLAS_TRY(linear(eng, eng->lm_head, eng->last_norm, eng->logits, eng->V, S, eng->H, true));
   MS_CUDA_TRY(launch_argmax(eng->logits, S, eng->V, eng->d_next, pa.seq_row, eng->d_slot_last, st));
   {
-    const int max_blk = (max_ctx + 15) / 16;
-    const int parts = (max_blk + part - 1) / part;
-    eng->kernel_launches += 3 + int64_t(eng->L) * (5 + (parts > 1 ? 1 : 0));
+    const int max_blk = (plan.max_ctx_dec + 15) / 16;
+    const int parts = plan.n_dec > 0 ? (max_blk + part - 1) / part : 0;
+    const int attn_launches = (plan.n_dec > 0 ? 1 + (parts > 1 ? 1 : 0) : 0) + (plan.n_tiles > 0 ? 1 : 0);
+    eng->kernel_launches += 3 + int64_t(eng->L) * (4 + attn_launches);
   }
   MS_CUDA_TRY(cudaMemcpyAsync(eng->h_next, eng->d_next, size_t(S) * 4, cudaMemcpyDeviceToHost, st));
   MS_CUDA_TRY(cudaMemcpyAsync(eng->h_status, eng->d_status, sizeof(unsigned), cudaMemcpyDeviceToHost, st));

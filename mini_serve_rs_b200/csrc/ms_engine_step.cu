@@ -46,7 +46,6 @@ int grow_staging(Engine *eng, size_t elems) {
 
 }  // namespace
 
-int enqueue_forward(Engine *eng, int S, int T, int max_ctx, long long total_blocks, int nd, double total_ctx);
 
 int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
   if (!eng->healthy) {
@@ -123,8 +122,50 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
     return eng->fail(MS_E_PRESSURE, "step needs " + std::to_string(T) + " tokens, engine holds " +
                                         std::to_string(eng->opts.max_tokens_per_step));
 
+  // ---- attention work split: decode rows (one token) and prefill tiles ----
+  StepPlan sp;
+  sp.S = S;
+  sp.T = T;
+  sp.nd = nd;
+  sp.split = eng->use_tc;
+  std::vector<int32_t> dec_rows, tiles;
+  if (sp.split) {
+    std::vector<int32_t> prow0, pntok, pstart, ptrow;
+    int row0 = 0;
+    for (int i = 0; i < S; ++i) {
+      const RowPlan &r = plan[i];
+      const int end = r.start + r.ntok;
+      if (r.ntok == 1) {
+        dec_rows.push_back(row0);
+        sp.max_ctx_dec = std::max(sp.max_ctx_dec, end);
+        sp.blocks_dec += (end + 15) / 16;
+        sp.ctx_dec += double(end);
+      } else {
+        prow0.push_back(row0);
+        pntok.push_back(r.ntok);
+        pstart.push_back(r.start);
+        ptrow.push_back(r.seq->slot);
+      }
+      row0 += r.ntok;
+    }
+    sp.n_dec = int(dec_rows.size());
+    if (!prow0.empty()) {
+      const int group = eng->hq / eng->hkv;
+      const int cap = T;  // a tile holds at least one token
+      tiles.resize(size_t(4) * cap);
+      sp.n_tiles = build_prefill_tiles(prow0.data(), pntok.data(), pstart.data(), ptrow.data(), int(prow0.size()),
+                                       group, tiles.data(), cap);
+      if (sp.n_tiles < 0) return eng->fail(MS_E_INVALID, "prefill tile list overflow");
+    }
+  } else {
+    sp.n_dec = T;
+    sp.max_ctx_dec = max_ctx;
+    sp.blocks_dec = total_blocks;
+    sp.ctx_dec = total_ctx;
+  }
+
   // ---- stage the step description: one pinned buffer, one upload ----
-  const size_t need = size_t(3) * S + T + size_t(3) * nd;
+  const size_t need = size_t(3) * S + T + size_t(3) * nd + (sp.split ? size_t(sp.n_dec) + 4 * size_t(sp.n_tiles) : 0);
   int rc = grow_staging(eng, need);
   if (rc != MS_OK) return rc;
   int32_t *h = eng->h_in;
@@ -148,9 +189,14 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
       h_dblk[d] = s.blocks[b];
     }
   }
+  if (sp.split) {
+    int32_t *h_dec = h_dblk + nd;
+    std::copy(dec_rows.begin(), dec_rows.end(), h_dec);
+    std::copy(tiles.begin(), tiles.begin() + 4 * size_t(sp.n_tiles), h_dec + sp.n_dec);
+  }
   MS_CUDA_TRY(cudaSetDevice(eng->dev));
   MS_CUDA_TRY(cudaMemcpyAsync(eng->d_in, eng->h_in, need * 4, cudaMemcpyHostToDevice, eng->stream));
-  rc = enqueue_forward(eng, S, T, max_ctx, total_blocks, nd, total_ctx);
+  rc = enqueue_forward(eng, sp);
   if (rc != MS_OK) return rc;
 
   // ---- commit host state ----

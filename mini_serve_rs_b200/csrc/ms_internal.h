@@ -35,6 +35,9 @@ struct AttnArgs {
   const void *k_map = nullptr;
   const void *v_map = nullptr;
   int64_t pool_tiles = 0;
+  // launch row i attends for packed row row_index[i] (q, out, row_ctx,
+  // row_table are indexed by the packed row); null -> identity
+  const int32_t *row_index = nullptr;
 };
 
 // Encode the TMA tensor map of one paged pool for the tensor-core attention
@@ -43,6 +46,38 @@ struct AttnArgs {
 bool encode_pool_tensor_map(void *map_out, const void *pool, int dtype, int head_dim, int64_t pool_tiles);
 
 cudaError_t launch_paged_attention(const AttnArgs &a, cudaStream_t stream);
+
+// K3p: ragged causal prefill over the paged pool (16-bit, tensor cores).
+// tiles [num_tiles][4] = (first packed row, rows, position of the first row,
+// block-table row); rows of a tile are consecutive tokens of one sequence.
+struct PrefillArgs {
+  const void *q;
+  const void *k_pool;
+  const void *v_pool;
+  const int32_t *block_tables;
+  int max_blocks_per_seq;
+  const int32_t *tiles;
+  int num_tiles;
+  void *out;
+  int num_heads;
+  int num_kv_heads;
+  int head_dim;
+  int block_size;
+  float scale;
+  int dtype;
+  unsigned *status = nullptr;
+  const void *k_map = nullptr;
+  const void *v_map = nullptr;
+  int64_t pool_tiles = 0;
+};
+cudaError_t launch_paged_prefill(const PrefillArgs &a, cudaStream_t stream);
+// true when the 16-bit tensor-core decode / prefill kernels serve this shape
+bool attention_tc_available(int dtype, int head_dim, int group);
+int prefill_tokens_per_tile(int group);
+// Host: split prefill sequences into tiles of prefill_tokens_per_tile(group)
+// tokens; returns the tile count or -1 if capacity is exceeded.
+int build_prefill_tiles(const int32_t *seq_row0, const int32_t *seq_ntok, const int32_t *seq_start,
+                        const int32_t *seq_trow, int num_seqs, int group, int32_t *tiles_out, int capacity);
 int choose_partition_blocks(int num_rows, int num_kv_heads, int max_ctx, long long total_blocks);
 int64_t attention_workspace_bytes(int num_rows, int num_heads, int max_ctx, int part_blocks);
 

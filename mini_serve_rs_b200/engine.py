@@ -77,6 +77,9 @@ _SIGS = {
     "ms_attention_workspace_bytes": ([_I32, _I32, _I32, _I32, _I32], C.c_int64),
     "ms_launch_paged_attention": ([_P, _P, _P, _P, _I32, _P, _P, _I32, _I32, _P, _I32, _I32, _I32, _I32, C.c_float,
                                    _I32, _P, C.c_int64, _I32, _P], C.c_int),
+    "ms_launch_paged_prefill": ([_P, _P, _P, _P, _I32, _P, _I32, _P, _I32, _I32, _I32, _I32, C.c_float, _I32, _P],
+                                C.c_int),
+    "ms_prefill_tiles": ([C.POINTER(_I32)] * 4 + [_I32, _I32, _I32, C.POINTER(_I32), _I32], C.c_int),
     "ms_launch_silu_mul": ([_P, _P, _I32, _I32, _I32, _P], C.c_int),
     "ms_launch_argmax": ([_P, _I32, _I32, _P, _P], C.c_int),
     "launch_rmsnorm_f32": ([_P, _P, _P, C.c_int, C.c_int, C.c_float], C.c_int),

@@ -344,3 +344,35 @@ def test_single_layer_intermediates_match_oracle_f32():
     last = rms_norm((resid + down)[[16, 56]], w["model.norm.weight"], 1e-6)
     np.testing.assert_allclose(got("last_norm", (2, H)), last.numpy(), atol=1e-4, rtol=1e-4)
     eng.close()
+
+
+def test_bf16_mixed_prefill_and_decode_step_matches_oracle(config1):
+    """One bf16 step that packs two fresh prompts (prefill tiles) with two
+    sequences already decoding (split-K rows), against the f32 oracle with the
+    reference's GPU tolerance."""
+    d, cfg, w = config1
+    model = QwenRef(cfg, w)
+    eng = _engine(cfg, E.MS_DTYPE_BF16, weights=w)
+    rng = np.random.Generator(np.random.PCG64(31))
+    p_dec = [[int(t) for t in rng.integers(0, cfg.vocab_size, n)] for n in (23, 50)]
+    p_new = [[int(t) for t in rng.integers(0, cfg.vocab_size, n)] for n in (70, 9)]
+    st = {}
+    for sid, p in zip((1, 2), p_dec):
+        eng.admit(sid, p, list(range(4 * sid, 4 * sid + 4)))
+        st[sid] = SeqState(cfg, 80)
+    toks, _ = eng.step([1, 2])
+    for sid, p in zip((1, 2), p_dec):
+        model.forward(p, st[sid], 0)
+    for sid, p in zip((3, 4), p_new):
+        eng.admit(sid, p, list(range(4 * sid + 8, 4 * sid + 14)))
+        st[sid] = SeqState(cfg, 80)
+    inputs = [int(toks[0]), int(toks[1]), 0, 0]
+    pos = [23, 50, 0, 0]
+    out, flags = eng.step([1, 2, 3, 4], inputs, pos, flags=E.MS_STEP_KEEP_LOGITS)
+    assert list(flags) == [0, 0, E.MS_FLAG_PREFILLED, E.MS_FLAG_PREFILLED]
+    lg = eng.logits(4)
+    _compare(lg[0], model.forward([inputs[0]], st[1], 23).numpy(), 0.25, 0.04)
+    _compare(lg[1], model.forward([inputs[1]], st[2], 50).numpy(), 0.25, 0.04)
+    _compare(lg[2], model.forward(p_new[0], st[3], 0).numpy(), 0.25, 0.04)
+    _compare(lg[3], model.forward(p_new[1], st[4], 0).numpy(), 0.25, 0.04)
+    eng.close()

@@ -346,3 +346,33 @@ def test_argmax_first_index_on_ties():
     sync_ok(E.lib().ms_launch_argmax(ptr(lg.to(DEV)), 9, V, ptr(out), None))
     assert out.cpu().tolist() == kernels_ref.argmax_rows(lg).tolist()
     assert out[1].item() == 100 and out[2].item() == 0 and out[3].item() == V - 1
+
+
+def test_paged_attention_ignores_nan_in_stale_page_slots():
+    """Pool slots past each row's context hold NaN (as never-written pages
+    may); decode attention must not read them into its result."""
+    gen = torch.Generator().manual_seed(77)
+    pool, hkv, D = 64, 8, 128
+    lens = [1, 15, 16, 17, 40, 100]
+    kp = torch.full((pool, hkv, 16, D), float("nan"))
+    vp = torch.full((pool, hkv, 16, D), float("nan"))
+    tables = torch.zeros(len(lens), 8, dtype=torch.int32)
+    perm = torch.randperm(pool, generator=gen)
+    off = 0
+    for i, L in enumerate(lens):
+        nb = (L + 15) // 16
+        tables[i, :nb] = perm[off:off + nb].to(torch.int32)
+        off += nb
+        pos = torch.arange(L)
+        pages = tables[i, pos // 16].long()
+        kp[pages, :, pos % 16] = torch.randn(L, hkv, D, generator=gen)
+        vp[pages, :, pos % 16] = torch.randn(L, hkv, D, generator=gen)
+    q = torch.randn(len(lens), 16, D, generator=gen).bfloat16()
+    kb, vb = kp.bfloat16(), vp.bfloat16()
+    want = kernels_ref.paged_gqa_attention(q.float(), torch.nan_to_num(kb.float()), torch.nan_to_num(vb.float()),
+                                           tables, lens, 1.0 / math.sqrt(D))
+    out = torch.empty(q.shape, dtype=torch.bfloat16, device=DEV)
+    attention(q.to(DEV), kb.to(DEV), vb.to(DEV), tables.to(DEV), torch.tensor(lens, dtype=torch.int32, device=DEV),
+              out, part=4)
+    assert torch.isfinite(out).all()
+    assert max_abs(out.cpu(), want) <= 2e-2
