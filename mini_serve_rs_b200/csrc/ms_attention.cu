@@ -161,7 +161,8 @@ __global__ void __launch_bounds__(kWarps * 32) paged_attention_kernel(Params p) 
   for (int k = 0; k < nb_w; ++k) {
     const int s = k % NSTAGE;
     const uint32_t parity = (k / NSTAGE) & 1;
-    if (!mbar_wait_bounded(&my_bar[s], parity)) {
+    // the whole warp agrees before leaving, so no lane is left waiting in a shuffle
+    if (!__all_sync(kFull, mbar_wait_bounded(&my_bar[s], parity))) {
       failed = true;
       kfail = k;
       break;

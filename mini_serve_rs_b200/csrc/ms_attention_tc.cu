@@ -147,7 +147,8 @@ __global__ void __launch_bounds__(kWarps * 32)
 
   for (int k = 0; k < nb_w; ++k) {
     const int s = k % NSTAGE;
-    if (!mbar_wait_bounded(&my_bar[s], (k / NSTAGE) & 1)) {
+    // the whole warp agrees before leaving, so no lane is left waiting in a shuffle
+    if (!__all_sync(kFull, mbar_wait_bounded(&my_bar[s], (k / NSTAGE) & 1))) {
       failed = true;
       kfail = k;
       break;

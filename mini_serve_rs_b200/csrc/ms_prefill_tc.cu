@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(kWarps * 32)
   for (int k = 0; k < npages; ++k) {
     const int s = k % NSTAGE;
     const uint32_t ph = (k / NSTAGE) & 1;
-    const bool ok = mbar_wait_bounded(&full[s], ph);
+    const bool ok = __all_sync(kFull, mbar_wait_bounded(&full[s], ph));  // warp-uniform
     const int key0 = k * kBS;
     if (ok && key0 <= warp_max_pos) {  // warp-uniform: some row of this warp sees this page
       unsigned char *st = smem + size_t(s) * STAGE_BYTES;
