@@ -363,8 +363,8 @@ def test_bf16_mixed_prefill_and_decode_step_matches_oracle(config1):
     toks, _ = eng.step([1, 2])
     for sid, p in zip((1, 2), p_dec):
         model.forward(p, st[sid], 0)
-    for sid, p in zip((3, 4), p_new):
-        eng.admit(sid, p, list(range(4 * sid + 8, 4 * sid + 14)))
+    for sid, p in zip((3, 4), p_new):  # pages 20..25 and 30..35, disjoint from each other and 4..11
+        eng.admit(sid, p, list(range(10 * sid - 10, 10 * sid - 4)))
         st[sid] = SeqState(cfg, 80)
     inputs = [int(toks[0]), int(toks[1]), 0, 0]
     pos = [23, 50, 0, 0]
