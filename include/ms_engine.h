@@ -137,6 +137,18 @@ int ms_engine_finalize(ms_engine *eng);
 int ms_engine_memory(const ms_engine *eng, int64_t *weights_bytes, int64_t *pool_bytes,
                      int64_t *workspace_bytes);
 
+/* ---- tensor parallelism (no counterpart in the reference) ---------------
+ * One engine per GPU; tp_size engines form one model replica, sharded by KV
+ * head (q/k/v rows and o_proj columns per KV-head group, gate/up rows and
+ * down columns per intermediate slice).  The partial o_proj and down_proj
+ * outputs are summed with an NCCL all-reduce on the engine stream.  These
+ * helpers create the communicator with the NCCL already loaded in the process
+ * (or libnccl.so.2): rank 0 makes the id, every rank passes the same bytes. */
+int ms_nccl_get_unique_id(uint8_t *out, int32_t len);
+int ms_nccl_comm_init(void **comm_out, int32_t nranks, const uint8_t *unique_id, int32_t rank,
+                      int32_t device);
+int ms_nccl_comm_destroy(void *comm);
+
 /* ---- sequence lifetime (scheduler deltas) ------------------------------ */
 
 /* Admit a sequence (scheduler.rs:347-369): its prompt tokens and the logical

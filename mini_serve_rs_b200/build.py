@@ -66,7 +66,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     lib64 = cuda_home() / "lib64"
     tmp = LIB.with_suffix(".so.tmp")
     cmd = [nvcc(), *ARCH, "-shared", "-Xcompiler", "-fPIC", *map(str, objs), "-o", str(tmp),
-           "-L", str(lib64), "-lcublas", "-lcudart", "-Xlinker", f"-rpath,{lib64}"]
+           "-L", str(lib64), "-lcublas", "-lcudart", "-ldl", "-Xlinker", f"-rpath,{lib64}"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -50,8 +50,14 @@ static uint16_t f32_to_bf16(float f) {
 int create_impl(const ms_model_cfg *cfg, const ms_engine_opts *opts, Engine *eng) {
   eng->cfg = *cfg;
   eng->opts = *opts;
-  if (opts->tp_size != 1 || opts->tp_rank != 0) {
-    return eng->fail(MS_E_INVALID, "tensor parallelism needs tp_size == 1 in this build");
+  if (opts->tp_size < 1 || opts->tp_rank < 0 || opts->tp_rank >= opts->tp_size)
+    return eng->fail(MS_E_INVALID, "tp_rank must lie in [0, tp_size)");
+  if (opts->tp_size > 1) {
+    if (!opts->nccl_comm) return eng->fail(MS_E_INVALID, "tp_size > 1 needs an NCCL communicator");
+    if (!nccl_available()) return eng->fail(MS_E_DEVICE, "NCCL is not loadable in this process");
+    if (cfg->num_kv_heads % opts->tp_size || cfg->num_heads % opts->tp_size ||
+        cfg->intermediate_size % opts->tp_size)
+      return eng->fail(MS_E_INVALID, "heads, kv heads and intermediate size must divide by tp_size");
   }
   if (cfg->head_dim != 128 && cfg->head_dim != 64) return eng->fail(MS_E_INVALID, "head_dim must be 64 or 128");
   if (cfg->num_heads <= 0 || cfg->num_kv_heads <= 0 || cfg->num_heads % cfg->num_kv_heads)
@@ -64,18 +70,21 @@ int create_impl(const ms_model_cfg *cfg, const ms_engine_opts *opts, Engine *eng
       opts->max_blocks_per_seq <= 0)
     return eng->fail(MS_E_INVALID, "pool_blocks, max_seqs, max_tokens_per_step and max_blocks_per_seq must be positive");
   const int vec = cfg->dtype == MS_DTYPE_F32 ? 4 : 8;
-  if (cfg->hidden_size % vec || cfg->intermediate_size % vec || cfg->hidden_size / vec > 1024)
+  if (cfg->hidden_size % vec || (cfg->intermediate_size / opts->tp_size) % vec || cfg->hidden_size / vec > 1024)
     return eng->fail(MS_E_INVALID, "hidden/intermediate sizes must be multiples of 8 (bf16) or 4 (f32)");
   if (opts->max_seqs > 16384) return eng->fail(MS_E_INVALID, "max_seqs must be <= 16384");
 
   eng->dev = opts->device;
   eng->dtype = cfg->dtype;
   eng->esize = dtype_size(cfg->dtype);
+  eng->tp = opts->tp_size;
+  eng->rank = opts->tp_rank;
+  eng->comm = opts->nccl_comm;
   eng->D = cfg->head_dim;
-  eng->hq = cfg->num_heads;
-  eng->hkv = cfg->num_kv_heads;
+  eng->hq = cfg->num_heads / eng->tp;
+  eng->hkv = cfg->num_kv_heads / eng->tp;
   eng->H = cfg->hidden_size;
-  eng->I = cfg->intermediate_size;
+  eng->I = cfg->intermediate_size / eng->tp;
   eng->V = cfg->vocab_size;
   eng->L = cfg->num_layers;
   eng->qkv_dim = (eng->hq + 2 * eng->hkv) * eng->D;

@@ -43,7 +43,9 @@ struct Engine {
   void *blas_ws = nullptr;
   int dtype = MS_DTYPE_BF16;
   size_t esize = 2;
-  int D = 128, hq = 0, hkv = 0, H = 0, I = 0, V = 0, L = 0;
+  int D = 128, hq = 0, hkv = 0, H = 0, I = 0, V = 0, L = 0;  // hq, hkv, I: this rank's shard
+  int tp = 1, rank = 0;
+  void *comm = nullptr;  // ncclComm_t when tp > 1
   int qkv_dim = 0;
 
   // weights (one allocation)

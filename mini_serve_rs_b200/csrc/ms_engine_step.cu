@@ -8,7 +8,10 @@
 // prompt + outputs - 1 (candle.rs:622-628).  Each sequence gets its greedy
 // token from the f32 logits of its last packed row (candle.rs:737-751).
 #include <algorithm>
+#include <chrono>
+#include <cstdlib>
 #include <string>
+#include <thread>
 
 #include "ms_engine.h"
 
@@ -222,6 +225,30 @@ int step_wait_impl(Engine *eng, uint32_t *out_tokens, uint8_t *out_flags) {
   eng->pending = false;
   const int S = eng->last_nseq;
   if (S == 0) return MS_OK;
+  if (eng->tp > 1) {
+    // Host watchdog for the collectives: a peer that died or hangs would
+    // otherwise block the step forever.  Poll the step's completion and the
+    // communicator's asynchronous error; past the deadline abort the
+    // communicator and quarantine the engine.
+    static const double timeout_s = [] {
+      const char *e = std::getenv("MS_STEP_TIMEOUT_S");
+      return e ? std::atof(e) : 120.0;
+    }();
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+      const cudaError_t q = cudaEventQuery(eng->done_ev);
+      if (q == cudaSuccess) break;
+      if (q != cudaErrorNotReady) return eng->fail(MS_E_DEVICE, std::string("step: ") + cudaGetErrorString(q));
+      const int ae = nccl_async_error(eng->comm);
+      const double el = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+      if ((ae != 0 && ae != 7 /* ncclInProgress */) || el > timeout_s) {
+        nccl_abort(eng->comm);
+        return eng->fail(MS_E_DEVICE, ae != 0 ? "NCCL asynchronous error " + std::to_string(ae)
+                                              : std::string("step exceeded the collective timeout"));
+      }
+      std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+  }
   MS_CUDA_TRY(cudaEventSynchronize(eng->done_ev));
   if (*eng->h_status != 0)
     return eng->fail(MS_E_DEVICE, "device status word " + std::to_string(*eng->h_status) +

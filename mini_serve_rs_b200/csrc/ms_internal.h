@@ -102,6 +102,12 @@ cudaError_t launch_embedding(const int32_t *tokens, const void *table, void *out
 cudaError_t launch_convert(const void *src, int src_dtype, void *dst, int dst_dtype, int64_t n,
                            cudaStream_t stream);
 
+// NCCL, resolved at run time (ms_nccl.cu)
+bool nccl_available();
+int nccl_allreduce_sum(void *buf, size_t count, int dtype, void *comm, cudaStream_t stream);
+int nccl_async_error(void *comm);
+void nccl_abort(void *comm);
+
 struct PackArgs {
   const int32_t *seq_row;    // [nseq] block-table row (engine slot) of each sequence
   const int32_t *seq_ntok;   // [nseq] tokens this step

@@ -61,6 +61,9 @@ _SIGS = {
     "ms_engine_set_profiling": ([_P, _I32], C.c_int),
     "ms_engine_profile": ([_P, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(C.c_double),
                            C.POINTER(C.c_double)], C.c_int),
+    "ms_nccl_get_unique_id": ([C.c_char_p, _I32], C.c_int),
+    "ms_nccl_comm_init": ([C.POINTER(_P), _I32, C.c_char_p, _I32, _I32], C.c_int),
+    "ms_nccl_comm_destroy": ([_P], C.c_int),
     "ms_is_healthy": ([_P], C.c_int),
     "ms_mark_unhealthy": ([_P], C.c_int),
     "ms_inject_fault": ([_P, _I32], C.c_int),
@@ -172,7 +175,7 @@ class Engine:
 
     def __init__(self, cfg, *, device: int = 0, pool_blocks: int, max_seqs: int = 256,
                  max_tokens_per_step: int = 8192, max_blocks_per_seq: int | None = None,
-                 dtype: int = MS_DTYPE_BF16):
+                 dtype: int = MS_DTYPE_BF16, tp_rank: int = 0, tp_size: int = 1, nccl_comm: int | None = None):
         """cfg: any object with the fields of oracle-style Config (vocab_size,
         hidden_size, intermediate_size, num_hidden_layers, num_attention_heads,
         num_key_value_heads, head_dim or hd(), max_position_embeddings,
@@ -186,7 +189,7 @@ class Engine:
                                 int(cfg.attention_bias), int(cfg.tie_word_embeddings), dtype)
         if max_blocks_per_seq is None:
             max_blocks_per_seq = (cfg.max_position_embeddings + 15) // 16
-        self.opts = MsEngineOpts(device, 0, 1, None, pool_blocks, 16, max_seqs, max_tokens_per_step,
+        self.opts = MsEngineOpts(device, tp_rank, tp_size, nccl_comm, pool_blocks, 16, max_seqs, max_tokens_per_step,
                                  max_blocks_per_seq)
         self.dtype = dtype
         self.max_seqs = max_seqs
@@ -340,3 +343,26 @@ class Engine:
         p = C.c_void_p()
         self._check(self.lib.ms_debug_pool_ptr(self.h, layer, which, C.byref(p)), "pool_ptr")
         return p.value
+
+
+# ---- NCCL communicator helpers (tensor parallelism) ------------------------------
+
+
+def nccl_unique_id() -> bytes:
+    buf = C.create_string_buffer(128)
+    rc = lib().ms_nccl_get_unique_id(buf, 128)
+    if rc != MS_OK:
+        raise error_for(rc, "ms_nccl_get_unique_id failed (NCCL not loadable?)")
+    return buf.raw
+
+
+def nccl_comm_init(nranks: int, unique_id: bytes, rank: int, device: int) -> int:
+    comm = C.c_void_p()
+    rc = lib().ms_nccl_comm_init(C.byref(comm), nranks, unique_id, rank, device)
+    if rc != MS_OK:
+        raise error_for(rc, "ms_nccl_comm_init failed")
+    return comm.value
+
+
+def nccl_comm_destroy(comm: int):
+    lib().ms_nccl_comm_destroy(comm)
