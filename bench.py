@@ -45,6 +45,9 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--batch", type=int, default=BATCH)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config5", action="store_true",
+                    help="BASELINE config 5: Qwen2.5-7B arch, 256 seqs x ctx U[1024,32768], tensor parallel")
+    ap.add_argument("--tp", type=int, default=2, help="tensor-parallel size for --config5")
     ap.add_argument("--kernel", choices=["attention"], default=None,
                     help="time one kernel in isolation (BASELINE config 2 for attention) instead of the step")
     return ap.parse_args()
@@ -181,12 +184,12 @@ def cudart():
     return lib
 
 
-def fill_pool(eng, cfg, pool_blocks, device, seed):
+def fill_pool(eng, cfg, pool_blocks, device, seed, kv_heads=None):
     """Seeded N(0,1) bf16 K/V in every page: one random chunk copied over each
     layer's K and V pool (the contents do not change the kernel's traffic)."""
     import torch
     rt = cudart()
-    layer_bytes = pool_blocks * cfg.num_key_value_heads * 16 * cfg.hd() * 2
+    layer_bytes = pool_blocks * (kv_heads or cfg.num_key_value_heads) * 16 * cfg.hd() * 2
     chunk = min(layer_bytes, 512 << 20)
     g = torch.Generator(device=f"cuda:{device}").manual_seed(seed)
     src = torch.randn(chunk // 2, generator=g, dtype=torch.bfloat16, device=f"cuda:{device}")
@@ -205,27 +208,30 @@ def fill_pool(eng, cfg, pool_blocks, device, seed):
     del src
 
 
-def run_ours(args, rank, world, local):
+def run_decode(args, rank, world, local, cfg, ctx, seed, tp_rank=0, tp_size=1, comm=None):
+    """Build one engine (one rank of a replica), admit len(ctx) sequences whose
+    contexts are already cached (synthetic N(0,1) K/V), then time decode steps:
+    `value` with decode inputs fed back on the device, `e2e` through ms_step with
+    host token arrays.  seed is per replica (all TP ranks of a replica agree)."""
     import numpy as np
     import torch
     import torch.distributed as dist
 
     from mini_serve_rs_b200 import engine as E
-    from mini_serve_rs_b200.config import qwen3_0_6b, random_device_weights
+    from mini_serve_rs_b200.config import iter_random_device_weights
 
     torch.cuda.set_device(local)
-    cfg = qwen3_0_6b()
-    B, K, W = args.batch, args.steps, args.warmup
-    ctx = contexts(B, SEED + rank)
+    B, K, W = len(ctx), args.steps, args.warmup
     extra = W + 2 * K + 2
     need = [(int(c) + extra + 15) // 16 for c in ctx]
-    pool_blocks = int(sum(need) * 1.05) + 64
-    mbps = (MAX_CTX + extra + 15) // 16 + 1
+    pool_blocks = int(sum(need) * 1.02) + 64
+    mbps = (max(int(c) for c in ctx) + extra + 15) // 16 + 1
     eng = E.Engine(cfg, device=local, pool_blocks=pool_blocks, max_seqs=B, max_tokens_per_step=max(B, 256),
-                   max_blocks_per_seq=mbps, dtype=E.MS_DTYPE_BF16)
-    eng.load_weights(random_device_weights(cfg, SEED, device=f"cuda:{local}"))
-    fill_pool(eng, cfg, pool_blocks, local, SEED + 17 * rank)
-    rng = np.random.Generator(np.random.PCG64(SEED + rank))
+                   max_blocks_per_seq=mbps, dtype=E.MS_DTYPE_BF16, tp_rank=tp_rank, tp_size=tp_size,
+                   nccl_comm=comm)
+    eng.load_weights(iter_random_device_weights(cfg, SEED, device=f"cuda:{local}"))
+    fill_pool(eng, cfg, pool_blocks, local, seed + 17 * tp_rank, kv_heads=cfg.num_key_value_heads // tp_size)
+    rng = np.random.Generator(np.random.PCG64(seed))
     perm = rng.permutation(pool_blocks).astype(np.int32)
     ids = np.arange(1, B + 1, dtype=np.uint64)
     off = 0
@@ -296,6 +302,11 @@ def run_ours(args, rank, world, local):
     return res
 
 
+def run_ours(args, rank, world, local):
+    from mini_serve_rs_b200.config import qwen3_0_6b
+    return run_decode(args, rank, world, local, qwen3_0_6b(), contexts(args.batch, SEED + rank), SEED + rank)
+
+
 def attention_config2(device: int, seed: int = 2, pool: int = 40000):
     """BASELINE config 2's isolated op: 256 rows, ctx ~ U[1,4096], 16/8 heads x
     128, bf16, block tables a seeded random permutation of the page pool."""
@@ -364,6 +375,54 @@ def run_attention_kernel(args, local):
                       "peak_gbs": peak, "frac": gbs / peak, "peak_source": kind}), flush=True)
 
 
+def run_config5(args, rank, world, local):
+    """BASELINE config 5 decode: Qwen2.5-7B architecture, tensor parallel by KV
+    head over `--tp` GPUs per replica (world / tp replicas), 256 sequences per
+    replica with contexts U[1024, 32768 - steps] (the model's 32768 positions
+    bound the last decode step), bf16.  Prints its own JSON line."""
+    import numpy as np
+    import torch.distributed as dist
+
+    from mini_serve_rs_b200 import engine as E
+    from mini_serve_rs_b200.config import qwen2_5_7b
+    tp = args.tp
+    if world < 2 or world % tp != 0:
+        raise SystemExit("--config5 runs under torchrun with a multiple of --tp ranks (TP=1 does not fit 248 GB of KV)")
+    group, tp_rank = rank // tp, rank % tp
+    uid = E.nccl_unique_id() if tp_rank == 0 else None
+    uids = [None] * world
+    dist.all_gather_object(uids, uid)
+    comm = E.nccl_comm_init(tp, uids[group * tp], tp_rank, local)
+    cfg = qwen2_5_7b()
+    extra = args.warmup + 2 * args.steps + 2
+    rng = np.random.Generator(np.random.PCG64(SEED + group))
+    ctx = rng.integers(1024, cfg.max_position_embeddings - extra + 1, args.batch)
+    r = run_decode(args, rank, world, local, cfg, ctx, SEED + group, tp_rank, tp, comm)
+    E.nccl_comm_destroy(comm)
+    if rank == 0:
+        replicas = world // tp
+        value = replicas * args.batch * args.steps / (r["ms"] / 1000.0)
+        e2e = replicas * args.batch * args.steps / (r["ms_e2e"] / 1000.0)
+        per_launch_ms = r["attn_ms"] / max(1, r["attn_launches"])
+        per_launch_bytes = r["attn_bytes"] / max(1, r["attn_launches"])
+        achieved = per_launch_bytes / (per_launch_ms / 1000.0) / 1e9
+        peak, kind = peaks()
+        print(json.dumps({
+            "metric": "decode tokens/s (Qwen2.5-7B arch, TP by KV head)", "value": value, "unit": UNIT,
+            "n_gpus": world, "tp": tp, "replicas": replicas, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": r["ms"] / args.steps, "tokens_per_s_per_gpu": value / world, "dtype": "bf16",
+            "data": "synthetic (seeded random-init weights, N(0,1) KV)",
+            "config": {"workload": "BASELINE config 5", "seqs_per_replica": args.batch,
+                       "ctx": f"uniform[1024,{cfg.max_position_embeddings - extra}]", "ctx_mean": r["ctx_mean"]},
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
+            "gpu_launches": r["gpu_launches"], "clocks": r["clocks"],
+            "roofline": {"kernel": "paged_attention_tc_kernel (per rank: its KV heads)", "bound": "hbm",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({kind})", "ms_per_launch": per_launch_ms,
+                         "share_of_step": r["attn_ms"] / r["ms"]},
+            "memory_bytes": r["memory"]}), flush=True)
+
+
 def traffic_per_launch(algorithmic_bytes: float):
     """dram bytes (read + write) per attention launch: the committed ncu ratio of
     dram bytes to algorithmic bytes (profiles/k3_attention_traffic.json, from a
@@ -412,10 +471,12 @@ def main():
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device(f"cuda:{local}"))
-    try:
-        r = run_ours(args, rank, world, local)
-    finally:
-        pass
+    if args.config5:
+        run_config5(args, rank, world, local)
+        dist.barrier()
+        dist.destroy_process_group()
+        return
+    r = run_ours(args, rank, world, local)
     if rank == 0:
         B, K = args.batch, args.steps
         value = n * B * K / (r["ms"] / 1000.0)

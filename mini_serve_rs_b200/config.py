@@ -60,6 +60,20 @@ def weight_shapes(cfg) -> Dict[str, tuple]:
     return out
 
 
+def iter_random_device_weights(cfg, seed: int, device: str = "cuda", std: float = 0.02):
+    """As random_device_weights, one tensor at a time (so a 7B model never
+    holds a full f32 copy on the device)."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    shapes = weight_shapes(cfg)
+    for name in sorted(shapes):
+        if name.endswith("norm.weight"):
+            yield name, torch.ones(shapes[name], dtype=torch.float32, device=device)
+        else:
+            yield name, torch.randn(shapes[name], generator=g, dtype=torch.float32, device=device) * std
+
+
 def random_device_weights(cfg, seed: int, device: str = "cuda", std: float = 0.02):
     """Seeded random-init weights generated directly on the GPU (benchmarks):
     matrices and biases ~ N(0, std), norm weights 1."""

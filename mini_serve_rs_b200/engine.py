@@ -224,10 +224,12 @@ class Engine:
             pass
 
     # -- weights
-    def load_weights(self, weights: Dict[str, "object"]):
-        """weights: name -> torch tensor (CPU or on this engine's device)."""
+    def load_weights(self, weights):
+        """weights: dict or iterable of (name, torch tensor) on the CPU or on this
+        engine's device; full (unsharded) tensors under tensor parallelism."""
         import torch
-        for name, t in weights.items():
+        items = weights.items() if hasattr(weights, "items") else weights
+        for name, t in items:
             t = t.contiguous()
             on_dev = 1 if t.is_cuda else 0
             if not on_dev and t.dtype not in (torch.float32, torch.bfloat16, torch.float16):
