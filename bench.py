@@ -48,7 +48,7 @@ def parse():
     ap.add_argument("--config5", action="store_true",
                     help="BASELINE config 5: Qwen2.5-7B arch, 256 seqs x ctx U[1024,32768], tensor parallel")
     ap.add_argument("--tp", type=int, default=2, help="tensor-parallel size for --config5")
-    ap.add_argument("--kernel", choices=["attention"], default=None,
+    ap.add_argument("--kernel", choices=["attention", "norm_rope"], default=None,
                     help="time one kernel in isolation (BASELINE config 2 for attention) instead of the step")
     return ap.parse_args()
 
@@ -222,7 +222,8 @@ def run_decode(args, rank, world, local, cfg, ctx, seed, tp_rank=0, tp_size=1, c
 
     torch.cuda.set_device(local)
     B, K, W = len(ctx), args.steps, args.warmup
-    extra = W + 2 * K + 2
+    KP = min(K, 10)
+    extra = W + 2 * K + KP + 2
     need = [(int(c) + extra + 15) // 16 for c in ctx]
     pool_blocks = int(sum(need) * 1.02) + 64
     mbps = (max(int(c) for c in ctx) + extra + 15) // 16 + 1
@@ -251,9 +252,8 @@ def run_decode(args, rank, world, local, cfg, ctx, seed, tp_rank=0, tp_size=1, c
         toks, _ = eng.step_wait()
     torch.cuda.synchronize()
 
-    # ---- value: device-resident inputs (decode tokens fed back on the device)
-    eng.profile()  # reset the event log
-    eng.set_profiling(True)
+    # ---- value: device-resident inputs (decode tokens fed back on the device);
+    # pure-decode steps replay a captured CUDA graph (captured during warm-up)
     launches0 = eng.profile()[0]
     barrier()
     torch.cuda.synchronize()
@@ -266,15 +266,26 @@ def run_decode(args, rank, world, local, cfg, ctx, seed, tp_rank=0, tp_size=1, c
         e1.record(stream)
         e1.synchronize()
     ms = e0.elapsed_time(e1)
-    klaunch, alaunch, attn_ms, attn_bytes = eng.profile()
+    gpu_launches = eng.profile()[0] - launches0
+    graphs = eng.graph_stats()
+    torch.cuda.synchronize()
+    barrier()
+
+    # ---- attention kernel time inside the step: KP more steps with CUDA
+    # events around every paged-attention launch (eager: events need launches)
+    eng.profile()  # reset the event log
+    eng.set_profiling(True)
+    for _ in range(KP):
+        eng.step_launch(ids, None, None, E.MS_STEP_TOKENS_FROM_DEVICE)
+        toks, _ = eng.step_wait()
+    _, alaunch, attn_ms, attn_bytes = eng.profile()
     eng.set_profiling(False)
-    gpu_launches = klaunch - launches0
     torch.cuda.synchronize()
     barrier()
 
     # ---- e2e: through the public step call with host token arrays
     # step 1 replayed the last cached prompt token; every later step added one
-    pos = np.array([int(c) + W + K - 1 for c in ctx], dtype=np.int32)
+    pos = np.array([int(c) + W + K + KP - 1 for c in ctx], dtype=np.int32)
     host_toks = np.asarray(toks, dtype=np.uint32)
     barrier()
     torch.cuda.synchronize()
@@ -295,7 +306,8 @@ def run_decode(args, rank, world, local, cfg, ctx, seed, tp_rank=0, tp_size=1, c
     res = {
         "ms": ms, "ms_e2e": ms_e2e, "gpu_launches": gpu_launches, "clocks": clk.summary(),
         "attn_launches": alaunch, "attn_ms": attn_ms, "attn_bytes": attn_bytes,
-        "h2d": (4 * B + 3 * B) * 4, "d2h": B * 4 + 4, "ctx_mean": float(np.mean(ctx)),
+        "h2d": (4 + 7 * B) * 4, "d2h": B * 4 + 4, "ctx_mean": float(np.mean(ctx)),
+        "graphs": {"captured": graphs[0], "replayed": graphs[1]}, "kp": KP,
         "memory": eng.memory(),
     }
     eng.close()
@@ -394,7 +406,7 @@ def run_config5(args, rank, world, local):
     dist.all_gather_object(uids, uid)
     comm = E.nccl_comm_init(tp, uids[group * tp], tp_rank, local)
     cfg = qwen2_5_7b()
-    extra = args.warmup + 2 * args.steps + 2
+    extra = args.warmup + 2 * args.steps + min(args.steps, 10) + 2
     rng = np.random.Generator(np.random.PCG64(SEED + group))
     ctx = rng.integers(1024, cfg.max_position_embeddings - extra + 1, args.batch)
     r = run_decode(args, rank, world, local, cfg, ctx, SEED + group, tp_rank, tp, comm)
@@ -419,8 +431,90 @@ def run_config5(args, rank, world, local):
             "roofline": {"kernel": "paged_attention_tc_kernel (per rank: its KV heads)", "bound": "hbm",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({kind})", "ms_per_launch": per_launch_ms,
-                         "share_of_step": r["attn_ms"] / r["ms"]},
-            "memory_bytes": r["memory"]}), flush=True)
+                         "share_of_step": (r["attn_ms"] / r["kp"]) / (r["ms"] / args.steps)},
+            "cuda_graphs": r["graphs"], "memory_bytes": r["memory"]}), flush=True)
+
+
+def run_norm_rope_kernels(args, local):
+    """a packed T=8192 bf16 batch (8 prefill chunks of
+    U[256,768] tokens, the rest single decode tokens): K4 fused residual-add +
+    RMSNorm over hidden 1024, then K5 QK-norm + RoPE (theta 1e6, 16/8 heads x
+    128, positions per sequence in [0, 8192)) fused with the paged K/V append.
+    L2 is flushed (256 MB scribble) before every timed launch; median of K."""
+    import ctypes as C
+    import numpy as np
+    import torch
+    from mini_serve_rs_b200 import engine as E
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    lib = E.lib()
+    T, H, hq, hkv, D = 8192, 1024, 16, 8, 128
+    rng = np.random.Generator(np.random.PCG64(3))
+    pos = []
+    for _ in range(8):
+        n = int(rng.integers(256, 769))
+        st = int(rng.integers(0, 8192 - n))
+        pos.extend(range(st, st + n))
+    while len(pos) < T:
+        pos.append(int(rng.integers(0, 8192)))
+    g = torch.Generator(device=dev).manual_seed(3)
+    x = torch.randn(T, H, generator=g, device=dev, dtype=torch.bfloat16)
+    r = torch.randn(T, H, generator=g, device=dev, dtype=torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(H, generator=g, device=dev)).to(torch.bfloat16)
+    resid, normed = torch.empty_like(x), torch.empty_like(x)
+    qkv = torch.randn(T, (hq + 2 * hkv) * D, generator=g, device=dev, dtype=torch.bfloat16)
+    qn = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).to(torch.bfloat16)
+    kn = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).to(torch.bfloat16)
+    half = D // 2
+    inv = torch.tensor([1.0 / (1e6 ** (i / D)) for i in range(0, D, 2)], dtype=torch.float32)
+    fr = torch.arange(8192, dtype=torch.float32).reshape(-1, 1) * inv.reshape(1, -1)
+    cos, sin = fr.cos().to(torch.bfloat16).to(dev), fr.sin().to(torch.bfloat16).to(dev)
+    posd = torch.tensor(pos, dtype=torch.int32, device=dev)
+    pool = 640
+    slots = torch.from_numpy(rng.permutation(pool * 16)[:T].astype(np.int64)).to(dev)
+    kp = torch.zeros(pool, hkv, 16, D, device=dev, dtype=torch.bfloat16)
+    vp = torch.zeros_like(kp)
+    qo = torch.empty(T, hq, D, device=dev, dtype=torch.bfloat16)
+    scribble = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    p = lambda t: C.c_void_p(t.data_ptr())
+    st = torch.cuda.current_stream()
+    ptr_st = C.c_void_p(st.cuda_stream)
+
+    def k4():
+        assert lib.ms_launch_add_rmsnorm(p(x), p(r), None, p(w), p(resid), p(normed), T, H, 1e-6,
+                                         E.MS_DTYPE_BF16, ptr_st) == 0
+
+    def k5():
+        assert lib.ms_launch_qk_norm_rope_append(p(qkv), None, p(qn), p(kn), p(cos), p(sin), p(posd), p(slots),
+                                                 p(qo), p(kp), p(vp), T, hq, hkv, D, 16, 1e-6, E.MS_DTYPE_BF16,
+                                                 ptr_st) == 0
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        ts = []
+        for _ in range(args.steps):
+            scribble.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            fn()
+            e1.record(st)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        ts.sort()
+        return ts[len(ts) // 2]
+
+    peak, kind = peaks()
+    k4_bytes = T * H * 2 * 4 + H * 2
+    k5_qk = T * (hq + hkv) * D * 2 * 2
+    k5_bytes = T * (hq + 2 * hkv) * D * 2 * 2 + T * 12 + 2 * D * 2
+    t4, t5 = timed(k4), timed(k5)
+    print(json.dumps({"workload": "BASELINE config 3 (T=8192 packed, bf16)", "l2": "256 MB scribble before each launch",
+                      "k4_add_rmsnorm": {"ms": t4, "bytes": k4_bytes, "gbs": k4_bytes / t4 / 1e6,
+                                         "frac": k4_bytes / t4 / 1e6 / peak},
+                      "k5_qk_norm_rope_append": {"ms": t5, "bytes": k5_bytes, "qk_only_bytes": k5_qk,
+                                                 "gbs": k5_bytes / t5 / 1e6, "frac": k5_bytes / t5 / 1e6 / peak},
+                      "peak_gbs": peak, "peak_source": kind}), flush=True)
 
 
 def traffic_per_launch(algorithmic_bytes: float):
@@ -448,6 +542,9 @@ def main():
 
     if args.kernel == "attention":
         run_attention_kernel(args, local)
+        return
+    if args.kernel == "norm_rope":
+        run_norm_rope_kernels(args, local)
         return
 
     if args.impl == "reference":
@@ -496,8 +593,8 @@ def main():
                              "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
                              "traffic": traffic_per_launch(per_launch_bytes), "algorithmic_bytes_per_launch": per_launch_bytes,
                              "ms_per_launch": per_launch_ms, "launches": r["attn_launches"],
-                             "share_of_step": r["attn_ms"] / r["ms"]},
-                "memory_bytes": r["memory"]}
+                             "share_of_step": (r["attn_ms"] / r["kp"]) / (r["ms"] / K)},
+                "cuda_graphs": r["graphs"], "memory_bytes": r["memory"]}
         if world <= 1 and not args.no_cpu_baseline:
             tps, cores, desc = cpu_sample(8, 2, 1)
             line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": desc}

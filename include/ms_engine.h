@@ -193,6 +193,18 @@ int ms_engine_set_profiling(ms_engine *eng, int32_t on);
 int ms_engine_profile(ms_engine *eng, int64_t *kernel_launches, int64_t *attn_launches,
                       double *attn_ms_total, double *attn_bytes_total);
 
+/* ---- CUDA graphs of decode steps (no counterpart in the reference) -------
+ * Steps with one token per sequence, at most num_seqs new block-table
+ * entries and tp_size 1 are replayed from captured CUDA graphs keyed by
+ * (num_seqs, attention partition size, context capacity): the first step of
+ * a key runs eagerly, the second is captured, later ones replay (the step
+ * description goes through a fixed-layout staging buffer).  Results are
+ * identical to eager steps.  On by default; the environment variable
+ * MS_CUDA_GRAPHS=0 or ms_engine_set_graphs(eng, 0) turns it off (which also
+ * drops the cached graphs).  Not used while profiling is on. */
+int ms_engine_set_graphs(ms_engine *eng, int32_t on);
+int ms_engine_graph_stats(const ms_engine *eng, int64_t *captures, int64_t *replays, int32_t *cached);
+
 /* ---- health (traits.rs:175-180, candle.rs:324-335) --------------------- */
 int ms_is_healthy(const ms_engine *eng);
 int ms_mark_unhealthy(ms_engine *eng);

@@ -199,6 +199,26 @@ extern "C" int ms_engine_set_profiling(ms_engine *eng, int32_t on) {
   return MS_OK;
 }
 
+extern "C" int ms_engine_set_graphs(ms_engine *eng, int32_t on) {
+  if (!eng) return MS_E_INVALID;
+  if (eng->pending) return eng->fail(MS_E_INVALID, "ms_engine_set_graphs between launch and wait");
+  eng->graphs_enabled = on != 0;
+  if (!eng->graphs_enabled) {
+    cudaSetDevice(eng->dev);
+    cudaStreamSynchronize(eng->stream);
+    eng->drop_graphs();
+  }
+  return MS_OK;
+}
+
+extern "C" int ms_engine_graph_stats(const ms_engine *eng, int64_t *captures, int64_t *replays, int32_t *cached) {
+  if (!eng) return MS_E_INVALID;
+  if (captures) *captures = eng->graph_captures;
+  if (replays) *replays = eng->graph_replays;
+  if (cached) *cached = int32_t(eng->graphs.size());
+  return MS_OK;
+}
+
 extern "C" int ms_engine_profile(ms_engine *eng, int64_t *kernel_launches, int64_t *attn_launches,
                                  double *attn_ms_total, double *attn_bytes_total) {
   if (!eng) return MS_E_INVALID;

@@ -355,16 +355,19 @@ __device__ unsigned g_status_scratch;
 
 int choose_partition_blocks(int num_rows, int num_kv_heads, int max_ctx, long long total_blocks) {
   // Aim for >= ~16 CTAs per SM in total while keeping >= 2 pages per warp.
-  const int max_blk = std::max(1, (max_ctx + attn::kBS - 1) / attn::kBS);
+  // Depends on the total work only, not on the longest row: a partition
+  // larger than a row is simply that row's single partition, and a graph
+  // captured for a context capacity keeps the same partitioning as an eager
+  // launch of the same step.
   long long work = std::max<long long>(1, total_blocks) * num_kv_heads;
   const long long target_ctas = 148LL * 16;
   long long pb = (work + target_ctas - 1) / target_ctas;
   pb = std::max<long long>(pb, 2 * attn::kWarps);
   pb = std::min<long long>(pb, 64);
   pb = ((pb + attn::kWarps - 1) / attn::kWarps) * attn::kWarps;
-  if (pb >= max_blk) pb = max_blk;
   (void)num_rows;
-  return int(std::max<long long>(1, pb));
+  (void)max_ctx;
+  return int(pb);
 }
 
 int64_t attention_workspace_bytes(int num_rows, int num_heads, int max_ctx, int part_blocks) {

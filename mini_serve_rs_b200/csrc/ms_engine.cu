@@ -11,6 +11,7 @@
 #include <cstdio>
 #include <cstring>
 #include <new>
+#include <cstdlib>
 #include <string>
 
 #include "ms_engine.h"
@@ -251,6 +252,13 @@ int create_impl(const ms_model_cfg *cfg, const ms_engine_opts *opts, Engine *eng
 
   MS_CUDA_TRY(cudaMallocHost(&eng->h_next, S * 4));
   MS_CUDA_TRY(cudaMallocHost(&eng->h_status, 4));
+  // fixed staging of graph-replayed steps (the captured copy reads these pointers)
+  MS_CUDA_TRY(cudaMallocHost(&eng->h_gin, graph_in_elems(opts->max_seqs) * 4));
+  MS_CUDA_TRY(cudaMalloc(&eng->d_gin, graph_in_elems(opts->max_seqs) * 4));
+  {
+    const char *e = std::getenv("MS_CUDA_GRAPHS");
+    eng->graphs_enabled = !(e && std::string(e) == "0");
+  }
   // the memsets and table uploads above ran on the legacy stream; the engine
   // stream is non-blocking, so finish them before any step can be enqueued
   MS_CUDA_TRY(cudaDeviceSynchronize());
@@ -261,11 +269,12 @@ void destroy_impl(Engine *eng) {
   if (!eng) return;
   cudaSetDevice(eng->dev);
   if (eng->stream) cudaStreamSynchronize(eng->stream);
+  eng->drop_graphs();
   if (eng->blas) cublasDestroy(eng->blas);
   for (void *p : {eng->blas_ws, eng->wbuf, eng->cos_t, eng->sin_t, eng->pool, (void *)eng->d_block_tables,
-                  (void *)eng->d_slot_last, (void *)eng->d_status, eng->sbuf, (void *)eng->d_in})
+                  (void *)eng->d_slot_last, (void *)eng->d_status, eng->sbuf, (void *)eng->d_in, (void *)eng->d_gin})
     if (p) cudaFree(p);
-  for (void *p : {(void *)eng->h_in, (void *)eng->h_next, (void *)eng->h_status})
+  for (void *p : {(void *)eng->h_in, (void *)eng->h_next, (void *)eng->h_status, (void *)eng->h_gin})
     if (p) cudaFreeHost(p);
   for (cudaEvent_t e : eng->prof_ev) cudaEventDestroy(e);
   if (eng->done_ev) cudaEventDestroy(eng->done_ev);

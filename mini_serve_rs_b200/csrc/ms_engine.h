@@ -95,8 +95,30 @@ struct Engine {
   unsigned *h_status = nullptr;
   cudaEvent_t done_ev = nullptr;
 
+  // CUDA graphs of pure-decode steps, keyed by (batch, attention partition,
+  // context capacity); replayed with a fixed-layout step description
+  struct StepGraph {
+    int S = 0, part = 0, max_ctx_cap = 0;
+    cudaGraphExec_t exec = nullptr;
+    int64_t launches = 0;  // kernels per replay
+    uint64_t last_use = 0;
+  };
+  bool graphs_enabled = true;
+  std::vector<StepGraph> graphs;
+  std::unordered_map<int64_t, int> graph_warm;  // (S, part) -> eager steps run
+  uint64_t graph_clock = 0;
+  int64_t graph_captures = 0, graph_replays = 0;
+  int32_t *d_gin = nullptr, *h_gin = nullptr;  // fixed graph staging, graph_in_elems(max_seqs)
+  void drop_graphs() {
+    for (auto &g : graphs)
+      if (g.exec) cudaGraphExecDestroy(g.exec);
+    graphs.clear();
+    graph_warm.clear();
+  }
+
   // instrumentation
   int64_t kernel_launches = 0;
+  int64_t last_launches = 0;  // kernels enqueued by the last enqueue_forward
   bool profiling = false;
   std::vector<cudaEvent_t> prof_ev;  // pairs: start, end
   size_t prof_used = 0;              // events in use (2 per bracketed launch)
@@ -154,7 +176,23 @@ struct StepPlan {
   long long blocks_dec = 0;  // sum over decode rows of pages read
   double ctx_dec = 0.0;      // sum over decode rows of keys read
   bool split = false;        // decode rows via row list + prefill tiles
+  // decode attention launch shape
+  int part = 1;              // pages per split-K partition
+  int max_ctx_launch = 0;    // grid sized for contexts up to this (>= max_ctx_dec)
+  // step description: pinned host staging -> device, one copy
+  //   [hdr][row S][ntok S][start S][tok T][drow dc][didx dc][dblk dc][dec n_dec][tiles 4 n_tiles]
+  const int32_t *h_desc = nullptr;
+  int32_t *d_desc = nullptr;
+  size_t desc_elems = 0;
+  int hdr = 0;               // leading words; with graph, word 0 = the delta count
+  int delta_cap = 0;         // dc: capacity of the delta arrays
+  bool graph = false;        // fixed layout read by a replayed graph
 };
+// Elements of the fixed graph staging for batches up to max_seqs.
+inline size_t graph_in_elems(int max_seqs) { return 4 + size_t(7) * max_seqs; }
+// Split-K partition size of the decode attention for a step (the same for the
+// eager and the graph path, so both produce identical results).
+int decode_partition(const Engine *eng, const StepPlan &plan, int max_ctx);
 int enqueue_forward(Engine *eng, const StepPlan &plan);
 int step_wait_impl(Engine *eng, uint32_t *out_tokens, uint8_t *out_flags);
 

@@ -53,17 +53,26 @@ cudaError_t prof_mark(Engine *eng) {
 }
 }  // namespace
 
+int decode_partition(const Engine *eng, const StepPlan &plan, int max_ctx) {
+  if (plan.n_dec <= 0) return 1;
+  int part = choose_partition_blocks(plan.n_dec, eng->hkv, max_ctx, plan.blocks_dec);
+  while (attention_workspace_bytes(plan.n_dec, eng->hq, max_ctx, part) > int64_t(eng->attn_ws_bytes)) part *= 2;
+  return part;
+}
+
 int enqueue_forward(Engine *eng, const StepPlan &plan) {
-  const int S = plan.S, T = plan.T, nd = plan.nd;
+  const int S = plan.S, T = plan.T, dc = plan.delta_cap;
   cudaStream_t st = eng->stream;
   const int dt = eng->dtype;
   const float eps = float(eng->cfg.rms_norm_eps);
   const size_t es = eng->esize;
 
+  // the step description, then a clean status word
+  MS_CUDA_TRY(cudaMemcpyAsync(plan.d_desc, plan.h_desc, plan.desc_elems * 4, cudaMemcpyHostToDevice, st));
   MS_CUDA_TRY(cudaMemsetAsync(eng->d_status, 0, sizeof(unsigned), st));
 
   // ---- K1: pack ----
-  int32_t *d = eng->d_in;
+  int32_t *d = plan.d_desc + plan.hdr;
   PackArgs pa{};
   pa.seq_row = d;
   pa.seq_ntok = d + S;
@@ -71,9 +80,10 @@ int enqueue_forward(Engine *eng, const StepPlan &plan) {
   pa.num_seqs = S;
   pa.tokens = d + 3 * S;
   pa.delta_row = pa.tokens + T;
-  pa.delta_idx = pa.delta_row + nd;
-  pa.delta_block = pa.delta_idx + nd;
-  pa.num_deltas = nd;
+  pa.delta_idx = pa.delta_row + dc;
+  pa.delta_block = pa.delta_idx + dc;
+  pa.num_deltas = dc;
+  pa.num_deltas_dev = plan.graph ? plan.d_desc : nullptr;
   pa.block_tables = eng->d_block_tables;
   pa.max_blocks_per_seq = eng->opts.max_blocks_per_seq;
   pa.block_size = eng->opts.block_size;
@@ -90,15 +100,9 @@ int enqueue_forward(Engine *eng, const StepPlan &plan) {
   MS_CUDA_TRY(launch_pack(pa, st));
   const int32_t *tokens = pa.tokens;
 
-  const int32_t *dec_rows = plan.split ? pa.delta_block + nd : nullptr;
-  const int32_t *tiles = plan.split ? pa.delta_block + nd + plan.n_dec : nullptr;
-  // decode attention partitioning: enough CTAs to fill the GPU, workspace bounded
-  int part = 1;
-  if (plan.n_dec > 0) {
-    part = choose_partition_blocks(plan.n_dec, eng->hkv, plan.max_ctx_dec, plan.blocks_dec);
-    while (attention_workspace_bytes(plan.n_dec, eng->hq, plan.max_ctx_dec, part) > int64_t(eng->attn_ws_bytes))
-      part *= 2;
-  }
+  const int32_t *dec_rows = plan.split ? pa.delta_block + dc : nullptr;
+  const int32_t *tiles = plan.split ? pa.delta_block + dc + plan.n_dec : nullptr;
+  const int part = plan.part;
   const int64_t pool_tiles = eng->opts.pool_blocks * eng->hkv;
 
   // ---- layer 0 input: embedding gather + input norm (K4 without residual) ----
@@ -126,7 +130,7 @@ int enqueue_forward(Engine *eng, const StepPlan &plan) {
       a.row_ctx = eng->d_row_ctx;
       a.row_index = dec_rows;
       a.num_rows = plan.n_dec;
-      a.max_ctx = plan.max_ctx_dec;
+      a.max_ctx = plan.max_ctx_launch;
       a.out = eng->attn;
       a.num_heads = eng->hq;
       a.num_kv_heads = eng->hkv;
@@ -199,14 +203,14 @@ int enqueue_forward(Engine *eng, const StepPlan &plan) {
   MS_BLAS_TRY(linear(eng, eng->lm_head, eng->last_norm, eng->logits, eng->V, S, eng->H, true));
   MS_CUDA_TRY(launch_argmax(eng->logits, S, eng->V, eng->d_next, pa.seq_row, eng->d_slot_last, st));
   {
-    const int max_blk = (plan.max_ctx_dec + 15) / 16;
+    const int max_blk = (plan.max_ctx_launch + 15) / 16;
     const int parts = plan.n_dec > 0 ? (max_blk + part - 1) / part : 0;
     const int attn_launches = (plan.n_dec > 0 ? 1 + (parts > 1 ? 1 : 0) : 0) + (plan.n_tiles > 0 ? 1 : 0);
-    eng->kernel_launches += 3 + int64_t(eng->L) * (4 + attn_launches);
+    eng->last_launches = 3 + int64_t(eng->L) * (4 + attn_launches);
+    eng->kernel_launches += eng->last_launches;
   }
   MS_CUDA_TRY(cudaMemcpyAsync(eng->h_next, eng->d_next, size_t(S) * 4, cudaMemcpyDeviceToHost, st));
   MS_CUDA_TRY(cudaMemcpyAsync(eng->h_status, eng->d_status, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
-  MS_CUDA_TRY(cudaEventRecord(eng->done_ev, st));
   return MS_OK;
 }
 

@@ -167,13 +167,75 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
     sp.ctx_dec = total_ctx;
   }
 
+  // ---- decode attention launch shape ----
+  sp.part = decode_partition(eng, sp, sp.max_ctx_dec);
+  sp.max_ctx_launch = sp.max_ctx_dec;
+
+  // ---- replay a captured graph for pure-decode steps ----
+  // Eligible: one token per sequence (so the decode rows are the packed rows
+  // and there are no prefill tiles), at most S block-table deltas, no
+  // collectives, no per-launch profiling events.
+  const bool graph_ok = eng->graphs_enabled && eng->tp == 1 && !eng->profiling && T == S && nd <= S &&
+                        (!sp.split || (sp.n_dec == S && sp.n_tiles == 0));
+  Engine::StepGraph *g = nullptr;
+  bool capture = false;
+  if (graph_ok) {
+    for (auto &c : eng->graphs)
+      if (c.S == S && c.part == sp.part && c.max_ctx_cap >= sp.max_ctx_dec) g = &c;
+    if (!g) {
+      // first step of a (batch, partition) key runs eagerly (one-time launch
+      // attributes, library heuristics); the next one is captured
+      int &warm = eng->graph_warm[int64_t(S) << 32 | uint32_t(sp.part)];
+      if (warm++ > 0) {
+        const int max_blk = (sp.max_ctx_dec + 15) / 16;
+        const int cap_ctx = ((max_blk + sp.part - 1) / sp.part + 1) * sp.part * 16;  // one spare partition
+        if (attention_workspace_bytes(S, eng->hq, cap_ctx, sp.part) <= int64_t(eng->attn_ws_bytes)) {
+          capture = true;
+          if (eng->graphs.size() >= 16) {  // evict the least recently used
+            auto lru = std::min_element(eng->graphs.begin(), eng->graphs.end(),
+                                        [](const Engine::StepGraph &x, const Engine::StepGraph &y) {
+                                          return x.last_use < y.last_use;
+                                        });
+            cudaGraphExecDestroy(lru->exec);
+            eng->graphs.erase(lru);
+          }
+          eng->graphs.emplace_back();
+          g = &eng->graphs.back();
+          g->S = S;
+          g->part = sp.part;
+          g->max_ctx_cap = cap_ctx;
+        }
+      }
+    }
+  }
+
   // ---- stage the step description: one pinned buffer, one upload ----
-  const size_t need = size_t(3) * S + T + size_t(3) * nd + (sp.split ? size_t(sp.n_dec) + 4 * size_t(sp.n_tiles) : 0);
-  int rc = grow_staging(eng, need);
-  if (rc != MS_OK) return rc;
-  int32_t *h = eng->h_in;
+  int32_t *h;
+  if (g) {
+    sp.graph = true;
+    sp.hdr = 4;
+    sp.delta_cap = S;
+    sp.max_ctx_launch = g->max_ctx_cap;
+    sp.h_desc = eng->h_gin;
+    sp.d_desc = eng->d_gin;
+    sp.desc_elems = 4 + size_t(7) * S;
+    h = eng->h_gin;
+    h[0] = nd;
+    h[1] = h[2] = h[3] = 0;
+    h += 4;
+  } else {
+    sp.delta_cap = nd;
+    const size_t need = size_t(3) * S + T + size_t(3) * nd + (sp.split ? size_t(sp.n_dec) + 4 * size_t(sp.n_tiles) : 0);
+    int rc = grow_staging(eng, need);
+    if (rc != MS_OK) return rc;
+    sp.h_desc = eng->h_in;
+    sp.d_desc = eng->d_in;
+    sp.desc_elems = need;
+    h = eng->h_in;
+  }
+  const int dc = sp.delta_cap;
   int32_t *h_row = h, *h_ntok = h + S, *h_start = h + 2 * S, *h_tok = h + 3 * S;
-  int32_t *h_drow = h_tok + T, *h_didx = h_drow + nd, *h_dblk = h_didx + nd;
+  int32_t *h_drow = h_tok + T, *h_didx = h_drow + dc, *h_dblk = h_didx + dc;
   int t = 0, d = 0;
   for (int i = 0; i < S; ++i) {
     const RowPlan &r = plan[i];
@@ -192,15 +254,43 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
       h_dblk[d] = s.blocks[b];
     }
   }
-  if (sp.split) {
-    int32_t *h_dec = h_dblk + nd;
+  if (sp.split && !sp.graph) {
+    int32_t *h_dec = h_dblk + dc;
     std::copy(dec_rows.begin(), dec_rows.end(), h_dec);
     std::copy(tiles.begin(), tiles.begin() + 4 * size_t(sp.n_tiles), h_dec + sp.n_dec);
   }
+  if (sp.graph) sp.split = false;  // decode rows are the packed rows: identity row list
   MS_CUDA_TRY(cudaSetDevice(eng->dev));
-  MS_CUDA_TRY(cudaMemcpyAsync(eng->d_in, eng->h_in, need * 4, cudaMemcpyHostToDevice, eng->stream));
-  rc = enqueue_forward(eng, sp);
-  if (rc != MS_OK) return rc;
+  if (g && !capture) {
+    MS_CUDA_TRY(cudaGraphLaunch(g->exec, eng->stream));
+    eng->kernel_launches += g->launches;
+    ++eng->graph_replays;
+  } else if (capture) {
+    MS_CUDA_TRY(cudaStreamBeginCapture(eng->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_forward(eng, sp);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(eng->stream, &graph);
+    if (rc != MS_OK) {
+      if (graph) cudaGraphDestroy(graph);
+      eng->graphs.pop_back();
+      return rc;
+    }
+    cudaError_t ie = ce;
+    if (ie == cudaSuccess) ie = cudaGraphInstantiate(&g->exec, graph, 0);
+    if (graph) cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) {
+      eng->graphs.pop_back();
+      return eng->fail(MS_E_DEVICE, std::string("graph capture: ") + cudaGetErrorString(ie));
+    }
+    g->launches = eng->last_launches;
+    ++eng->graph_captures;
+    MS_CUDA_TRY(cudaGraphLaunch(g->exec, eng->stream));
+  } else {
+    int rc = enqueue_forward(eng, sp);
+    if (rc != MS_OK) return rc;
+  }
+  if (g) g->last_use = ++eng->graph_clock;
+  MS_CUDA_TRY(cudaEventRecord(eng->done_ev, eng->stream));
 
   // ---- commit host state ----
   eng->last_slots.resize(S);

@@ -116,7 +116,8 @@ struct PackArgs {
   const int32_t *delta_row;
   const int32_t *delta_idx;
   const int32_t *delta_block;
-  int num_deltas;
+  int num_deltas;                  // capacity of the delta arrays
+  const int32_t *num_deltas_dev;   // when set, the delta count is read here (<= num_deltas)
   int32_t *block_tables;  // [rows][max_blocks_per_seq]
   int max_blocks_per_seq;
   int block_size;

@@ -54,8 +54,9 @@ __global__ void __launch_bounds__(kThreads) pack_kernel(PackArgs a) {
   __shared__ int warp_tot[33];
   const int tid = threadIdx.x;
 
-  // 1. block-table deltas
-  for (int i = tid; i < a.num_deltas; i += kThreads) {
+  // 1. block-table deltas (count from device memory when the launch is replayed from a graph)
+  const int nd = a.num_deltas_dev ? min(*a.num_deltas_dev, a.num_deltas) : a.num_deltas;
+  for (int i = tid; i < nd; i += kThreads) {
     const int row = a.delta_row[i], idx = a.delta_idx[i], blk = a.delta_block[i];
     const bool ok = row >= 0 && idx >= 0 && idx < a.max_blocks_per_seq && blk >= 0 &&
                     (a.pool_blocks <= 0 || blk < a.pool_blocks);

@@ -61,6 +61,8 @@ _SIGS = {
     "ms_engine_set_profiling": ([_P, _I32], C.c_int),
     "ms_engine_profile": ([_P, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(C.c_double),
                            C.POINTER(C.c_double)], C.c_int),
+    "ms_engine_set_graphs": ([_P, _I32], C.c_int),
+    "ms_engine_graph_stats": ([_P, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(_I32)], C.c_int),
     "ms_nccl_get_unique_id": ([C.c_char_p, _I32], C.c_int),
     "ms_nccl_comm_init": ([C.POINTER(_P), _I32, C.c_char_p, _I32, _I32], C.c_int),
     "ms_nccl_comm_destroy": ([_P], C.c_int),
@@ -304,6 +306,16 @@ class Engine:
         self._check(self.lib.ms_engine_profile(self.h, C.byref(kl), C.byref(al), C.byref(ms), C.byref(by)),
                     "profile")
         return kl.value, al.value, ms.value, by.value
+
+    def set_graphs(self, on: bool):
+        """Replay pure-decode steps from captured CUDA graphs (default on)."""
+        self._check(self.lib.ms_engine_set_graphs(self.h, 1 if on else 0), "set_graphs")
+
+    def graph_stats(self):
+        """(graphs captured, steps replayed, graphs cached)."""
+        c, r, n = C.c_int64(), C.c_int64(), _I32()
+        self._check(self.lib.ms_engine_graph_stats(self.h, C.byref(c), C.byref(r), C.byref(n)), "graph_stats")
+        return c.value, r.value, n.value
 
     # -- health
     def is_healthy(self) -> bool:
