@@ -106,6 +106,102 @@ template <> struct Vec2<__half> {
   }
 };
 
+// ---- 16 bytes of T kept as raw bits (one vector load / store) ----------------
+// Values that are already representable in T (sums rounded to the model dtype)
+// stay packed in registers at half the cost of f32 copies for 16-bit T.
+template <typename T> struct Raw16;
+template <> struct Raw16<float> {
+  static constexpr int N = 4;
+  static __device__ __forceinline__ void unpack(const uint4 &v, float (&o)[4]) {
+    o[0] = __uint_as_float(v.x); o[1] = __uint_as_float(v.y);
+    o[2] = __uint_as_float(v.z); o[3] = __uint_as_float(v.w);
+  }
+  static __device__ __forceinline__ uint4 pack(const float (&o)[4]) {
+    return make_uint4(__float_as_uint(o[0]), __float_as_uint(o[1]), __float_as_uint(o[2]), __float_as_uint(o[3]));
+  }
+};
+template <> struct Raw16<__nv_bfloat16> {
+  static constexpr int N = 8;
+  static __device__ __forceinline__ void unpack(const uint4 &v, float (&o)[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      o[2 * k] = __uint_as_float(w[k] << 16);
+      o[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+    }
+  }
+  static __device__ __forceinline__ uint4 pack(const float (&o)[8]) {
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(o[2 * k], o[2 * k + 1]);
+      w[k] = *reinterpret_cast<uint32_t *>(&h);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+};
+template <> struct Raw16<__half> {
+  static constexpr int N = 8;
+  static __device__ __forceinline__ void unpack(const uint4 &v, float (&o)[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[k]));
+      o[2 * k] = f.x;
+      o[2 * k + 1] = f.y;
+    }
+  }
+  static __device__ __forceinline__ uint4 pack(const float (&o)[8]) {
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      __half2 h = __floats2half2_rn(o[2 * k], o[2 * k + 1]);
+      w[k] = *reinterpret_cast<uint32_t *>(&h);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+};
+
+__device__ __forceinline__ bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// ---- x / n for many x and one n ----------------------------------------------
+// Markstein's correction (P. Markstein, "Computation of elementary functions
+// on the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990): with
+// r = RN(1/n) and q0 = RN(x * r), the residual e = x - n * q0 is exact in one
+// FMA and RN(q0 + e * r) is the correctly rounded quotient RN(x / n) for
+// normal operands.  Callers compute r = 1.0f / n once (an IEEE division) and
+// pay two FMAs and a multiply per element instead of a full division.
+__device__ __forceinline__ float div_by(float x, float n, float r) {
+  const float q0 = x * r;
+  const float e = fmaf(-q0, n, x);
+  return fmaf(e, r, q0);
+}
+
+// ---- packed bf16x2 arithmetic on raw 32-bit words ----------------------------
+// For bf16 operands a product is exact in f32 and a sum is either exact in f32
+// or differs from the larger operand by far less than half a bf16 ulp, so
+// round_to<bf16>(float(a) op float(b)) equals the correctly rounded bf16x2
+// result of the hardware instruction: one instruction per two values and no
+// f32 -> bf16 conversion.
+__device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hmul2(*reinterpret_cast<const __nv_bfloat162 *>(&a), *reinterpret_cast<const __nv_bfloat162 *>(&b));
+  return *reinterpret_cast<uint32_t *>(&r);
+}
+__device__ __forceinline__ uint32_t bf2_add(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hadd2(*reinterpret_cast<const __nv_bfloat162 *>(&a), *reinterpret_cast<const __nv_bfloat162 *>(&b));
+  return *reinterpret_cast<uint32_t *>(&r);
+}
+__device__ __forceinline__ uint32_t bf2_pack(float lo, float hi) {
+  __nv_bfloat162 r = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&r);
+}
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ uint32_t u4_get(const uint4 &v, int k) { return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w; }
+__device__ __forceinline__ void u4_set(uint4 &v, int k, uint32_t w) {
+  if (k == 0) v.x = w; else if (k == 1) v.y = w; else if (k == 2) v.z = w; else v.w = w;
+}
+
 // ---- warp reductions ---------------------------------------------------------
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

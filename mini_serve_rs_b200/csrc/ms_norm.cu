@@ -6,11 +6,15 @@
 // variance is taken in f32 from the rounded sum, the row is divided by
 // sqrt(var + eps), rounded, then multiplied by the weight and rounded again.
 // One CTA per row, 16-byte vector loads, warp-shuffle + shared-memory reduce.
+#include <type_traits>
+
 #include "ms_common.cuh"
 #include "ms_internal.h"
 
 namespace ms {
 namespace {
+
+inline bool host_aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 template <typename T> struct V16;  // 16 bytes of T
 template <> struct V16<float> {
@@ -83,6 +87,116 @@ __global__ void add_rmsnorm_kernel(const T *__restrict__ x, const T *__restrict_
     for (int i = 0; i < N; ++i) y[i] = round_to<T>(round_to<T>(s[i] / norm) * ww[i]);
     V16<T>::store(norm_out + size_t(row) * hidden + c * N, y);
   }
+}
+
+// Warp-per-row K4 (the path for 16-byte aligned rows of up to 8 x 32 chunks,
+// i.e. hidden <= 2048 in 16-bit types; wider rows use add_rmsnorm_kernel):
+// a warp issues every load of its row at once (x, r: CPL 16-byte chunks per
+// lane), reduces with shuffles only, and a CTA of 4 warps covers 4 rows, so a
+// config-3 batch (8192 rows of 1024) fits one wave of resident warps.  The
+// rounded sums stay packed in registers.  Same rounding points as
+// add_rmsnorm_kernel.
+template <typename T, int CPL>
+__global__ void __launch_bounds__(128) add_rmsnorm_warp_kernel(const T *__restrict__ x, const T *__restrict__ r,
+                                                               const int32_t *__restrict__ row_index,
+                                                               const T *__restrict__ w, T *__restrict__ resid_out,
+                                                               T *__restrict__ norm_out, int rows, int hidden,
+                                                               float eps) {
+  using R = Raw16<T>;
+  constexpr int N = R::N;
+  const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (row >= rows) return;  // warp-uniform
+  const int lane = threadIdx.x & 31;
+  const int chunks = hidden / N;
+  const size_t src = row_index ? size_t(row_index[row]) : size_t(row);
+  const uint4 *xr = reinterpret_cast<const uint4 *>(x + src * hidden);
+  const uint4 *rr = r ? reinterpret_cast<const uint4 *>(r + src * hidden) : nullptr;
+  uint4 sv[CPL], rv[CPL];
+#pragma unroll
+  for (int k = 0; k < CPL; ++k) {
+    const int c = lane + 32 * k;
+    if (c < chunks) {
+      sv[k] = __ldg(xr + c);
+      if (rr) rv[k] = __ldg(rr + c);
+    }
+  }
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  float sq = 0.f;
+#pragma unroll
+  for (int k = 0; k < CPL; ++k) {
+    const int c = lane + 32 * k;
+    if (c < chunks) {
+      if constexpr (kBf16) {  // packed adds, exact f32 squares in element order
+        if (rr)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) u4_set(sv[k], j, bf2_add(u4_get(sv[k], j), u4_get(rv[k], j)));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t v = u4_get(sv[k], j);
+          sq = fmaf(bf_lo(v), bf_lo(v), sq);
+          sq = fmaf(bf_hi(v), bf_hi(v), sq);
+        }
+      } else {
+        float s[N];
+        R::unpack(sv[k], s);
+        if (rr) {
+          float b[N];
+          R::unpack(rv[k], b);
+#pragma unroll
+          for (int i = 0; i < N; ++i) s[i] = round_to<T>(s[i] + b[i]);
+          sv[k] = R::pack(s);
+        }
+#pragma unroll
+        for (int i = 0; i < N; ++i) sq = fmaf(s[i], s[i], sq);
+      }
+      if (resid_out) reinterpret_cast<uint4 *>(resid_out + size_t(row) * hidden)[c] = sv[k];
+    }
+  }
+  sq = warp_sum(sq);
+  const float norm = sqrtf(sq / float(hidden) + eps);
+  const float rn = 1.0f / norm;
+  const uint4 *wr = reinterpret_cast<const uint4 *>(w);
+  uint4 *out = reinterpret_cast<uint4 *>(norm_out + size_t(row) * hidden);
+#pragma unroll
+  for (int k = 0; k < CPL; ++k) {
+    const int c = lane + 32 * k;
+    if (c < chunks) {
+      const uint4 wv = __ldg(wr + c);
+      if constexpr (kBf16) {
+        uint4 y;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t v = u4_get(sv[k], j);
+          u4_set(y, j, bf2_mul(bf2_pack(div_by(bf_lo(v), norm, rn), div_by(bf_hi(v), norm, rn)), u4_get(wv, j)));
+        }
+        out[c] = y;
+      } else {
+        float s[N], ww[N], y[N];
+        R::unpack(sv[k], s);
+        R::unpack(wv, ww);
+#pragma unroll
+        for (int i = 0; i < N; ++i) y[i] = round_to<T>(round_to<T>(s[i] / norm) * ww[i]);
+        out[c] = R::pack(y);
+      }
+    }
+  }
+}
+
+template <typename T>
+cudaError_t launch_add_rmsnorm_warp(const void *x, const void *r, const int32_t *row_index, const void *w,
+                                    void *resid_out, void *norm_out, int rows, int hidden, float eps,
+                                    cudaStream_t st) {
+  const int per_lane = (hidden / Raw16<T>::N + 31) / 32;
+  const dim3 grid((rows + 3) / 4);
+  auto go = [&](auto kern) {
+    kern<<<grid, 128, 0, st>>>((const T *)x, (const T *)r, row_index, (const T *)w, (T *)resid_out, (T *)norm_out,
+                               rows, hidden, eps);
+    return cudaGetLastError();
+  };
+  if (per_lane <= 1) return go(add_rmsnorm_warp_kernel<T, 1>);
+  if (per_lane <= 2) return go(add_rmsnorm_warp_kernel<T, 2>);
+  if (per_lane <= 4) return go(add_rmsnorm_warp_kernel<T, 4>);
+  return go(add_rmsnorm_warp_kernel<T, 8>);
 }
 
 // act = silu(gate).to(dtype) * up, gate_up = [gate | up] per row (qwen2.rs:169-174).
@@ -185,6 +299,17 @@ cudaError_t launch_add_rmsnorm(const void *x, const void *r, const int32_t *row_
   if (rows < 0 || hidden <= 0) return cudaErrorInvalidValue;
   const int n = dtype == MS_DTYPE_F32 ? 4 : 8;
   if (hidden % n != 0 || hidden / n > 1024) return cudaErrorInvalidValue;
+  const bool vec16 = (hidden * (dtype == MS_DTYPE_F32 ? 4 : 2)) % 16 == 0 && hidden / n <= 8 * 32 && host_aligned16(x) &&
+                     (!r || host_aligned16(r)) && host_aligned16(w) && (!resid_out || host_aligned16(resid_out)) &&
+                     host_aligned16(norm_out);
+  if (vec16) {
+    switch (dtype) {
+      case MS_DTYPE_F32: return launch_add_rmsnorm_warp<float>(x, r, row_index, w, resid_out, norm_out, rows, hidden, eps, st);
+      case MS_DTYPE_BF16: return launch_add_rmsnorm_warp<__nv_bfloat16>(x, r, row_index, w, resid_out, norm_out, rows, hidden, eps, st);
+      case MS_DTYPE_F16: return launch_add_rmsnorm_warp<__half>(x, r, row_index, w, resid_out, norm_out, rows, hidden, eps, st);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   const int threads = ((hidden / n + 31) / 32) * 32;
   switch (dtype) {
     case MS_DTYPE_F32:

@@ -10,8 +10,13 @@
 // by slot_mapping), the rotated q into a dense [T, Hq, D] buffer for K3.
 // Every product and sum is rounded to the model dtype where Candle rounds.
 //
-// One warp per (token, head); lane l holds dims [l*D/32, (l+1)*D/32), so the
-// rotate-half partner of each dim sits in lane l ^ 16.
+// Two builds: qk_norm_rope_append_vec_kernel (16-byte aligned operands, the
+// engine's case) moves 16-byte vectors, several per thread; the general
+// qk_norm_rope_append_kernel runs one warp per (token, head), lane l holding
+// dims [l*D/32, (l+1)*D/32), so the rotate-half partner of each dim sits in
+// lane l ^ 16.
+#include <type_traits>
+
 #include "ms_common.cuh"
 #include "ms_internal.h"
 
@@ -103,11 +108,187 @@ __global__ void qk_norm_rope_append_kernel(const T *__restrict__ qkv, const T *_
   }
 }
 
+// Vectorised K5 (16-byte aligned operands, power-of-two page size): one CTA
+// per token.  An item is 16 bytes (N values) of one head; TPH = D / N
+// consecutive threads hold one head, so the QK-norm sum reduces over those
+// lanes and the rotate-half partner of item c is item c ^ TPH/2.  Thread i
+// takes items i, i + 256, ... (K at most) of its token: every load is issued
+// before any math, the token's position and slot are read once, and no index
+// needs a division.  Every lane runs the shuffles (V heads and the items past
+// the token's end compute and discard), so the warp never splits around them.
+// Rounding points as in qk_norm_rope_append_kernel; for bf16 each rounded add
+// and product is one packed bf16x2 instruction (equal to the f32-then-round
+// form) and x / norm uses one reciprocal per head.
+template <typename T, int D, int K>
+__global__ void __launch_bounds__(256) qk_norm_rope_append_vec_kernel(
+    const T *__restrict__ qkv, const T *__restrict__ bias, const T *__restrict__ qn, const T *__restrict__ kn,
+    const T *__restrict__ cos_t, const T *__restrict__ sin_t, const int32_t *__restrict__ positions,
+    const int64_t *__restrict__ slot_mapping, T *__restrict__ q_out, T *__restrict__ k_pool,
+    T *__restrict__ v_pool, int hq, int hkv, int bs_shift, float eps) {
+  using R = Raw16<T>;
+  constexpr int N = R::N;
+  constexpr int TPH = D / N;
+  constexpr int HALF = D / 2;
+  constexpr int HPP = 256 / TPH;  // heads per pass of the CTA
+  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  const int heads = hq + 2 * hkv;
+  const int t = blockIdx.x;
+  const int c = threadIdx.x % TPH;
+  const int d0 = c * N;
+  const int h0 = threadIdx.x / TPH;
+
+  const uint4 *src = reinterpret_cast<const uint4 *>(qkv + size_t(t) * heads * D);
+  uint4 xv[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int h = h0 + k * HPP;
+    xv[k] = h < heads ? __ldg(src + h * TPH + c) : make_uint4(0, 0, 0, 0);
+  }
+  const int pos = __ldg(positions + t);
+  const int64_t slot = __ldg(slot_mapping + t);
+  const int64_t blk = slot >> bs_shift;
+  const int off = int(slot & ((int64_t(1) << bs_shift) - 1));
+  const size_t tab = size_t(pos) * HALF + (d0 % HALF);
+  const uint4 cs = __ldg(reinterpret_cast<const uint4 *>(cos_t + tab));
+  const uint4 sn = __ldg(reinterpret_cast<const uint4 *>(sin_t + tab));
+  const bool lower = c < TPH / 2;  // lower half rotates in -x2
+
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int h = h0 + k * HPP;
+    const bool ok = h < heads;
+    const int hc = ok ? h : 0;
+    const bool is_v = hc >= hq + hkv;
+    const bool is_q = hc < hq;
+    const T *nw = is_v ? nullptr : (is_q ? qn : kn);
+    uint4 out;  // what this item stores
+    if constexpr (kBf16) {
+      uint4 x = xv[k];
+      if (bias) {
+        const uint4 b = __ldg(reinterpret_cast<const uint4 *>(bias + size_t(hc) * D + d0));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) u4_set(x, j, bf2_add(u4_get(x, j), u4_get(b, j)));
+      }
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t v = u4_get(x, j);
+        ss = fmaf(bf_lo(v), bf_lo(v), ss);
+        ss = fmaf(bf_hi(v), bf_hi(v), ss);
+      }
+#pragma unroll
+      for (int o = TPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
+      uint4 y = x;
+      if (nw) {
+        const float norm = sqrtf(ss / float(D) + eps);
+        const float rn = 1.0f / norm;
+        const uint4 w = __ldg(reinterpret_cast<const uint4 *>(nw + d0));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t v = u4_get(x, j);
+          u4_set(y, j, bf2_mul(bf2_pack(div_by(bf_lo(v), norm, rn), div_by(bf_hi(v), norm, rn)), u4_get(w, j)));
+        }
+      }
+      uint4 pv;
+      pv.x = __shfl_xor_sync(kFull, y.x, TPH / 2);
+      pv.y = __shfl_xor_sync(kFull, y.y, TPH / 2);
+      pv.z = __shfl_xor_sync(kFull, y.z, TPH / 2);
+      pv.w = __shfl_xor_sync(kFull, y.w, TPH / 2);
+      const uint32_t neg = lower ? 0x80008000u : 0u;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        u4_set(out, j, bf2_add(bf2_mul(u4_get(y, j), u4_get(cs, j)), bf2_mul(u4_get(pv, j) ^ neg, u4_get(sn, j))));
+      if (is_v) out = x;
+    } else {
+      float x[N];
+      R::unpack(xv[k], x);
+      if (bias) {
+        float b[N];
+        R::unpack(__ldg(reinterpret_cast<const uint4 *>(bias + size_t(hc) * D + d0)), b);
+#pragma unroll
+        for (int i = 0; i < N; ++i) x[i] = round_to<T>(x[i] + b[i]);
+      }
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < N; ++i) ss = fmaf(x[i], x[i], ss);
+#pragma unroll
+      for (int o = TPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
+      float y[N];
+      if (nw) {
+        const float norm = sqrtf(ss / float(D) + eps);
+        float w[N];
+        R::unpack(__ldg(reinterpret_cast<const uint4 *>(nw + d0)), w);
+#pragma unroll
+        for (int i = 0; i < N; ++i) y[i] = round_to<T>(round_to<T>(x[i] / norm) * w[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < N; ++i) y[i] = x[i];
+      }
+      const uint4 yv = R::pack(y);
+      uint4 pv;
+      pv.x = __shfl_xor_sync(kFull, yv.x, TPH / 2);
+      pv.y = __shfl_xor_sync(kFull, yv.y, TPH / 2);
+      pv.z = __shfl_xor_sync(kFull, yv.z, TPH / 2);
+      pv.w = __shfl_xor_sync(kFull, yv.w, TPH / 2);
+      float partner[N], cf[N], sf[N], o[N];
+      R::unpack(pv, partner);
+      R::unpack(cs, cf);
+      R::unpack(sn, sf);
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const float rot = lower ? -partner[i] : partner[i];
+        const float a = round_to<T>(y[i] * cf[i]);
+        const float b = round_to<T>(rot * sf[i]);
+        o[i] = round_to<T>(a + b);
+      }
+      out = is_v ? R::pack(x) : R::pack(o);
+    }
+    if (!ok) continue;
+    T *dst;
+    if (is_q) dst = q_out + (size_t(t) * hq + hc) * D + d0;
+    else if (is_v) dst = v_pool + ((size_t(blk) * hkv + (hc - hq - hkv)) * (size_t(1) << bs_shift) + off) * D + d0;
+    else dst = k_pool + ((size_t(blk) * hkv + (hc - hq)) * (size_t(1) << bs_shift) + off) * D + d0;
+    *reinterpret_cast<uint4 *>(dst) = out;
+  }
+}
+
+template <typename T, int D>
+cudaError_t launch_vec(const void *qkv, const void *bias, const void *qn, const void *kn, const void *cs,
+                       const void *sn, const int32_t *positions, const int64_t *slots, void *q_out, void *k_pool,
+                       void *v_pool, int T_, int hq, int hkv, int bs_shift, float eps, cudaStream_t st) {
+  const int per_thread = ((hq + 2 * hkv) * (D / Raw16<T>::N) + 255) / 256;
+  auto go = [&](auto kern) {
+    kern<<<T_, 256, 0, st>>>((const T *)qkv, (const T *)bias, (const T *)qn, (const T *)kn, (const T *)cs,
+                             (const T *)sn, positions, slots, (T *)q_out, (T *)k_pool, (T *)v_pool, hq, hkv, bs_shift,
+                             eps);
+    return cudaGetLastError();
+  };
+  if (per_thread <= 1) return go(qk_norm_rope_append_vec_kernel<T, D, 1>);
+  if (per_thread <= 2) return go(qk_norm_rope_append_vec_kernel<T, D, 2>);
+  if (per_thread <= 4) return go(qk_norm_rope_append_vec_kernel<T, D, 4>);
+  return go(qk_norm_rope_append_vec_kernel<T, D, 8>);
+}
+
+inline bool host_aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 template <typename T>
 cudaError_t launch_typed(const void *qkv, const void *bias, const void *qn, const void *kn, const void *cs,
                          const void *sn, const int32_t *positions, const int64_t *slots, void *q_out,
                          void *k_pool, void *v_pool, int T_, int hq, int hkv, int D, int bs, float eps,
                          cudaStream_t st) {
+  int bs_shift = 0;
+  while ((1 << bs_shift) < bs) ++bs_shift;
+  const bool vec = (D == 128 || D == 64) && (1 << bs_shift) == bs && (hq + 2 * hkv) * (D * int(sizeof(T)) / 16) <= 8 * 256 &&
+                   host_aligned16(qkv) && (!bias || host_aligned16(bias)) &&
+                   (!qn || host_aligned16(qn)) && (!kn || host_aligned16(kn)) && host_aligned16(cs) &&
+                   host_aligned16(sn) && host_aligned16(q_out) && host_aligned16(k_pool) && host_aligned16(v_pool);
+  if (vec) {
+    if (D == 128)
+      return launch_vec<T, 128>(qkv, bias, qn, kn, cs, sn, positions, slots, q_out, k_pool, v_pool, T_, hq, hkv,
+                                bs_shift, eps, st);
+    return launch_vec<T, 64>(qkv, bias, qn, kn, cs, sn, positions, slots, q_out, k_pool, v_pool, T_, hq, hkv,
+                             bs_shift, eps, st);
+  }
   const long long warps = (long long)T_ * (hq + 2 * hkv);
   const int threads = 256;
   const long long blocks = (warps * 32 + threads - 1) / threads;
