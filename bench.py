@@ -48,7 +48,7 @@ def parse():
     ap.add_argument("--config5", action="store_true",
                     help="BASELINE config 5: Qwen2.5-7B arch, 256 seqs x ctx U[1024,32768], tensor parallel")
     ap.add_argument("--tp", type=int, default=2, help="tensor-parallel size for --config5")
-    ap.add_argument("--kernel", choices=["attention", "norm_rope"], default=None,
+    ap.add_argument("--kernel", choices=["attention", "norm_rope", "sample"], default=None,
                     help="time one kernel in isolation (BASELINE config 2 for attention) instead of the step")
     return ap.parse_args()
 
@@ -519,6 +519,51 @@ def run_norm_rope_kernels(args, local):
                       "peak_gbs": peak, "peak_source": kind}), flush=True)
 
 
+def run_sample_kernel(args, local):
+    """K6b on-device sampling for a decode batch: 256 rows of f32 logits over
+    the Qwen3 vocabulary (151936), temperature 0.8, with top-p 0.9 (race pass
+    + nucleus checks) and without (one race pass).  Median of K CUDA-event
+    intervals of one launch each; the argmax kernel over the same rows for
+    scale."""
+    import ctypes as C
+    import torch
+    from mini_serve_rs_b200 import engine as E
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    lib = E.lib()
+    rows, V = 256, 151936
+    g = torch.Generator(device=dev).manual_seed(5)
+    lg = torch.randn(rows, V, generator=g, device=dev) * 3
+    t = torch.full((rows,), 0.8, device=dev)
+    p9 = torch.full((rows,), 0.9, device=dev)
+    sd = torch.arange(rows, device=dev, dtype=torch.int64)
+    out = torch.zeros(rows, dtype=torch.int32, device=dev)
+    st = torch.cuda.current_stream()
+    ptr = lambda x: C.c_void_p(x.data_ptr())
+    sp = C.c_void_p(st.cuda_stream)
+
+    def timed(fn):
+        for _ in range(args.warmup):
+            fn()
+        ts = []
+        for _ in range(args.steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            fn()
+            e1.record(st)
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        ts.sort()
+        return ts[len(ts) // 2]
+
+    topp = timed(lambda: lib.ms_launch_sample(ptr(lg), rows, V, ptr(t), ptr(p9), ptr(sd), ptr(out), sp))
+    plain = timed(lambda: lib.ms_launch_sample(ptr(lg), rows, V, ptr(t), None, ptr(sd), ptr(out), sp))
+    amax = timed(lambda: lib.ms_launch_argmax(ptr(lg), rows, V, ptr(out), sp))
+    print(json.dumps({"workload": "256 rows x 151936 f32 logits (Qwen3 vocabulary), temperature 0.8",
+                      "logits_bytes": rows * V * 4, "ms_top_p_0.9": topp, "ms_temperature_only": plain,
+                      "ms_argmax": amax}), flush=True)
+
+
 def traffic_per_launch(algorithmic_bytes: float):
     """dram bytes (read + write) per attention launch: the committed ncu ratio of
     dram bytes to algorithmic bytes (profiles/k3_attention_traffic.json, from a
@@ -547,6 +592,9 @@ def main():
         return
     if args.kernel == "norm_rope":
         run_norm_rope_kernels(args, local)
+        return
+    if args.kernel == "sample":
+        run_sample_kernel(args, local)
         return
 
     if args.impl == "reference":

@@ -114,6 +114,15 @@ typedef struct ms_step_desc {
   const uint32_t *input_tokens; /* may be NULL with MS_STEP_TOKENS_FROM_DEVICE */
   const int32_t *positions;     /* may be NULL */
   uint32_t flags;
+  /* Sampling, per sequence (sample_token, candle.rs:737-763).  All three may
+   * be NULL: greedy argmax for every sequence.  temperature[i] < 1e-7 (or
+   * NULL) is greedy; otherwise the token is drawn from softmax(logits /
+   * temperature[i]), cut to the top-p nucleus when 0 < top_p[i] < 1 (top_p
+   * NULL: no cut), with the random stream seeded by seeds[i] (NULL: 0).
+   * Zero-initialised descriptors from older callers stay greedy. */
+  const float *temperature;
+  const float *top_p;
+  const uint64_t *seeds;
 } ms_step_desc;
 
 /* ---- engine lifetime --------------------------------------------------- */
@@ -304,6 +313,15 @@ int ms_launch_paged_prefill(const void *q, const void *k_pool, const void *v_poo
 int ms_prefill_tiles(const int32_t *seq_row0, const int32_t *seq_ntok, const int32_t *seq_start,
                      const int32_t *seq_table_row, int32_t num_seqs, int32_t num_heads,
                      int32_t num_kv_heads, int32_t *tiles_out, int32_t capacity);
+
+/* K6b on-device sampling over f32 logits [rows, vocab]: for each row with
+ * temperature[row] >= 1e-7 the token is drawn as candle-transformers'
+ * LogitsProcessor draws it (softmax of logits / temperature, top-p nucleus
+ * when 0 < top_p[row] < 1, ties at the nucleus edge kept in index order) from
+ * a counter-based stream seeded by seeds[row]; rows below 1e-7 are left as
+ * they are in out (run ms_launch_argmax first).  top_p and seeds may be NULL. */
+int ms_launch_sample(const float *logits, int32_t rows, int32_t vocab, const float *temperature,
+                     const float *top_p, const uint64_t *seeds, int32_t *out, void *stream);
 
 /* K6 glue. */
 int ms_launch_silu_mul(const void *gate_up, void *out, int32_t rows, int32_t inter,

@@ -180,16 +180,18 @@ struct StepPlan {
   int part = 1;              // pages per split-K partition
   int max_ctx_launch = 0;    // grid sized for contexts up to this (>= max_ctx_dec)
   // step description: pinned host staging -> device, one copy
-  //   [hdr][row S][ntok S][start S][tok T][drow dc][didx dc][dblk dc][dec n_dec][tiles 4 n_tiles]
+  //   [hdr][row S][ntok S][start S][tok T]([temp S][top_p S][seed_lo S][seed_hi S] when sample)
+  //   [drow dc][didx dc][dblk dc][dec n_dec][tiles 4 n_tiles]
   const int32_t *h_desc = nullptr;
   int32_t *d_desc = nullptr;
   size_t desc_elems = 0;
   int hdr = 0;               // leading words; with graph, word 0 = the delta count
   int delta_cap = 0;         // dc: capacity of the delta arrays
   bool graph = false;        // fixed layout read by a replayed graph
+  bool sample = false;       // per-row sampling parameters staged, sampling kernel launched
 };
 // Elements of the fixed graph staging for batches up to max_seqs.
-inline size_t graph_in_elems(int max_seqs) { return 4 + size_t(7) * max_seqs; }
+inline size_t graph_in_elems(int max_seqs) { return 4 + size_t(11) * max_seqs; }
 // Split-K partition size of the decode attention for a step (the same for the
 // eager and the graph path, so both produce identical results).
 int decode_partition(const Engine *eng, const StepPlan &plan, int max_ctx);

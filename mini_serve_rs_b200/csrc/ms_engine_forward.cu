@@ -79,7 +79,8 @@ int enqueue_forward(Engine *eng, const StepPlan &plan) {
   pa.seq_start = d + 2 * S;
   pa.num_seqs = S;
   pa.tokens = d + 3 * S;
-  pa.delta_row = pa.tokens + T;
+  int32_t *samp = pa.tokens + T;  // [temp S][top_p S][seed_lo S][seed_hi S] when plan.sample
+  pa.delta_row = samp + (plan.sample ? 4 * S : 0);
   pa.delta_idx = pa.delta_row + dc;
   pa.delta_block = pa.delta_idx + dc;
   pa.num_deltas = dc;
@@ -202,11 +203,25 @@ int enqueue_forward(Engine *eng, const StepPlan &plan) {
   // lm_head in f32 output, greedy argmax, tokens back to the host
   MS_BLAS_TRY(linear(eng, eng->lm_head, eng->last_norm, eng->logits, eng->V, S, eng->H, true));
   MS_CUDA_TRY(launch_argmax(eng->logits, S, eng->V, eng->d_next, pa.seq_row, eng->d_slot_last, st));
+  if (plan.sample) {  // rows with temperature >= 1e-7 replace their argmax by a draw
+    SampleArgs sa;
+    sa.logits = eng->logits;
+    sa.rows = S;
+    sa.vocab = eng->V;
+    sa.temperature = reinterpret_cast<const float *>(samp);
+    sa.top_p = reinterpret_cast<const float *>(samp + S);
+    sa.seed_lo = reinterpret_cast<const uint32_t *>(samp + 2 * S);
+    sa.seed_hi = reinterpret_cast<const uint32_t *>(samp + 3 * S);
+    sa.out = eng->d_next;
+    sa.row_slot = pa.seq_row;
+    sa.slot_last = eng->d_slot_last;
+    MS_CUDA_TRY(launch_sample(sa, st));
+  }
   {
     const int max_blk = (plan.max_ctx_launch + 15) / 16;
     const int parts = plan.n_dec > 0 ? (max_blk + part - 1) / part : 0;
     const int attn_launches = (plan.n_dec > 0 ? 1 + (parts > 1 ? 1 : 0) : 0) + (plan.n_tiles > 0 ? 1 : 0);
-    eng->last_launches = 3 + int64_t(eng->L) * (4 + attn_launches);
+    eng->last_launches = 3 + (plan.sample ? 1 : 0) + int64_t(eng->L) * (4 + attn_launches);
     eng->kernel_launches += eng->last_launches;
   }
   MS_CUDA_TRY(cudaMemcpyAsync(eng->h_next, eng->d_next, size_t(S) * 4, cudaMemcpyDeviceToHost, st));

@@ -210,22 +210,29 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
   }
 
   // ---- stage the step description: one pinned buffer, one upload ----
+  // (a graph always carries the sampling block: all-greedy rows exit at once)
+  bool want_sample = false;
+  if (desc->temperature)
+    for (int i = 0; i < S && !want_sample; ++i) want_sample = double(desc->temperature[i]) >= 1e-7;
   int32_t *h;
   if (g) {
     sp.graph = true;
+    sp.sample = true;
     sp.hdr = 4;
     sp.delta_cap = S;
     sp.max_ctx_launch = g->max_ctx_cap;
     sp.h_desc = eng->h_gin;
     sp.d_desc = eng->d_gin;
-    sp.desc_elems = 4 + size_t(7) * S;
+    sp.desc_elems = 4 + size_t(11) * S;
     h = eng->h_gin;
     h[0] = nd;
     h[1] = h[2] = h[3] = 0;
     h += 4;
   } else {
+    sp.sample = want_sample;
     sp.delta_cap = nd;
-    const size_t need = size_t(3) * S + T + size_t(3) * nd + (sp.split ? size_t(sp.n_dec) + 4 * size_t(sp.n_tiles) : 0);
+    const size_t need = size_t(3) * S + T + (sp.sample ? size_t(4) * S : 0) + size_t(3) * nd +
+                        (sp.split ? size_t(sp.n_dec) + 4 * size_t(sp.n_tiles) : 0);
     int rc = grow_staging(eng, need);
     if (rc != MS_OK) return rc;
     sp.h_desc = eng->h_in;
@@ -235,7 +242,19 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
   }
   const int dc = sp.delta_cap;
   int32_t *h_row = h, *h_ntok = h + S, *h_start = h + 2 * S, *h_tok = h + 3 * S;
-  int32_t *h_drow = h_tok + T, *h_didx = h_drow + dc, *h_dblk = h_didx + dc;
+  int32_t *h_samp = h_tok + T;
+  int32_t *h_drow = h_samp + (sp.sample ? 4 * S : 0), *h_didx = h_drow + dc, *h_dblk = h_didx + dc;
+  if (sp.sample) {
+    float *temp = reinterpret_cast<float *>(h_samp), *topp = reinterpret_cast<float *>(h_samp + S);
+    uint32_t *slo = reinterpret_cast<uint32_t *>(h_samp + 2 * S), *shi = reinterpret_cast<uint32_t *>(h_samp + 3 * S);
+    for (int i = 0; i < S; ++i) {
+      temp[i] = desc->temperature ? desc->temperature[i] : 0.f;
+      topp[i] = desc->top_p ? desc->top_p[i] : 1.f;
+      const uint64_t sd = desc->seeds ? desc->seeds[i] : 0ull;
+      slo[i] = uint32_t(sd);
+      shi[i] = uint32_t(sd >> 32);
+    }
+  }
   int t = 0, d = 0;
   for (int i = 0; i < S; ++i) {
     const RowPlan &r = plan[i];

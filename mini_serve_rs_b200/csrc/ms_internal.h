@@ -95,6 +95,19 @@ cudaError_t launch_qk_norm_rope_append(const void *qkv, const void *bias, const 
 
 cudaError_t launch_silu_mul(const void *gate_up, void *out, int rows, int inter, int dtype,
                             cudaStream_t stream);
+// K6b sampling (ms_sample.cu).  seeds, or seed_lo/seed_hi halves, or neither (0).
+struct SampleArgs {
+  const float *logits = nullptr;  // [rows, vocab]
+  int rows = 0, vocab = 0;
+  const float *temperature = nullptr;  // [rows]; < 1e-7 leaves out[row] untouched
+  const float *top_p = nullptr;        // [rows] or null
+  const uint64_t *seeds = nullptr;
+  const uint32_t *seed_lo = nullptr, *seed_hi = nullptr;
+  int32_t *out = nullptr;               // [rows]
+  const int32_t *row_slot = nullptr;    // with slot_last: also record the token per slot
+  int32_t *slot_last = nullptr;
+};
+cudaError_t launch_sample(const SampleArgs &a, cudaStream_t st);
 cudaError_t launch_argmax(const float *logits, int rows, int vocab, int32_t *out,
                           const int32_t *row_slot, int32_t *slot_last_token, cudaStream_t stream);
 cudaError_t launch_embedding(const int32_t *tokens, const void *table, void *out, int rows,

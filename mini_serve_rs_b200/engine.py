@@ -39,7 +39,8 @@ class MsEngineOpts(C.Structure):
 class MsStepDesc(C.Structure):
     _fields_ = [("num_seqs", C.c_int32), ("seq_ids", C.POINTER(C.c_uint64)),
                 ("input_tokens", C.POINTER(C.c_uint32)), ("positions", C.POINTER(C.c_int32)),
-                ("flags", C.c_uint32)]
+                ("flags", C.c_uint32), ("temperature", C.POINTER(C.c_float)), ("top_p", C.POINTER(C.c_float)),
+                ("seeds", C.POINTER(C.c_uint64))]
 
 
 _P = C.c_void_p
@@ -87,6 +88,7 @@ _SIGS = {
     "ms_prefill_tiles": ([C.POINTER(_I32)] * 4 + [_I32, _I32, _I32, C.POINTER(_I32), _I32], C.c_int),
     "ms_launch_silu_mul": ([_P, _P, _I32, _I32, _I32, _P], C.c_int),
     "ms_launch_argmax": ([_P, _I32, _I32, _P, _P], C.c_int),
+    "ms_launch_sample": ([_P, _I32, _I32, _P, _P, _P, _P, _P], C.c_int),
     "launch_rmsnorm_f32": ([_P, _P, _P, C.c_int, C.c_int, C.c_float], C.c_int),
     "launch_rmsnorm_f16": ([_P, _P, _P, C.c_int, C.c_int, C.c_float], C.c_int),
     "launch_rmsnorm_bf16": ([_P, _P, _P, C.c_int, C.c_int, C.c_float], C.c_int),
@@ -264,24 +266,40 @@ class Engine:
         return v.value
 
     # -- step
-    def _desc(self, seq_ids, input_tokens, positions, flags):
+    def _desc(self, seq_ids, input_tokens, positions, flags, temperature=None, top_p=None, seeds=None):
         ids = np.ascontiguousarray(seq_ids, dtype=np.uint64)
         toks = None if input_tokens is None else np.ascontiguousarray(input_tokens, dtype=np.uint32)
         pos = None if positions is None else np.ascontiguousarray(positions, dtype=np.int32)
-        d = MsStepDesc(len(ids), ids.ctypes.data_as(C.POINTER(C.c_uint64)),
-                       None if toks is None else _u32p(toks), None if pos is None else _i32p(pos), flags)
-        return d, (ids, toks, pos)
+        n = len(ids)
 
-    def step(self, seq_ids, input_tokens=None, positions=None, flags: int = 0):
-        d, keep = self._desc(seq_ids, input_tokens, positions, flags)
+        def per_seq(v, dt):  # scalar or per-sequence array -> contiguous [n]
+            if v is None:
+                return None
+            return np.ascontiguousarray(np.broadcast_to(np.asarray(v, dtype=dt), (n,)), dtype=dt)
+
+        temp = per_seq(temperature, np.float32)
+        tp = per_seq(top_p, np.float32)
+        sd = per_seq(seeds, np.uint64)
+        fp = lambda a: None if a is None else a.ctypes.data_as(C.POINTER(C.c_float))
+        d = MsStepDesc(n, ids.ctypes.data_as(C.POINTER(C.c_uint64)),
+                       None if toks is None else _u32p(toks), None if pos is None else _i32p(pos), flags,
+                       fp(temp), fp(tp), None if sd is None else sd.ctypes.data_as(C.POINTER(C.c_uint64)))
+        return d, (ids, toks, pos, temp, tp, sd)
+
+    def step(self, seq_ids, input_tokens=None, positions=None, flags: int = 0, temperature=None, top_p=None,
+             seeds=None):
+        """One step; temperature / top_p / seeds (scalars or per-sequence) select
+        on-device sampling for rows with temperature >= 1e-7 (greedy otherwise)."""
+        d, keep = self._desc(seq_ids, input_tokens, positions, flags, temperature, top_p, seeds)
         n = len(keep[0])
         rc = self.lib.ms_step(self.h, C.byref(d), _u32p(self._out_tok),
                               self._out_flags.ctypes.data_as(C.POINTER(C.c_uint8)))
         self._check(rc, "step")
         return self._out_tok[:n].copy(), self._out_flags[:n].copy()
 
-    def step_launch(self, seq_ids, input_tokens=None, positions=None, flags: int = 0):
-        d, keep = self._desc(seq_ids, input_tokens, positions, flags)
+    def step_launch(self, seq_ids, input_tokens=None, positions=None, flags: int = 0, temperature=None,
+                    top_p=None, seeds=None):
+        d, keep = self._desc(seq_ids, input_tokens, positions, flags, temperature, top_p, seeds)
         self._pending_n = len(keep[0])
         self._check(self.lib.ms_step_launch(self.h, C.byref(d)), "step_launch")
 

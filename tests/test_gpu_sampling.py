@@ -1,0 +1,133 @@
+"""On-device temperature / top-p sampling (K6b, ms_launch_sample and the
+engine's step) against the CPU restatements in oracle.sampling_ref.
+
+* Exact: for a given seed the kernel draws the token the restatement of the
+  kernel draws (same weights, nucleus edge, SplitMix64 stream), on the race
+  path and on the radix-select fallback (small top_p).
+* Distribution: over 8192 seeds the draws follow LogitsProcessor's
+  distribution (candle.rs:737-763), and no token outside its nucleus appears.
+* Greedy rows (temperature < 1e-7) keep the argmax already in `out`.
+* In the engine, sampled rows of a step are the restatement's draw from that
+  step's logits, eager and replayed from a CUDA graph alike.
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+from scipy.stats import chi2
+
+from mini_serve_rs_b200 import engine as E
+from oracle.qwen_ref import random_weights
+from oracle.sampling_ref import candle_probs, sample_like_kernel
+from tests.golden.golden_cases import MODEL_CASES
+from tests.gpu_util import need_gpu
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def _launch(logits, temps, tops, seeds, out_init):
+    lib = E.lib()
+    lg = torch.from_numpy(np.ascontiguousarray(logits, np.float32)).to(DEV)
+    t = torch.from_numpy(np.asarray(temps, np.float32)).to(DEV)
+    p = None if tops is None else torch.from_numpy(np.asarray(tops, np.float32)).to(DEV)
+    s = torch.from_numpy(np.asarray(seeds, np.uint64).view(np.int64)).to(DEV)
+    out = torch.from_numpy(np.asarray(out_init, np.int32)).to(DEV)
+    rc = lib.ms_launch_sample(C.c_void_p(lg.data_ptr()), lg.shape[0], lg.shape[1], C.c_void_p(t.data_ptr()),
+                              None if p is None else C.c_void_p(p.data_ptr()), C.c_void_p(s.data_ptr()),
+                              C.c_void_p(out.data_ptr()), None)
+    assert rc == 0
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def test_kernel_draws_equal_restatement():
+    need_gpu()
+    rng = np.random.default_rng(3)
+    rows, V = 48, 151936
+    x = (rng.standard_normal((rows, V)) * 3).astype(np.float32)
+    temps = rng.uniform(0.3, 1.5, rows).astype(np.float32)
+    temps[::8] = 0.0  # greedy rows
+    tops = rng.choice(np.array([1.0, 0.5, 0.9, 0.99, 0.3], np.float32), rows)
+    seeds = rng.integers(0, 2 ** 63, rows, dtype=np.uint64)
+    out = _launch(x, temps, tops, seeds, np.full(rows, -7, np.int32))
+    agree = 0
+    for r in range(rows):
+        want = sample_like_kernel(x[r], temps[r], float(tops[r]), int(seeds[r]))
+        if want is None:
+            assert out[r] == -7, r
+            agree += 1
+        else:
+            agree += int(out[r] == want)
+    assert agree >= rows - 1, (agree, rows)
+
+
+def test_kernel_small_top_p_takes_the_radix_path_and_still_agrees():
+    """Flat rows with top_p 0.05: most rows reject 8 race candidates and fall
+    back to the radix-select edge; the draw must still be the restatement's."""
+    need_gpu()
+    rng = np.random.default_rng(21)
+    rows, V = 32, 4096
+    x = (rng.standard_normal((rows, V)) * 0.1).astype(np.float32)
+    seeds = rng.integers(0, 2 ** 63, rows, dtype=np.uint64)
+    out = _launch(x, np.ones(rows, np.float32), np.full(rows, 0.05, np.float32), seeds, np.zeros(rows, np.int32))
+    agree = sum(int(out[r] == sample_like_kernel(x[r], 1.0, 0.05, int(seeds[r]))) for r in range(rows))
+    assert agree >= rows - 1, agree
+
+
+@pytest.mark.parametrize("t,p", [(1.0, None), (0.8, 0.9), (1.3, 0.5), (0.5, 0.97)])
+def test_kernel_distribution_matches_logits_processor(t, p):
+    need_gpu()
+    rng = np.random.default_rng(9)
+    V, n = 64, 8192
+    row = (rng.standard_normal(V) * 2).astype(np.float32)
+    x = np.tile(row, (n, 1))
+    out = _launch(x, np.full(n, t, np.float32), None if p is None else np.full(n, p, np.float32),
+                  np.arange(n, dtype=np.uint64) * 7919 + 1, np.zeros(n, np.int32))
+    counts = np.bincount(out, minlength=V)
+    q = candle_probs(row, t, p)
+    q = q / q.sum()
+    nz = q > 0
+    assert counts[~nz].sum() == 0
+    stat = float(((counts[nz] - n * q[nz]) ** 2 / (n * q[nz])).sum())
+    assert stat < chi2.ppf(0.9995, int(nz.sum()) - 1), stat
+
+
+def test_kernel_ties_at_nucleus_edge():
+    need_gpu()
+    row = np.array([0.0, 2.0, 1.0, 1.0, 1.0, 1.0, -1.0] + [-30.0] * 57, np.float32)
+    n = 4096
+    out = _launch(np.tile(row, (n, 1)), np.ones(n, np.float32), np.full(n, 0.6, np.float32),
+                  np.arange(n, dtype=np.uint64), np.zeros(n, np.int32))
+    assert set(np.unique(out).tolist()) == {1, 2, 3}  # top token + the first two ties in index order
+
+
+def test_engine_step_samples_like_restatement():
+    need_gpu()
+    case = MODEL_CASES[1]
+    cfg = case["cfg"]
+    eng = E.Engine(cfg, pool_blocks=128, max_seqs=8, max_tokens_per_step=512, max_blocks_per_seq=32,
+                   dtype=E.MS_DTYPE_BF16)
+    eng.load_weights(random_weights(cfg, case["seed"], norm_std=case.get("norm_std", 0.0)))
+    rng = np.random.default_rng(4)
+    ids = [1, 2, 3, 4]
+    for k, sid in enumerate(ids):
+        eng.admit(sid, list(rng.integers(0, cfg.vocab_size, 10 + 7 * k)), list(range(8 * k, 8 * k + 8)))
+    temps = np.array([0.0, 0.8, 1.2, 0.0], np.float32)
+    tops = np.array([1.0, 0.9, 0.5, 1.0], np.float32)
+    checked = 0
+    for step in range(12):  # prefill, an eager decode, a captured one, then graph replays
+        seeds = np.array([11, 1000 + step, 2000 + step, 13], np.uint64)
+        flags = 0 if step == 0 else E.MS_STEP_TOKENS_FROM_DEVICE
+        toks, _ = eng.step(ids, flags=flags, temperature=temps, top_p=tops, seeds=seeds)
+        lg = eng.logits(len(ids))
+        for i in range(len(ids)):
+            want = sample_like_kernel(lg[i], temps[i], float(tops[i]), int(seeds[i]))
+            if want is None:
+                want = int(np.argmax(lg[i]))
+            assert int(toks[i]) == want, (step, i, int(toks[i]), want)
+            checked += 1
+    assert eng.graph_stats()[1] >= 8
+    eng.close()
+    assert checked == 48
