@@ -24,8 +24,9 @@
 //      a superset of it is the winner over it whenever it is itself kept, so
 //      each candidate costs one pass: its ranked-before mass against the
 //      target, plus the race over the tokens ranked above it (the next
-//      candidate when it is rejected).  Each check succeeds with probability
-//      at least top_p;
+//      candidate when it is rejected); after the first, which also sums W,
+//      only tokens ranked above the candidate compute anything.  Each check
+//      succeeds with probability at least top_p;
 //   3. after 8 rejections a 4-pass radix select over the bits of e (u64 mass
 //      histograms in shared memory) finds the edge key v*: tokens above v*
 //      are kept, and of the tokens equal to v* the first c in index order,
@@ -43,7 +44,6 @@ namespace {
 
 constexpr int kThreads = 512;  // 2 CTAs (rows) per SM: a 256-row batch is one wave
 constexpr int kWarpsPerCta = kThreads / 32;
-constexpr float kFix = 1099511627776.0f;  // 2^40: fixed-point scale of the mass weights
 constexpr uint64_t kGolden = 0x9E3779B97F4A7C15ull;
 
 __device__ __forceinline__ uint64_t splitmix64_mix(uint64_t z) {
@@ -67,7 +67,39 @@ __device__ __forceinline__ float uniform_open(uint64_t state) {
 __device__ __forceinline__ float scaled(float x, float inv_t) { return __fmul_rn(x, inv_t); }
 __device__ __forceinline__ float weight_e(float z, float m) { return expf(__fsub_rn(z, m)); }
 
-__device__ __forceinline__ uint64_t weight_of(float e) { return e > 0.f ? uint64_t(e * kFix) : 0ull; }
+// trunc(e * 2^40) for 0 <= e <= 1 from the bits of e: e = mant * 2^(exp - 150)
+// with the implicit bit, so e * 2^40 = mant * 2^(exp - 110) (exact; integer
+// ALU work instead of a float -> u64 conversion).  Zero for e < 2^-40.
+__device__ __forceinline__ uint64_t weight_of(float e) {
+  const uint32_t b = __float_as_uint(e);
+  const int ex = int(b >> 23);  // sign is 0 for e > 0
+  if (!(e > 0.f) || ex == 0 || ex > 127) return 0ull;  // zero, NaN, subnormal (< 2^-126), above 1
+  const uint64_t mant = (b & 0x7fffffu) | 0x800000u;
+  const int sh = ex - 110;
+  return sh >= 0 ? mant << sh : (sh > -24 ? mant >> (-sh) : 0ull);
+}
+
+// Calls f(x[i], i) for every i < V owned by this thread: two 16-byte loads
+// in flight per iteration when the row is 16-byte aligned, scalar otherwise.
+template <typename F>
+__device__ __forceinline__ void for_row(const float *x, int V, F &&f) {
+  if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const float4 *x4 = reinterpret_cast<const float4 *>(x);
+    const int n4 = V >> 2;
+    for (int q = threadIdx.x; q < n4; q += 2 * kThreads) {
+      const bool hb = q + kThreads < n4;
+      const float4 a = x4[q];
+      const float4 b = hb ? x4[q + kThreads] : make_float4(0.f, 0.f, 0.f, 0.f);
+      f(a.x, 4 * q); f(a.y, 4 * q + 1); f(a.z, 4 * q + 2); f(a.w, 4 * q + 3);
+      if (hb) {
+        const int qb = 4 * (q + kThreads);
+        f(b.x, qb); f(b.y, qb + 1); f(b.z, qb + 2); f(b.w, qb + 3);
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += kThreads) f(x[i], i);
+  }
+}
 
 // Race score of token i: z_i - log(E_i), E_i = -log(U_i) ~ Exp(1).  The
 // largest score over a set picks i with probability exp(z_i) / sum(exp(z)).
@@ -176,20 +208,17 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
     }
   };
 
-  // 1. max of the scaled logits and the race winner over every token.  A
-  //    token whose weight underflows (e < 2^-40) cannot win against the top
-  //    token (its score is below m - 11, the top token's above m - 3), so the
-  //    race needs no weights.
+  // 1. max of the scaled logits and the race over every token: token i
+  //    scores z_i - log(E_i).  A token whose weight underflows (e < 2^-40)
+  //    cannot win against the top token (its score is below m - 11, the top
+  //    token's above m - 3), so the race needs no weights.
   float m = -INFINITY;
   Best best{-INFINITY, 0x7fffffff};
-  {
-    uint64_t st = splitmix_state(seed, threadIdx.x);
-    for (int i = threadIdx.x; i < V; i += kThreads, st += uint64_t(kThreads) * kGolden) {
-      const float z = scaled(x[i], inv_t);
-      m = fmaxf(m, z);
-      take(best, race_score(z, st), i);
-    }
-  }
+  for_row(x, V, [&](float xv, int i) {
+    const float z = scaled(xv, inv_t);
+    m = fmaxf(m, z);
+    take(best, race_score(z, splitmix_state(seed, i)), i);
+  });
   m = block_max(m, redf);
   best = block_best(best, redf, redi);
   if (!(m > -INFINITY) || !(m < INFINITY) || best.idx == 0x7fffffff) return;  // all -inf / NaN: keep argmax
@@ -204,15 +233,21 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
   //    is itself kept, it is the winner over the kept set; otherwise the kept
   //    set lies inside the tokens ranked above it, so race again there.  Each
   //    check is one pass: the mass ranked before candidate j against
-  //    ceil(top_p * W), and the next candidate.
+  //    ceil(top_p * W), and the next candidate.  The first check also sums W
+  //    (e for every token); later ones compute e only where it can rank
+  //    before j: e = exp(z - m) is monotone in z, so that needs z >= z_j less
+  //    a margin wider than the span of z that rounds to the same e.
   uint64_t target = 0;
   int j = best.idx;
   for (int iter = 0; iter < 8; ++iter) {
-    const float ej = weight_e(scaled(x[j], inv_t), m);
+    const float zj = scaled(x[j], inv_t);
+    const float ej = weight_e(zj, m);
+    const float zlo = iter == 0 ? -INFINITY : zj - 1e-6f * (1.0f + fabsf(zj - m));
     uint64_t w_all = 0, w_before = 0;
     Best next{-INFINITY, 0x7fffffff};
-    for (int i = threadIdx.x; i < V; i += kThreads) {
-      const float z = scaled(x[i], inv_t);
+    for_row(x, V, [&](float xv, int i) {
+      const float z = scaled(xv, inv_t);
+      if (z < zlo) return;
       const float e = weight_e(z, m);
       const uint64_t w = weight_of(e);
       w_all += w;
@@ -220,7 +255,7 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
         w_before += w;
         take(next, race_score(z, splitmix_state(seed, i)), i);
       }
-    }
+    });
     if (iter == 0) target = uint64_t(ceil(top_p * double(block_sum_u64(w_all, red64))));
     w_before = block_sum_u64(w_before, red64);
     next = block_best(next, redf, redi);
@@ -309,12 +344,12 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
   }
   best = Best{-INFINITY, 0x7fffffff};
   if (keep_ties < 0) {
-    for (int i = threadIdx.x; i < V; i += kThreads) {
-      const float z = scaled(x[i], inv_t);
+    for_row(x, V, [&](float xv, int i) {
+      const float z = scaled(xv, inv_t);
       const float e = weight_e(z, m);
-      if (__float_as_uint(e) < edge || weight_of(e) == 0) continue;
+      if (__float_as_uint(e) < edge || weight_of(e) == 0) return;
       take(best, race_score(z, splitmix_state(seed, i)), i);
-    }
+    });
   } else {
     // ties at the edge are kept in index order: contiguous chunks per thread
     const int per = (V + kThreads - 1) / kThreads;
