@@ -175,6 +175,53 @@ int ms_seq_release(ms_engine *eng, uint64_t seq_id);
 /* Number of tokens whose K/V the engine holds for seq_id. */
 int ms_seq_cached_tokens(const ms_engine *eng, uint64_t seq_id, int32_t *out);
 
+/* ---- paged prefix cache (kv_cache.rs:14-145 + prefix_cache.rs:57-345) ---
+ * A host-side page manager the scheduler uses in place of KVCache.  A cached
+ * 16-token chunk is the pool page holding its K/V, so a prefix hit shares
+ * pages (reference counts) instead of copying snapshots; chain keys are the
+ * reference's SHA-256 chain (prefix_cache.rs:103-124).  Flow per request:
+ * ms_pages_admit -> ms_seq_admit(eng, id, prompt, blocks, n, cached) ->
+ * steps (ms_pages_allocate_block + ms_seq_append_block as it grows) ->
+ * ms_pages_publish once its prompt is prefilled -> ms_seq_release +
+ * ms_pages_release.  Thread-safe (one mutex); one manager per pool. */
+typedef struct ms_pages ms_pages;
+typedef struct ms_pages_stats {
+  int64_t total_blocks;
+  int64_t free_blocks;       /* on the free stack */
+  int64_t cached_chunks;     /* prefix-cache entries (one page each) */
+  int64_t cache_only_blocks; /* cached pages no sequence holds (evictable) */
+  int64_t hits, misses, tokens_saved; /* record_reuse, prefix_cache.rs:359-367 */
+  int64_t evictions;         /* cached chunks evicted */
+  int64_t rejections;        /* admissions / block requests refused (CachePressure) */
+} ms_pages_stats;
+/* max_chunks = 0 disables the prefix cache: block ids are then exactly
+ * KVCache's (LIFO stack popping 0, 1, 2, ... first). */
+int ms_pages_create(int64_t total_blocks, int32_t block_size, int32_t max_chunks, ms_pages **out);
+int ms_pages_destroy(ms_pages *pm);
+/* Scheduler admission (scheduler.rs:347-369): pages for max(prompt_len, 1)
+ * tokens, the leading ones shared from the prefix cache (at most
+ * (prompt_len - 1) / block_size chunks, so the last prompt token is always
+ * computed), the rest fresh.  cached_tokens_out = shared chunks * block_size,
+ * the num_cached of ms_seq_admit.  All or nothing; MS_E_PRESSURE when the free
+ * pages, after evicting unused cached chunks, do not suffice. */
+int ms_pages_admit(ms_pages *pm, uint64_t seq_id, const uint32_t *prompt, int32_t prompt_len,
+                   int32_t *blocks_out, int32_t capacity, int32_t *num_blocks_out, int32_t *cached_tokens_out);
+/* KVCache::allocate_block (kv_cache.rs:86-99). */
+int ms_pages_allocate_block(ms_pages *pm, uint64_t seq_id, int32_t *block_out);
+/* KVCache::release (kv_cache.rs:101-111): drops the sequence's references. */
+int ms_pages_release(ms_pages *pm, uint64_t seq_id, int32_t *released_out);
+/* After the sequence's prompt is prefilled (insert_kv, candle.rs:552-573):
+ * its full prompt chunks not yet cached enter the cache as its own pages. */
+int ms_pages_publish(ms_pages *pm, uint64_t seq_id, const uint32_t *prompt, int32_t prompt_len,
+                     int32_t *published_out);
+/* PrefixCache::lookup (prefix_cache.rs:126-157): leading cached tokens. */
+int ms_pages_lookup(ms_pages *pm, const uint32_t *prompt, int32_t prompt_len, int32_t *matched_tokens);
+int ms_pages_stats_get(ms_pages *pm, ms_pages_stats *out);
+/* The chain keys (32 bytes each) of the full chunks of tokens; returns their
+ * count, -1 on bad arguments or capacity (in keys) too small. */
+int ms_prefix_chunk_hashes(const uint32_t *tokens, int32_t num_tokens, int32_t chunk_size, uint8_t *out,
+                           int32_t capacity);
+
 /* ---- the hot path ------------------------------------------------------ */
 
 /* step_batch: one token per sequence into out_tokens[num_seqs] (greedy

@@ -43,6 +43,11 @@ class MsStepDesc(C.Structure):
                 ("seeds", C.POINTER(C.c_uint64))]
 
 
+class MsPagesStats(C.Structure):
+    _fields_ = [(n, C.c_int64) for n in ("total_blocks", "free_blocks", "cached_chunks", "cache_only_blocks",
+                                         "hits", "misses", "tokens_saved", "evictions", "rejections")]
+
+
 _P = C.c_void_p
 _I32 = C.c_int32
 _SIGS = {
@@ -89,6 +94,15 @@ _SIGS = {
     "ms_launch_silu_mul": ([_P, _P, _I32, _I32, _I32, _P], C.c_int),
     "ms_launch_argmax": ([_P, _I32, _I32, _P, _P], C.c_int),
     "ms_launch_sample": ([_P, _I32, _I32, _P, _P, _P, _P, _P], C.c_int),
+    "ms_pages_create": ([C.c_int64, _I32, _I32, C.POINTER(_P)], C.c_int),
+    "ms_pages_destroy": ([_P], C.c_int),
+    "ms_pages_admit": ([_P, C.c_uint64, _P, _I32, _P, _I32, C.POINTER(_I32), C.POINTER(_I32)], C.c_int),
+    "ms_pages_allocate_block": ([_P, C.c_uint64, C.POINTER(_I32)], C.c_int),
+    "ms_pages_release": ([_P, C.c_uint64, C.POINTER(_I32)], C.c_int),
+    "ms_pages_publish": ([_P, C.c_uint64, _P, _I32, C.POINTER(_I32)], C.c_int),
+    "ms_pages_lookup": ([_P, _P, _I32, C.POINTER(_I32)], C.c_int),
+    "ms_pages_stats_get": ([_P, C.POINTER(MsPagesStats)], C.c_int),
+    "ms_prefix_chunk_hashes": ([_P, _I32, _I32, _P, _I32], C.c_int),
     "launch_rmsnorm_f32": ([_P, _P, _P, C.c_int, C.c_int, C.c_float], C.c_int),
     "launch_rmsnorm_f16": ([_P, _P, _P, C.c_int, C.c_int, C.c_float], C.c_int),
     "launch_rmsnorm_bf16": ([_P, _P, _P, C.c_int, C.c_int, C.c_float], C.c_int),
@@ -378,6 +392,91 @@ class Engine:
 
 
 # ---- NCCL communicator helpers (tensor parallelism) ------------------------------
+
+
+class Pages:
+    """Host-side paged prefix cache + block manager (ms_pages_*): the
+    scheduler's KVCache with prefix-cache page sharing.  No GPU needed."""
+
+    def __init__(self, total_blocks: int, block_size: int = 16, max_chunks: int = 512):
+        self.lib = lib()
+        h = C.c_void_p()
+        rc = self.lib.ms_pages_create(total_blocks, block_size, max_chunks, C.byref(h))
+        if rc != MS_OK:
+            raise error_for(rc, "ms_pages_create")
+        self.h = h
+        self.block_size = block_size
+
+    @staticmethod
+    def _toks(prompt):
+        return np.ascontiguousarray(prompt, dtype=np.uint32)
+
+    def admit(self, seq_id: int, prompt):
+        """(block ids, cached tokens) for a new request; raises CachePressure."""
+        pr = self._toks(prompt)
+        cap = max(1, -(-max(len(pr), 1) // self.block_size))
+        out = np.zeros(cap, np.int32)
+        n, cached = _I32(), _I32()
+        rc = self.lib.ms_pages_admit(self.h, seq_id, pr.ctypes.data, len(pr), out.ctypes.data, cap,
+                                     C.byref(n), C.byref(cached))
+        if rc != MS_OK:
+            raise error_for(rc, "ms_pages_admit")
+        return out[:n.value].tolist(), cached.value
+
+    def allocate_block(self, seq_id: int) -> int:
+        b = _I32()
+        rc = self.lib.ms_pages_allocate_block(self.h, seq_id, C.byref(b))
+        if rc != MS_OK:
+            raise error_for(rc, "ms_pages_allocate_block")
+        return b.value
+
+    def release(self, seq_id: int) -> int:
+        n = _I32()
+        self.lib.ms_pages_release(self.h, seq_id, C.byref(n))
+        return n.value
+
+    def publish(self, seq_id: int, prompt) -> int:
+        pr = self._toks(prompt)
+        n = _I32()
+        rc = self.lib.ms_pages_publish(self.h, seq_id, pr.ctypes.data, len(pr), C.byref(n))
+        if rc != MS_OK:
+            raise error_for(rc, "ms_pages_publish")
+        return n.value
+
+    def lookup(self, prompt) -> int:
+        pr = self._toks(prompt)
+        n = _I32()
+        rc = self.lib.ms_pages_lookup(self.h, pr.ctypes.data, len(pr), C.byref(n))
+        if rc != MS_OK:
+            raise error_for(rc, "ms_pages_lookup")
+        return n.value
+
+    def stats(self) -> dict:
+        st = MsPagesStats()
+        self.lib.ms_pages_stats_get(self.h, C.byref(st))
+        return {n: getattr(st, n) for n, _ in MsPagesStats._fields_}
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.ms_pages_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def chunk_hashes(tokens, chunk_size: int = 16):
+    """The reference's chain keys (hex strings) computed by the library."""
+    tk = np.ascontiguousarray(tokens, dtype=np.uint32)
+    cap = max(1, len(tk) // chunk_size)
+    out = np.zeros(cap * 32, np.uint8)
+    n = lib().ms_prefix_chunk_hashes(tk.ctypes.data, len(tk), chunk_size, out.ctypes.data, cap)
+    if n < 0:
+        raise ValueError("ms_prefix_chunk_hashes")
+    return [bytes(out[32 * i:32 * i + 32]).hex() for i in range(n)]
 
 
 def nccl_unique_id() -> bytes:
