@@ -60,6 +60,7 @@ extern "C" {
 
 /* ms_step out_flags bits */
 #define MS_FLAG_PREFILLED 1u /* this step ran the sequence's prefill */
+#define MS_FLAG_NO_TOKEN 2u  /* no token this step: the prompt is still being prefilled in chunks */
 
 /* Model configuration.  Mirrors the fields of qwen2.rs:9-54 (Config) that the
  * forward step reads.  qk_norm / attn_bias / tie_word_embeddings are decided
@@ -123,6 +124,14 @@ typedef struct ms_step_desc {
   const float *temperature;
   const float *top_p;
   const uint64_t *seeds;
+  /* Chunked prefill: at most token_budget packed tokens this step (0: no
+   * limit).  Decode rows come first (one token each, never deferred); the
+   * rest of the budget goes to unfinished prompts in list order, each taking
+   * as many of its remaining prompt tokens as fit.  A prompt that does not
+   * finish gets MS_FLAG_NO_TOKEN (its out_tokens entry is 0) and continues
+   * from where it stopped in the next step; its block table only has to
+   * cover the tokens scheduled so far. */
+  int32_t token_budget;
 } ms_step_desc;
 
 /* ---- engine lifetime --------------------------------------------------- */

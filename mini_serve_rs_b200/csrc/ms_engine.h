@@ -137,6 +137,9 @@ struct Engine {
   std::vector<int> last_slots;
   std::vector<uint8_t> last_flags;
   std::vector<uint64_t> last_ids;
+  int last_in = 0;             // sequences listed in the last step description
+  std::vector<int> last_map;   // listed index -> packed row, -1 when not run
+  std::vector<uint8_t> last_out_flags;  // per listed sequence
 
   int fail(int code, const std::string &msg) {
     err = msg;

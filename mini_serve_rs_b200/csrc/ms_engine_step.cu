@@ -30,6 +30,8 @@ struct RowPlan {
   Seq *seq;
   int ntok, start;
   bool prefill;
+  bool partial = false;  // a prompt chunk that does not reach the prompt's end
+  int orig = 0;          // index in the step description
 };
 
 int grow_staging(Engine *eng, size_t elems) {
@@ -62,32 +64,33 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
     eng->inject = 0;
     return eng->fail(MS_E_INJECTED, "injected fault");
   }
-  const int S = desc->num_seqs;
-  if (S < 0 || S > eng->opts.max_seqs) return eng->fail(MS_E_INVALID, "num_seqs out of range");
-  if (S == 0) {  // candle.rs:381-383: an empty batch is a no-op
+  const int S_in = desc->num_seqs;
+  if (S_in < 0 || S_in > eng->opts.max_seqs) return eng->fail(MS_E_INVALID, "num_seqs out of range");
+  if (desc->token_budget < 0) return eng->fail(MS_E_INVALID, "negative token_budget");
+  if (S_in == 0) {  // candle.rs:381-383: an empty batch is a no-op
     eng->pending = true;
     eng->last_nseq = 0;
+    eng->last_in = 0;
     eng->last_T = 0;
     return MS_OK;
   }
   if (!desc->seq_ids) return eng->fail(MS_E_INVALID, "null seq_ids");
-  eng->last_ids.assign(desc->seq_ids, desc->seq_ids + S);
+  eng->last_ids.assign(desc->seq_ids, desc->seq_ids + S_in);
   const bool from_dev = (desc->flags & MS_STEP_TOKENS_FROM_DEVICE) != 0;
 
   // ---- plan (validate everything before touching state) ----
-  std::vector<RowPlan> plan(S);
+  std::vector<RowPlan> all(S_in);
   std::unordered_map<uint64_t, int> seen;
-  int T = 0, nd = 0, max_ctx = 0;
-  long long total_blocks = 0;
-  double total_ctx = 0.0;  // sum over packed rows of the keys each row attends to
-  for (int i = 0; i < S; ++i) {
+  int n_decode = 0;
+  for (int i = 0; i < S_in; ++i) {
     const uint64_t id = desc->seq_ids[i];
     auto it = eng->seqs.find(id);
     if (it == eng->seqs.end()) return eng->fail(MS_E_NOT_FOUND, "unknown sequence id " + std::to_string(id));
     if (!seen.emplace(id, i).second) return eng->fail(MS_E_INVALID, "sequence listed twice in one step");
     Seq &s = it->second;
-    RowPlan &r = plan[i];
+    RowPlan &r = all[i];
     r.seq = &s;
+    r.orig = i;
     r.prefill = !s.prefilled;
     const int plen = int(s.prompt.size());
     if (r.prefill) {
@@ -99,6 +102,7 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
         r.ntok = plen - s.cached;
       }
     } else {
+      ++n_decode;
       r.start = s.cached;
       r.ntok = 1;
       if (desc->positions && desc->positions[i] != s.cached)
@@ -109,6 +113,32 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
         if (desc->input_tokens[i] >= uint32_t(eng->V)) return eng->fail(MS_E_INVALID, "input token outside the vocabulary");
       }
     }
+  }
+  // chunked prefill: decode rows first, then prompt tokens in list order
+  if (desc->token_budget > 0) {
+    long long left = (long long)desc->token_budget - n_decode;
+    for (RowPlan &r : all) {
+      if (!r.prefill) continue;
+      const int take = int(std::max(0LL, std::min<long long>(r.ntok, left)));
+      left -= take;
+      r.partial = take < r.ntok;
+      r.ntok = take;
+    }
+  }
+  std::vector<RowPlan> plan;
+  std::vector<int> map(S_in, -1);
+  plan.reserve(S_in);
+  for (int i = 0; i < S_in; ++i)
+    if (all[i].ntok > 0) {
+      map[i] = int(plan.size());
+      plan.push_back(all[i]);
+    }
+  const int S = int(plan.size());
+  int T = 0, nd = 0, max_ctx = 0;
+  long long total_blocks = 0;
+  double total_ctx = 0.0;  // sum over packed rows of the keys each row attends to
+  for (RowPlan &r : plan) {
+    const Seq &s = *r.seq;
     const int end = r.start + r.ntok;
     if (end > eng->rope_len) return eng->fail(MS_E_TOKEN_LIMIT, "position beyond max_position_embeddings");
     if (int64_t(end) > int64_t(s.blocks.size()) * eng->opts.block_size)
@@ -124,6 +154,15 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
   if (T > eng->opts.max_tokens_per_step)
     return eng->fail(MS_E_PRESSURE, "step needs " + std::to_string(T) + " tokens, engine holds " +
                                         std::to_string(eng->opts.max_tokens_per_step));
+  eng->last_in = S_in;
+  eng->last_map = map;
+  eng->last_out_flags.assign(S_in, uint8_t(MS_FLAG_NO_TOKEN));
+  if (S == 0) {  // every listed prompt deferred by a zero budget
+    eng->pending = true;
+    eng->last_nseq = 0;
+    eng->last_T = 0;
+    return MS_OK;
+  }
 
   // ---- attention work split: decode rows (one token) and prefill tiles ----
   StepPlan sp;
@@ -213,7 +252,7 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
   // (a graph always carries the sampling block: all-greedy rows exit at once)
   bool want_sample = false;
   if (desc->temperature)
-    for (int i = 0; i < S && !want_sample; ++i) want_sample = double(desc->temperature[i]) >= 1e-7;
+    for (int i = 0; i < S && !want_sample; ++i) want_sample = double(desc->temperature[plan[i].orig]) >= 1e-7;
   int32_t *h;
   if (g) {
     sp.graph = true;
@@ -248,9 +287,10 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
     float *temp = reinterpret_cast<float *>(h_samp), *topp = reinterpret_cast<float *>(h_samp + S);
     uint32_t *slo = reinterpret_cast<uint32_t *>(h_samp + 2 * S), *shi = reinterpret_cast<uint32_t *>(h_samp + 3 * S);
     for (int i = 0; i < S; ++i) {
-      temp[i] = desc->temperature ? desc->temperature[i] : 0.f;
-      topp[i] = desc->top_p ? desc->top_p[i] : 1.f;
-      const uint64_t sd = desc->seeds ? desc->seeds[i] : 0ull;
+      const int o = plan[i].orig;
+      temp[i] = desc->temperature ? desc->temperature[o] : 0.f;
+      topp[i] = desc->top_p ? desc->top_p[o] : 1.f;
+      const uint64_t sd = desc->seeds ? desc->seeds[o] : 0ull;
       slo[i] = uint32_t(sd);
       shi[i] = uint32_t(sd >> 32);
     }
@@ -265,7 +305,7 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
     if (r.prefill) {
       for (int j = 0; j < r.ntok; ++j) h_tok[t++] = int32_t(s.prompt[r.start + j]);
     } else {
-      h_tok[t++] = from_dev ? -1 : int32_t(desc->input_tokens[i]);
+      h_tok[t++] = from_dev ? -1 : int32_t(desc->input_tokens[r.orig]);
     }
     for (int b = s.synced; b < int(s.blocks.size()); ++b, ++d) {
       h_drow[d] = s.slot;
@@ -317,9 +357,11 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
   for (int i = 0; i < S; ++i) {
     RowPlan &r = plan[i];
     eng->last_slots[i] = r.seq->slot;
-    if (r.prefill) eng->last_flags[i] = MS_FLAG_PREFILLED;
+    if (r.partial) eng->last_flags[i] = MS_FLAG_NO_TOKEN;
+    else if (r.prefill) eng->last_flags[i] = MS_FLAG_PREFILLED;
+    eng->last_out_flags[r.orig] = eng->last_flags[i];
     r.seq->cached = r.start + r.ntok;
-    r.seq->prefilled = true;
+    if (!r.partial) r.seq->prefilled = true;
     r.seq->synced = int(r.seq->blocks.size());
   }
   eng->last_nseq = S;
@@ -332,8 +374,14 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
 int step_wait_impl(Engine *eng, uint32_t *out_tokens, uint8_t *out_flags) {
   if (!eng->pending) return eng->fail(MS_E_INVALID, "ms_step_wait without a launched step");
   eng->pending = false;
-  const int S = eng->last_nseq;
-  if (S == 0) return MS_OK;
+  const int S = eng->last_nseq, S_in = eng->last_in;
+  if (S == 0) {
+    for (int i = 0; i < S_in; ++i) {
+      if (out_tokens) out_tokens[i] = 0;
+      if (out_flags) out_flags[i] = MS_FLAG_NO_TOKEN;
+    }
+    return MS_OK;
+  }
   if (eng->tp > 1) {
     // Host watchdog for the collectives: a peer that died or hangs would
     // otherwise block the step forever.  Poll the step's completion and the
@@ -362,10 +410,12 @@ int step_wait_impl(Engine *eng, uint32_t *out_tokens, uint8_t *out_flags) {
   if (*eng->h_status != 0)
     return eng->fail(MS_E_DEVICE, "device status word " + std::to_string(*eng->h_status) +
                                       " (1 = bounded wait gave up, 2 = index out of range)");
-  if (out_tokens)
-    for (int i = 0; i < S; ++i) out_tokens[i] = uint32_t(eng->h_next[i]);
-  if (out_flags)
-    for (int i = 0; i < S; ++i) out_flags[i] = eng->last_flags[i];
+  for (int i = 0; i < S_in; ++i) {
+    const int p = eng->last_map[i];
+    const uint8_t f = eng->last_out_flags[i];
+    if (out_tokens) out_tokens[i] = (p < 0 || (f & MS_FLAG_NO_TOKEN)) ? 0u : uint32_t(eng->h_next[p]);
+    if (out_flags) out_flags[i] = f;
+  }
   return MS_OK;
 }
 

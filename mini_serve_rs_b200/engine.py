@@ -20,6 +20,7 @@ MS_DTYPE_F32, MS_DTYPE_BF16, MS_DTYPE_F16 = 0, 1, 2
 MS_STEP_TOKENS_FROM_DEVICE = 1
 MS_STEP_KEEP_LOGITS = 2
 MS_FLAG_PREFILLED = 1
+MS_FLAG_NO_TOKEN = 2
 
 
 class MsModelCfg(C.Structure):
@@ -40,7 +41,7 @@ class MsStepDesc(C.Structure):
     _fields_ = [("num_seqs", C.c_int32), ("seq_ids", C.POINTER(C.c_uint64)),
                 ("input_tokens", C.POINTER(C.c_uint32)), ("positions", C.POINTER(C.c_int32)),
                 ("flags", C.c_uint32), ("temperature", C.POINTER(C.c_float)), ("top_p", C.POINTER(C.c_float)),
-                ("seeds", C.POINTER(C.c_uint64))]
+                ("seeds", C.POINTER(C.c_uint64)), ("token_budget", C.c_int32)]
 
 
 class MsPagesStats(C.Structure):
@@ -280,7 +281,8 @@ class Engine:
         return v.value
 
     # -- step
-    def _desc(self, seq_ids, input_tokens, positions, flags, temperature=None, top_p=None, seeds=None):
+    def _desc(self, seq_ids, input_tokens, positions, flags, temperature=None, top_p=None, seeds=None,
+              token_budget=0):
         ids = np.ascontiguousarray(seq_ids, dtype=np.uint64)
         toks = None if input_tokens is None else np.ascontiguousarray(input_tokens, dtype=np.uint32)
         pos = None if positions is None else np.ascontiguousarray(positions, dtype=np.int32)
@@ -297,14 +299,16 @@ class Engine:
         fp = lambda a: None if a is None else a.ctypes.data_as(C.POINTER(C.c_float))
         d = MsStepDesc(n, ids.ctypes.data_as(C.POINTER(C.c_uint64)),
                        None if toks is None else _u32p(toks), None if pos is None else _i32p(pos), flags,
-                       fp(temp), fp(tp), None if sd is None else sd.ctypes.data_as(C.POINTER(C.c_uint64)))
+                       fp(temp), fp(tp), None if sd is None else sd.ctypes.data_as(C.POINTER(C.c_uint64)),
+                       int(token_budget))
         return d, (ids, toks, pos, temp, tp, sd)
 
     def step(self, seq_ids, input_tokens=None, positions=None, flags: int = 0, temperature=None, top_p=None,
-             seeds=None):
+             seeds=None, token_budget: int = 0):
         """One step; temperature / top_p / seeds (scalars or per-sequence) select
-        on-device sampling for rows with temperature >= 1e-7 (greedy otherwise)."""
-        d, keep = self._desc(seq_ids, input_tokens, positions, flags, temperature, top_p, seeds)
+        on-device sampling for rows with temperature >= 1e-7 (greedy otherwise);
+        token_budget > 0 chunks prefills (rows flagged MS_FLAG_NO_TOKEN)."""
+        d, keep = self._desc(seq_ids, input_tokens, positions, flags, temperature, top_p, seeds, token_budget)
         n = len(keep[0])
         rc = self.lib.ms_step(self.h, C.byref(d), _u32p(self._out_tok),
                               self._out_flags.ctypes.data_as(C.POINTER(C.c_uint8)))
@@ -312,8 +316,8 @@ class Engine:
         return self._out_tok[:n].copy(), self._out_flags[:n].copy()
 
     def step_launch(self, seq_ids, input_tokens=None, positions=None, flags: int = 0, temperature=None,
-                    top_p=None, seeds=None):
-        d, keep = self._desc(seq_ids, input_tokens, positions, flags, temperature, top_p, seeds)
+                    top_p=None, seeds=None, token_budget: int = 0):
+        d, keep = self._desc(seq_ids, input_tokens, positions, flags, temperature, top_p, seeds, token_budget)
         self._pending_n = len(keep[0])
         self._check(self.lib.ms_step_launch(self.h, C.byref(d)), "step_launch")
 
