@@ -48,6 +48,10 @@ def parse():
     ap.add_argument("--config5", action="store_true",
                     help="BASELINE config 5: Qwen2.5-7B arch, 256 seqs x ctx U[1024,32768], tensor parallel")
     ap.add_argument("--tp", type=int, default=2, help="tensor-parallel size for --config5")
+    ap.add_argument("--config4", action="store_true",
+                    help="BASELINE config 4: serving trace (1024 Poisson arrivals at 64 req/s), one replica per GPU")
+    ap.add_argument("--requests", type=int, default=1024, help="requests in the --config4 trace")
+    ap.add_argument("--token-budget", type=int, default=2048, help="packed tokens per step for --config4")
     ap.add_argument("--kernel", choices=["attention", "norm_rope", "sample"], default=None,
                     help="time one kernel in isolation (BASELINE config 2 for attention) instead of the step")
     return ap.parse_args()
@@ -387,6 +391,86 @@ def run_attention_kernel(args, local):
                       "peak_gbs": peak, "frac": gbs / peak, "peak_source": kind}), flush=True)
 
 
+def config4_trace(n_req: int, vocab: int, seed: int = 4):
+    """BASELINE config 4, seeded: Poisson arrivals at 64 req/s; prompt length
+    lognormal (median 512, sigma 1.0) clipped to [16, 8192]; output length
+    U[32, 1024]; 30 % of prompts are a shared 1024-token prefix + their own
+    suffix (total clipped to 8192); token ids U[0, V)."""
+    import numpy as np
+    from mini_serve_rs_b200.serving import Request
+    rng = np.random.Generator(np.random.PCG64(seed))
+    shared = rng.integers(0, vocab, 1024).tolist()
+    t = 0.0
+    reqs = []
+    for i in range(n_req):
+        t += float(rng.exponential(1.0 / 64.0))
+        n = int(np.clip(np.round(rng.lognormal(np.log(512.0), 1.0)), 16, 8192))
+        own = rng.integers(0, vocab, n).tolist()
+        prompt = (shared + own)[:8192] if rng.random() < 0.3 else own
+        reqs.append(Request(rid=i + 1, prompt=prompt, max_tokens=int(rng.integers(32, 1025)), arrival=t))
+    return reqs
+
+
+def run_config4(args, rank, world, local):
+    """One replica per GPU (one process each).  Requests go round-robin over
+    replicas, which is what the router's score (router.rs:23-30, (queue +
+    active + 1) x latency) gives for identical replicas under one trace.  Each
+    replica runs the continuous-batching loop (serving.ServingLoop) in real
+    time; rank 0 reports aggregate and per-GPU token rates and TTFT."""
+    import torch
+    import torch.distributed as dist
+    from mini_serve_rs_b200 import engine as E
+    from mini_serve_rs_b200.config import iter_random_device_weights, qwen3_0_6b
+    from mini_serve_rs_b200.serving import ServingLoop, summarize
+    torch.cuda.set_device(local)
+    cfg = qwen3_0_6b()
+    page_bytes = cfg.num_hidden_layers * 2 * cfg.num_key_value_heads * 16 * cfg.hd() * 2
+    pool_blocks = int(100e9 // page_bytes)
+    max_active = 256
+    eng = E.Engine(cfg, device=local, pool_blocks=pool_blocks, max_seqs=max_active,
+                   max_tokens_per_step=args.token_budget + max_active, max_blocks_per_seq=(8192 + 1024) // 16 + 1,
+                   dtype=E.MS_DTYPE_BF16)
+    eng.load_weights(iter_random_device_weights(cfg, SEED, device=f"cuda:{local}"))
+    pages = E.Pages(pool_blocks, 16, max_chunks=pool_blocks // 2)
+    reqs = [r for r in config4_trace(args.requests, cfg.vocab_size) if (r.rid - 1) % world == rank]
+    # warm-up: a few requests outside the trace (first-launch costs, library heuristics)
+    warm = ServingLoop(eng, pages, max_active, args.token_budget)
+    from mini_serve_rs_b200.serving import Request
+    warm.run([Request(rid=10_000_000 + k, prompt=list(range(100 + 37 * k)), max_tokens=8) for k in range(4)])
+    pages.close()
+    pages = E.Pages(pool_blocks, 16, max_chunks=pool_blocks // 2)
+    loop = ServingLoop(eng, pages, max_active, args.token_budget)
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        elapsed = loop.run(reqs, timeout_s=900.0)
+    summ = summarize(loop.finished, elapsed)
+    summ["steps"] = loop.steps
+    summ["prefix"] = pages.stats()
+    summ["clocks"] = clk.summary()
+    summ["gpu_launches"] = eng.profile()[0]
+    eng.close()
+    alls = [summ]
+    if world > 1:
+        alls = [None] * world
+        dist.all_gather_object(alls, summ)
+    if rank == 0:
+        tokens = sum(x["tokens"] for x in alls)
+        span = max(x["elapsed_s"] for x in alls)
+        agg = tokens / span
+        print(json.dumps({
+            "metric": "serving trace decode tokens/s (BASELINE config 4)", "value": agg, "unit": UNIT,
+            "n_gpus": world, "higher_is_better": True, "scaling": "weak", "dtype": "bf16",
+            "data": "synthetic seeded trace (random-init Qwen3-0.6B-arch weights)",
+            "config": {"workload": "BASELINE config 4", "requests": args.requests, "arrival_rate_per_s": 64,
+                       "prompt": "lognormal median 512 sigma 1.0 clipped [16,8192], 30% shared 1024-token prefix",
+                       "output": "uniform[32,1024]", "token_budget": args.token_budget, "max_active": max_active,
+                       "sampling": "greedy", "routing": "round-robin over replicas"},
+            "tokens_per_s_per_gpu": agg / world, "tokens": tokens, "elapsed_s": span,
+            "ttft_ms_p50": alls[0]["ttft_ms_p50"], "ttft_ms_p90": alls[0]["ttft_ms_p90"],
+            "ttft_ms_p99": alls[0]["ttft_ms_p99"], "per_rank": alls}), flush=True)
+
+
 def run_config5(args, rank, world, local):
     """BASELINE config 5 decode: Qwen2.5-7B architecture, tensor parallel by KV
     head over `--tp` GPUs per replica (world / tp replicas), 256 sequences per
@@ -622,6 +706,12 @@ def main():
         run_config5(args, rank, world, local)
         dist.barrier()
         dist.destroy_process_group()
+        return
+    if args.config4:
+        run_config4(args, rank, world, local)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
         return
     r = run_ours(args, rank, world, local)
     if rank == 0:

@@ -1,0 +1,176 @@
+"""Continuous-batching serving loop over the engine and the page manager.
+
+The caller side of the hot path, as the reference's Scheduler runs it
+(src/scheduler/scheduler.rs):
+* FIFO admission while there is room (:312-382).  A request that does not
+  get its pages (CachePressure) stays queued.
+* One ragged ms_step per iteration over every active request (:422-449).
+* Block growth before a step (:430-431).
+* Release when a request finishes (:555) or fails (:446).
+It also uses the B200 path's additions: pages from Pages (prefix-cache page
+sharing), prompts prefilled in chunks under a per-step token budget, and
+decode tokens fed back on the device.  Time is wall-clock; TTFT and
+per-request decode rate follow examples/bench.rs:85-108.
+"""
+from __future__ import annotations
+
+import time
+from collections import deque
+from dataclasses import dataclass, field
+from typing import Deque, Dict, List, Optional
+
+from . import engine as E
+
+
+@dataclass
+class Request:
+    rid: int
+    prompt: List[int]
+    max_tokens: int
+    arrival: float = 0.0          # seconds from the start of the trace
+    temperature: float = 0.0
+    top_p: float = 1.0
+    seed: int = 0
+    # filled in while serving
+    blocks: List[int] = field(default_factory=list)
+    cached: int = 0
+    prefilled: bool = False
+    out: List[int] = field(default_factory=list)
+    admitted_at: Optional[float] = None
+    first_token_at: Optional[float] = None
+    last_token_at: Optional[float] = None
+    done_at: Optional[float] = None
+    error: Optional[str] = None
+
+
+class ServingLoop:
+    def __init__(self, eng: E.Engine, pages: E.Pages, max_active: int = 256, token_budget: int = 2048,
+                 block_size: int = 16):
+        self.eng = eng
+        self.pages = pages
+        self.max_active = max_active
+        self.token_budget = token_budget
+        self.bs = block_size
+        self.queue: Deque[Request] = deque()
+        self.active: List[Request] = []
+        self.finished: List[Request] = []
+        self.steps = 0
+
+    def submit(self, r: Request):
+        self.queue.append(r)
+
+    def _admit(self, now: float):
+        while self.queue and self.queue[0].arrival <= now and len(self.active) < self.max_active:
+            r = self.queue[0]
+            try:
+                r.blocks, r.cached = self.pages.admit(r.rid, r.prompt)
+            except E.CachePressure:
+                break
+            try:
+                self.eng.admit(r.rid, r.prompt, r.blocks, num_cached=r.cached)
+            except E.EngineError as e:
+                self.pages.release(r.rid)
+                self.queue.popleft()
+                r.error = str(e)
+                self.finished.append(r)
+                continue
+            r.admitted_at = now
+            self.queue.popleft()
+            self.active.append(r)
+
+    def _finish(self, r: Request, now: float, error: Optional[str] = None):
+        self.eng.release(r.rid)
+        self.pages.release(r.rid)
+        r.done_at = now
+        r.error = error
+        self.finished.append(r)
+
+    def _grow(self, now: float):
+        failed = []
+        for r in self.active:
+            c = self.eng.cached_tokens(r.rid)
+            if r.prefilled:
+                reach = c + 1
+            else:
+                rem = len(r.prompt) - c
+                reach = c + (min(rem, self.token_budget) if self.token_budget else rem)
+            try:
+                while len(r.blocks) * self.bs < reach:
+                    b = self.pages.allocate_block(r.rid)
+                    r.blocks.append(b)
+                    self.eng.append_block(r.rid, b)
+            except E.CachePressure as e:
+                failed.append((r, str(e)))
+        for r, msg in failed:  # scheduler.rs:430-446: the request fails
+            self.active.remove(r)
+            self._finish(r, now, msg)
+
+    def step(self, now: float) -> bool:
+        """One iteration at trace time `now`; False when there was nothing to run."""
+        self._admit(now)
+        if not self.active:
+            return False
+        self._grow(now)
+        if not self.active:
+            return False
+        ids = [r.rid for r in self.active]
+        temps = [r.temperature for r in self.active]
+        need_sampling = any(t >= 1e-7 for t in temps)
+        toks, flags = self.eng.step(
+            ids, flags=E.MS_STEP_TOKENS_FROM_DEVICE, token_budget=self.token_budget,
+            temperature=temps if need_sampling else None,
+            top_p=[r.top_p for r in self.active] if need_sampling else None,
+            seeds=[(r.seed << 20) + len(r.out) for r in self.active] if need_sampling else None)
+        self.steps += 1
+        t = self.clock()
+        done = []
+        for r, tok, f in zip(self.active, toks, flags):
+            if f & E.MS_FLAG_NO_TOKEN:
+                continue
+            if f & E.MS_FLAG_PREFILLED:
+                r.prefilled = True
+                r.first_token_at = t
+                self.pages.publish(r.rid, r.prompt)
+            r.out.append(int(tok))
+            r.last_token_at = t
+            if len(r.out) >= r.max_tokens:
+                done.append(r)
+        for r in done:
+            self.active.remove(r)
+            self._finish(r, t)
+        return True
+
+    # trace clock: seconds since run() started
+    def clock(self) -> float:
+        return time.perf_counter() - self._t0
+
+    def run(self, requests: List[Request], timeout_s: float = 600.0) -> float:
+        """Serve a trace in real time; returns the elapsed seconds."""
+        for r in sorted(requests, key=lambda r: r.arrival):
+            self.submit(r)
+        self._t0 = time.perf_counter()
+        while self.queue or self.active:
+            now = self.clock()
+            if now > timeout_s:
+                raise TimeoutError("trace did not finish")
+            if not self.step(now):
+                nxt = self.queue[0].arrival if self.queue else now
+                time.sleep(max(0.0, min(nxt - now, 0.01)))
+        return self.clock()
+
+
+def summarize(reqs: List[Request], elapsed: float) -> Dict[str, float]:
+    """Aggregate tokens/s and TTFT percentiles (examples/bench.rs:85-108, 189)."""
+    ok = [r for r in reqs if r.error is None]
+    tokens = sum(len(r.out) for r in ok)
+    ttft = sorted((r.first_token_at - r.arrival) * 1000.0 for r in ok if r.first_token_at is not None)
+    dec = [(len(r.out) - 1) / (r.last_token_at - r.first_token_at) for r in ok
+           if len(r.out) > 1 and r.last_token_at > r.first_token_at]
+
+    def pct(v, q):
+        return v[min(len(v) - 1, int(q * len(v)))] if v else float("nan")
+
+    return {"requests": len(reqs), "failed": len(reqs) - len(ok), "tokens": tokens, "elapsed_s": elapsed,
+            "aggregate_tokens_per_s": tokens / elapsed if elapsed > 0 else 0.0,
+            "ttft_ms_p50": pct(ttft, 0.5), "ttft_ms_p90": pct(ttft, 0.9), "ttft_ms_p99": pct(ttft, 0.99),
+            "per_request_decode_tokens_per_s_median": pct(sorted(dec), 0.5)}
