@@ -311,7 +311,7 @@ def run_decode(args, rank, world, local, cfg, ctx, seed, tp_rank=0, tp_size=1, c
         "ms": ms, "ms_e2e": ms_e2e, "gpu_launches": gpu_launches, "clocks": clk.summary(),
         "attn_launches": alaunch, "attn_ms": attn_ms, "attn_bytes": attn_bytes,
         "h2d": (4 + 7 * B) * 4, "d2h": B * 4 + 4, "ctx_mean": float(np.mean(ctx)),
-        "graphs": {"captured": graphs[0], "replayed": graphs[1]}, "kp": KP,
+        "graphs": {"captured": graphs[0], "replayed": graphs[1]}, "kp": KP, "tp_fused": eng.tp_fused(),
         "memory": eng.memory(),
     }
     eng.close()
@@ -516,6 +516,8 @@ def run_config5(args, rank, world, local):
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({kind})", "ms_per_launch": per_launch_ms,
                          "share_of_step": (r["attn_ms"] / r["kp"]) / (r["ms"] / args.steps)},
+            "tp_allreduce": ("fused peer-memory all-reduce + residual add + RMSNorm (NVLink, CUDA IPC)"
+                             if r["tp_fused"] else "NCCL all-reduce + K4"),
             "cuda_graphs": r["graphs"], "memory_bytes": r["memory"]}), flush=True)
 
 

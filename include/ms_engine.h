@@ -270,6 +270,13 @@ int ms_engine_profile(ms_engine *eng, int64_t *kernel_launches, int64_t *attn_la
 int ms_engine_set_graphs(ms_engine *eng, int32_t on);
 int ms_engine_graph_stats(const ms_engine *eng, int64_t *captures, int64_t *replays, int32_t *cached);
 
+/* Tensor parallelism: *fused = 1 when the all-reduces after o_proj and
+ * down_proj run as one peer-memory kernel fused with the residual add and
+ * RMSNorm (NVLink, CUDA IPC mappings set up at creation), 0 when they go
+ * through NCCL (tp_size 1, MS_TP_FUSED=0, or a rank that could not map its
+ * peers -- all ranks then agree on NCCL).  No reference counterpart. */
+int ms_engine_tp_fused(const ms_engine *eng, int32_t *fused);
+
 /* ---- health (traits.rs:175-180, candle.rs:324-335) --------------------- */
 int ms_is_healthy(const ms_engine *eng);
 int ms_mark_unhealthy(ms_engine *eng);

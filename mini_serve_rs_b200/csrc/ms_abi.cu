@@ -199,6 +199,12 @@ extern "C" int ms_engine_set_profiling(ms_engine *eng, int32_t on) {
   return MS_OK;
 }
 
+extern "C" int ms_engine_tp_fused(const ms_engine *eng, int32_t *fused) {
+  if (!eng || !fused) return MS_E_INVALID;
+  *fused = eng->ar_fused ? 1 : 0;
+  return MS_OK;
+}
+
 extern "C" int ms_engine_set_graphs(ms_engine *eng, int32_t on) {
   if (!eng) return MS_E_INVALID;
   if (eng->pending) return eng->fail(MS_E_INVALID, "ms_engine_set_graphs between launch and wait");

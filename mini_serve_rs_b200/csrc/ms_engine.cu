@@ -262,6 +262,10 @@ int create_impl(const ms_model_cfg *cfg, const ms_engine_opts *opts, Engine *eng
   // the memsets and table uploads above ran on the legacy stream; the engine
   // stream is non-blocking, so finish them before any step can be enqueued
   MS_CUDA_TRY(cudaDeviceSynchronize());
+  if (eng->tp > 1) {
+    const int rc = tp_fused_setup(eng);
+    if (rc != MS_OK) return rc;
+  }
   return MS_OK;
 }
 
@@ -270,6 +274,7 @@ void destroy_impl(Engine *eng) {
   cudaSetDevice(eng->dev);
   if (eng->stream) cudaStreamSynchronize(eng->stream);
   eng->drop_graphs();
+  tp_fused_teardown(eng);
   if (eng->blas) cublasDestroy(eng->blas);
   for (void *p : {eng->blas_ws, eng->wbuf, eng->cos_t, eng->sin_t, eng->pool, (void *)eng->d_block_tables,
                   (void *)eng->d_slot_last, (void *)eng->d_status, eng->sbuf, (void *)eng->d_in, (void *)eng->d_gin})

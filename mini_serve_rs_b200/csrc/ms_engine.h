@@ -116,6 +116,15 @@ struct Engine {
     graph_warm.clear();
   }
 
+  // tensor parallelism: peer-mapped partial-sum buffers for the fused
+  // all-reduce + residual add + RMSNorm (ms_tp_allreduce.cu)
+  bool ar_fused = false;
+  void *ar_sym = nullptr;               // own allocation: 2 partial-sum buffers + signal array
+  void *ar_buf[2][8] = {};              // [buffer][rank]
+  uint32_t *ar_sig[8] = {};             // each rank's signal array
+  std::vector<void *> ar_peer_maps;     // IPC mappings to close
+  uint32_t ar_epoch = 0;
+
   // instrumentation
   int64_t kernel_launches = 0;
   int64_t last_launches = 0;  // kernels enqueued by the last enqueue_forward
@@ -199,6 +208,10 @@ inline size_t graph_in_elems(int max_seqs) { return 4 + size_t(11) * max_seqs; }
 // eager and the graph path, so both produce identical results).
 int decode_partition(const Engine *eng, const StepPlan &plan, int max_ctx);
 int enqueue_forward(Engine *eng, const StepPlan &plan);
+int tp_fused_setup(Engine *eng);
+void tp_fused_teardown(Engine *eng);
+cudaError_t launch_ar_add_rmsnorm(Engine *eng, int which, const void *residual, const int32_t *row_index,
+                                  const void *w, void *resid_out, void *norm_out, int rows, cudaStream_t st);
 int step_wait_impl(Engine *eng, uint32_t *out_tokens, uint8_t *out_flags);
 
 }  // namespace ms

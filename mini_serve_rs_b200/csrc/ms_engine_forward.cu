@@ -180,14 +180,29 @@ int enqueue_forward(Engine *eng, const StepPlan &plan) {
       MS_CUDA_TRY(launch_paged_prefill(pf, st));
     }
     // o_proj, residual add + post-attention norm
-    MS_BLAS_TRY(linear(eng, w.w_o, eng->attn, eng->x_tmp, eng->H, T, eng->hq * eng->D));
-    if (eng->tp > 1 && nccl_allreduce_sum(eng->x_tmp, size_t(T) * eng->H, dt, eng->comm, st) != 0)
-      return eng->fail(MS_E_DEVICE, "NCCL all-reduce after o_proj failed");
-    MS_CUDA_TRY(launch_add_rmsnorm(eng->x_tmp, eng->x_resid, nullptr, w.ln2, eng->x_resid, eng->x_norm, T, eng->H,
-                                   eps, dt, st));
+    if (eng->ar_fused) {  // partial sums into the peer-mapped buffer, then sum + add + norm in one kernel
+      MS_BLAS_TRY(linear(eng, w.w_o, eng->attn, eng->ar_buf[0][eng->rank], eng->H, T, eng->hq * eng->D));
+      MS_CUDA_TRY(launch_ar_add_rmsnorm(eng, 0, eng->x_resid, nullptr, w.ln2, eng->x_resid, eng->x_norm, T, st));
+    } else {
+      MS_BLAS_TRY(linear(eng, w.w_o, eng->attn, eng->x_tmp, eng->H, T, eng->hq * eng->D));
+      if (eng->tp > 1 && nccl_allreduce_sum(eng->x_tmp, size_t(T) * eng->H, dt, eng->comm, st) != 0)
+        return eng->fail(MS_E_DEVICE, "NCCL all-reduce after o_proj failed");
+      MS_CUDA_TRY(launch_add_rmsnorm(eng->x_tmp, eng->x_resid, nullptr, w.ln2, eng->x_resid, eng->x_norm, T,
+                                     eng->H, eps, dt, st));
+    }
     // MLP
     MS_BLAS_TRY(linear(eng, w.w_gu, eng->x_norm, eng->gu, 2 * eng->I, T, eng->H));
     MS_CUDA_TRY(launch_silu_mul(eng->gu, eng->act, T, eng->I, dt, st));
+    if (eng->ar_fused) {
+      MS_BLAS_TRY(linear(eng, w.w_down, eng->act, eng->ar_buf[1][eng->rank], eng->H, T, eng->I));
+      if (l + 1 < eng->L)
+        MS_CUDA_TRY(launch_ar_add_rmsnorm(eng, 1, eng->x_resid, nullptr, eng->layers[l + 1].ln1, eng->x_resid,
+                                          eng->x_norm, T, st));
+      else  // final norm on each sequence's last row only
+        MS_CUDA_TRY(launch_ar_add_rmsnorm(eng, 1, eng->x_resid, eng->d_last_index, eng->final_norm, nullptr,
+                                          eng->last_norm, S, st));
+      continue;
+    }
     MS_BLAS_TRY(linear(eng, w.w_down, eng->act, eng->x_tmp, eng->H, T, eng->I));
     if (eng->tp > 1 && nccl_allreduce_sum(eng->x_tmp, size_t(T) * eng->H, dt, eng->comm, st) != 0)
       return eng->fail(MS_E_DEVICE, "NCCL all-reduce after down_proj failed");

@@ -118,6 +118,8 @@ cudaError_t launch_convert(const void *src, int src_dtype, void *dst, int dst_dt
 // NCCL, resolved at run time (ms_nccl.cu)
 bool nccl_available();
 int nccl_allreduce_sum(void *buf, size_t count, int dtype, void *comm, cudaStream_t stream);
+int nccl_allgather_bytes(void *buf, size_t bytes, int rank, void *comm, cudaStream_t stream);
+int nccl_allreduce_min_i32(int32_t *buf, void *comm, cudaStream_t stream);
 int nccl_async_error(void *comm);
 void nccl_abort(void *comm);
 

@@ -22,6 +22,7 @@ struct NcclApi {
   ncclResult_t (*async_error)(ncclComm_t, ncclResult_t *) = nullptr;
   ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                              cudaStream_t) = nullptr;
+  ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   bool ok = false;
 };
 
@@ -40,7 +41,9 @@ const NcclApi &api() {
     a.comm_abort = reinterpret_cast<decltype(a.comm_abort)>(dlsym(h, "ncclCommAbort"));
     a.async_error = reinterpret_cast<decltype(a.async_error)>(dlsym(h, "ncclCommGetAsyncError"));
     a.all_reduce = reinterpret_cast<decltype(a.all_reduce)>(dlsym(h, "ncclAllReduce"));
-    a.ok = a.get_unique_id && a.comm_init_rank && a.comm_destroy && a.comm_abort && a.async_error && a.all_reduce;
+    a.all_gather = reinterpret_cast<decltype(a.all_gather)>(dlsym(h, "ncclAllGather"));
+    a.ok = a.get_unique_id && a.comm_init_rank && a.comm_destroy && a.comm_abort && a.async_error && a.all_reduce &&
+           a.all_gather;
   });
   return a;
 }
@@ -54,6 +57,19 @@ int nccl_allreduce_sum(void *buf, size_t count, int dtype, void *comm, cudaStrea
   if (!api().ok) return -1;
   const ncclDataType_t t = dtype == MS_DTYPE_F32 ? ncclFloat32 : dtype == MS_DTYPE_BF16 ? ncclBfloat16 : ncclFloat16;
   return int(api().all_reduce(buf, buf, count, t, ncclSum, static_cast<ncclComm_t>(comm), stream));
+}
+
+// In-place all-gather of `bytes` per rank: rank r's part sits at buf + r * bytes.
+int nccl_allgather_bytes(void *buf, size_t bytes, int rank, void *comm, cudaStream_t stream) {
+  if (!api().ok) return -1;
+  return int(api().all_gather(static_cast<char *>(buf) + size_t(rank) * bytes, buf, bytes, ncclUint8,
+                              static_cast<ncclComm_t>(comm), stream));
+}
+
+// Minimum over ranks of one int32 in device memory, in place.
+int nccl_allreduce_min_i32(int32_t *buf, void *comm, cudaStream_t stream) {
+  if (!api().ok) return -1;
+  return int(api().all_reduce(buf, buf, 1, ncclInt32, ncclMin, static_cast<ncclComm_t>(comm), stream));
 }
 
 // 0 = healthy, otherwise the communicator's asynchronous error code.

@@ -69,6 +69,7 @@ _SIGS = {
     "ms_engine_profile": ([_P, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(C.c_double),
                            C.POINTER(C.c_double)], C.c_int),
     "ms_engine_set_graphs": ([_P, _I32], C.c_int),
+    "ms_engine_tp_fused": ([_P, C.POINTER(_I32)], C.c_int),
     "ms_engine_graph_stats": ([_P, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(_I32)], C.c_int),
     "ms_nccl_get_unique_id": ([C.c_char_p, _I32], C.c_int),
     "ms_nccl_comm_init": ([C.POINTER(_P), _I32, C.c_char_p, _I32, _I32], C.c_int),
@@ -342,6 +343,12 @@ class Engine:
         self._check(self.lib.ms_engine_profile(self.h, C.byref(kl), C.byref(al), C.byref(ms), C.byref(by)),
                     "profile")
         return kl.value, al.value, ms.value, by.value
+
+    def tp_fused(self) -> bool:
+        """True when TP all-reduces run as the fused peer-memory kernel."""
+        v = _I32()
+        self._check(self.lib.ms_engine_tp_fused(self.h, C.byref(v)), "tp_fused")
+        return bool(v.value)
 
     def set_graphs(self, on: bool):
         """Replay pure-decode steps from captured CUDA graphs (default on)."""

@@ -1,4 +1,6 @@
-"""Tensor parallelism (KV-head sharding + NCCL all-reduce) on two GPUs.
+"""Tensor parallelism (KV-head sharding; the all-reduce after o_proj and
+down_proj either fused with the residual add + RMSNorm over NVLink peer
+memory -- the default -- or through NCCL) on two GPUs.
 
 Each of two spawned processes drives one engine (tp_size 2) on its own GPU;
 both must reproduce the transformers goldens of the single-GPU tests (logits
@@ -16,9 +18,10 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 
-def _rank_main(rank, world, uid, case_idx, q):
+def _rank_main(rank, world, uid, case_idx, q, fused=True):
     try:
         os.environ.setdefault("MS_STEP_TIMEOUT_S", "60")
+        os.environ["MS_TP_FUSED"] = "1" if fused else "0"
         torch.cuda.set_device(rank)
         from mini_serve_rs_b200 import engine as E
         from oracle.qwen_ref import random_weights
@@ -30,6 +33,8 @@ def _rank_main(rank, world, uid, case_idx, q):
         eng = E.Engine(cfg, device=rank, pool_blocks=256, max_seqs=8, max_tokens_per_step=512,
                        max_blocks_per_seq=64, dtype=E.MS_DTYPE_F32, tp_rank=rank, tp_size=world, nccl_comm=comm)
         eng.load_weights(random_weights(cfg, case["seed"], norm_std=case.get("norm_std", 0.0)))
+        if eng.tp_fused() != fused:
+            raise RuntimeError(f"tp_fused() = {eng.tp_fused()}, wanted {fused}")
         g = golden()
         prompts = case["prompts"]
         ids = list(range(1, len(prompts) + 1))
@@ -59,15 +64,16 @@ def _rank_main(rank, world, uid, case_idx, q):
         q.put((rank, None, None, repr(e)))
 
 
-@pytest.mark.parametrize("case_idx", [1, 2], ids=["qwen3_small", "qwen2_small"])
-def test_tp2_matches_transformers_goldens(case_idx):
+@pytest.mark.parametrize("case_idx,fused", [(1, True), (2, True), (1, False)],
+                         ids=["qwen3_small-fused", "qwen2_small-fused", "qwen3_small-nccl"])
+def test_tp2_matches_transformers_goldens(case_idx, fused):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     from mini_serve_rs_b200 import engine as E
     uid = E.nccl_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, uid, case_idx, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, uid, case_idx, q, fused)) for r in range(2)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in procs]
