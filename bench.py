@@ -52,6 +52,7 @@ def parse():
                     help="BASELINE config 4: serving trace (1024 Poisson arrivals at 64 req/s), one replica per GPU")
     ap.add_argument("--requests", type=int, default=1024, help="requests in the --config4 trace")
     ap.add_argument("--token-budget", type=int, default=2048, help="packed tokens per step for --config4")
+    ap.add_argument("--max-active", type=int, default=512, help="concurrent requests per replica for --config4")
     ap.add_argument("--kernel", choices=["attention", "norm_rope", "sample"], default=None,
                     help="time one kernel in isolation (BASELINE config 2 for attention) instead of the step")
     return ap.parse_args()
@@ -426,7 +427,7 @@ def run_config4(args, rank, world, local):
     cfg = qwen3_0_6b()
     page_bytes = cfg.num_hidden_layers * 2 * cfg.num_key_value_heads * 16 * cfg.hd() * 2
     pool_blocks = int(100e9 // page_bytes)
-    max_active = 256
+    max_active = args.max_active
     eng = E.Engine(cfg, device=local, pool_blocks=pool_blocks, max_seqs=max_active,
                    max_tokens_per_step=args.token_budget + max_active, max_blocks_per_seq=(8192 + 1024) // 16 + 1,
                    dtype=E.MS_DTYPE_BF16)
