@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--requests", type=int, default=1024, help="requests in the --config4 trace")
     ap.add_argument("--token-budget", type=int, default=2048, help="packed tokens per step for --config4")
     ap.add_argument("--max-active", type=int, default=512, help="concurrent requests per replica for --config4")
-    ap.add_argument("--kernel", choices=["attention", "norm_rope", "sample"], default=None,
+    ap.add_argument("--kernel", choices=["attention", "norm_rope", "sample", "prefill"], default=None,
                     help="time one kernel in isolation (BASELINE config 2 for attention) instead of the step")
     return ap.parse_args()
 
@@ -651,6 +651,68 @@ def run_sample_kernel(args, local):
                       "ms_argmax": amax}), flush=True)
 
 
+def run_prefill_kernel(args, local, seqs: int = 4, length: int = 4096):
+    """K3p causal prefill attention over the paged pool: `seqs` prompts of
+    `length` tokens from position 0 (Qwen3-0.6B heads: 16 q / 8 kv x 128,
+    bf16), packed as one ragged batch.  Algorithmic FLOPs = sum over tokens of
+    4 * Hq * D * (keys attended) (QK^T and PV, causal).  Median of K launches,
+    CUDA events; compared with the measured dense bf16 peak."""
+    import ctypes as C
+    import numpy as np
+    import torch
+    from mini_serve_rs_b200 import engine as E
+    torch.cuda.set_device(local)
+    dev = f"cuda:{local}"
+    lib = E.lib()
+    hq, hkv, D = 16, 8, 128
+    T = seqs * length
+    pages = T // 16
+    g = torch.Generator(device=dev).manual_seed(9)
+    kp = torch.randn(pages, hkv, 16, D, generator=g, device=dev).to(torch.bfloat16)
+    vp = torch.randn(pages, hkv, 16, D, generator=g, device=dev).to(torch.bfloat16)
+    q = torch.randn(T, hq, D, generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    mbps = length // 16
+    tables = torch.arange(pages, dtype=torch.int32, device=dev).reshape(seqs, mbps)
+    row0 = np.arange(seqs, dtype=np.int32) * length
+    ntok = np.full(seqs, length, np.int32)
+    start = np.zeros(seqs, np.int32)
+    trow = np.arange(seqs, dtype=np.int32)
+    cap = T
+    tiles = np.zeros(4 * cap, np.int32)
+    ip = lambda a: a.ctypes.data_as(C.POINTER(C.c_int32))
+    nt = lib.ms_prefill_tiles(ip(row0), ip(ntok), ip(start), ip(trow), seqs, hq, hkv, ip(tiles), cap)
+    assert nt > 0
+    tiles_d = torch.from_numpy(tiles[:4 * nt].copy()).to(dev)
+    st = torch.cuda.current_stream()
+    P = lambda t: C.c_void_p(t.data_ptr())
+
+    def launch():
+        rc = lib.ms_launch_paged_prefill(P(q), P(kp), P(vp), P(tables), mbps, P(tiles_d), nt, P(out), hq, hkv, D, 16,
+                                         1.0 / (D ** 0.5), E.MS_DTYPE_BF16, C.c_void_p(st.cuda_stream))
+        assert rc == 0
+
+    for _ in range(args.warmup):
+        launch()
+    ts = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        launch()
+        e1.record(st)
+        e1.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    ts.sort()
+    ms = ts[len(ts) // 2]
+    flops = seqs * 4.0 * hq * D * (length * (length + 1) / 2)
+    peaks_d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak = float(peaks_d.get("bf16_tflops", 1590.0))
+    tf = flops / (ms / 1000.0) / 1e12
+    print(json.dumps({"workload": f"{seqs} prompts x {length} tokens, causal, 16/8 heads x 128, bf16",
+                      "tiles": nt, "ms": ms, "tflops": tf, "peak_tflops": peak, "frac": tf / peak,
+                      "peak_source": "MEASURED_PEAKS.json bf16_tflops" if peaks_d else "fallback"}), flush=True)
+
+
 def traffic_per_launch(algorithmic_bytes: float):
     """dram bytes (read + write) per attention launch: the committed ncu ratio of
     dram bytes to algorithmic bytes (profiles/k3_attention_traffic.json, from a
@@ -682,6 +744,9 @@ def main():
         return
     if args.kernel == "sample":
         run_sample_kernel(args, local)
+        return
+    if args.kernel == "prefill":
+        run_prefill_kernel(args, local)
         return
 
     if args.impl == "reference":
