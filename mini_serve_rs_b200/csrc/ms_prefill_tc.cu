@@ -280,9 +280,17 @@ cudaError_t prefill_group(const PrefillParams &p, const CUtensorMap &km, const C
 
 }  // namespace
 __device__ unsigned g_prefill_status;
+// tcgen05 build (ms_prefill_tc5.cu)
+bool prefill_tc5_enabled();
+int prefill_tc5_tokens_per_tile(int group);
+cudaError_t launch_prefill_tc5(const void *q, void *out, const int32_t *block_tables, int max_blocks_per_seq,
+                               const int32_t *tiles, int num_tiles, int num_kv_heads, int group, int head_dim,
+                               float scale, unsigned *status, int dtype, const CUtensorMap &km, const CUtensorMap &vm,
+                               cudaStream_t stream);
 }  // namespace attn
 
 int prefill_tokens_per_tile(int group) {
+  if (attn::prefill_tc5_enabled()) return attn::prefill_tc5_tokens_per_tile(group);
   const int rpt = group <= 1 ? 1 : group <= 2 ? 2 : group <= 4 ? 4 : 8;
   return attn::kWarps * (16 / rpt);
 }
@@ -315,6 +323,9 @@ cudaError_t launch_paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     p.status = static_cast<unsigned *>(sp);
   }
+  if (attn::prefill_tc5_enabled())
+    return attn::launch_prefill_tc5(a.q, a.out, a.block_tables, a.max_blocks_per_seq, a.tiles, a.num_tiles,
+                                    a.num_kv_heads, group, a.head_dim, a.scale, p.status, a.dtype, km, vm, stream);
   if (a.dtype == MS_DTYPE_BF16) {
     return a.head_dim == 128 ? attn::prefill_group<__nv_bfloat16, 128>(p, km, vm, group, a.num_tiles, stream)
                              : attn::prefill_group<__nv_bfloat16, 64>(p, km, vm, group, a.num_tiles, stream);
