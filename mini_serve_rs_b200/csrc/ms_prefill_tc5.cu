@@ -5,33 +5,35 @@
 // of Attention::forward, src/backends/qwen2.rs:329-345, causal mask of
 // :476-503 incl. the offset columns of a cached prefix), but a CTA takes 128
 // query rows: TPB = 128 / RPT tokens x the G query heads of one KV head
-// (RPT = G rounded up to 1, 2, 4 or 8; padding rows are masked).  Thread t
-// owns row t, which is TMEM lane t, so the softmax needs no shuffles.
+// (RPT = G rounded up to 1, 2, 4 or 8; padding rows are computed like the
+// tile's first row and not stored).  Softmax thread t owns row t, which is
+// TMEM lane t, so the softmax needs no shuffles.
 //
-// Per group of 64 keys (4 pages of the sequence, landed by TMA in one of two
-// stages, 128-byte swizzle):
-//   1. thread 0 issues S = Q K^T: D/16 tcgen05.mma (M 128, N 64, K 16) with Q
-//      and K read from shared memory through K-major descriptors, S in TMEM
-//      columns [0, 64); tcgen05.commit -> mbarrier;
-//   2. every thread tcgen05.ld's its row of S, masks (key <= its position),
-//      and runs the online softmax in base 2.  The running max is only moved
-//      when the tile's max exceeds it by more than 8 (then O and l are
-//      rescaled: tcgen05.ld / st of the row), so P = 2^(s - m) stays <= 256;
-//   3. P (rounded to the K/V type) overwrites the group's K tile -- the S MMA
-//      has consumed it -- in the K-major swizzled layout, V rows of keys past
-//      the sequence are zeroed, fence.proxy.async, CTA barrier;
-//   4. thread 0 issues O += P V: 4 tcgen05.mma (M 128, N D, K 16) with V as an
-//      MN-major operand, O in TMEM columns [64, 64 + D).
-// The next group's S MMA is issued after this PV MMA by the same thread, so
-// its completion implies the PV finished: the stage it used is then refilled
-// two groups ahead.  At the end each thread loads its O row, divides by l and
-// stores it.  Shared memory: Q (128 x D) + 2 stages of K/P and V (64 keys x D)
-// = 96 KiB for D = 128, so two CTAs share an SM and overlap one CTA's softmax
-// with the other's MMAs; TMEM: 256 columns per CTA (128 for D = 64).
+// Keys go in groups of 64 (4 pages).  The CTA has three roles that meet only
+// at mbarriers:
+//   * warps 0-3, softmax: for group g, wait until S(g) is in TMEM, tcgen05.ld
+//     the row, mask causally (only groups that reach past the tile's first
+//     position), and run the online softmax in base 2 with the scale folded
+//     into one FMA before ex2.  The running max moves only when the group's
+//     max exceeds it by more than 8 (then the warp rescales its O rows in
+//     TMEM after the previous PV finished), so P = 2^(s - m) stays <= 256.
+//     P, rounded to the K/V type, is stored back over S(g)'s own TMEM columns
+//     (two 16-bit values per column) and the warp arrives on p_ready;
+//   * warp 4, one thread, MMAs in the order S0 S1 PV0 S2 PV1 ... : S(g) = Q
+//     K(g)^T (D/16 MMAs, M 128, N 64, K-major Q and K from shared memory)
+//     into S buffer g & 1, so S(g+1) runs while the softmax works on S(g);
+//     O += P(g) V(g) (4 MMAs, M 128, N D, A = P read from TMEM, V an MN-major
+//     operand).  MMAs of one thread run in order, so S(g+2) overwrites the
+//     buffer only after PV(g) read P(g) from it;
+//   * warp 5, one thread, TMA: the K and V tiles (16 KB each for D = 128) in
+//     the order the MMAs consume them, through a ring of shared-memory slots
+//     freed by tcgen05.commit of the consuming MMA.
+// Shared memory: Q (128 x D) + 4 slots = 96 KiB for D = 128, so two CTAs
+// share an SM; TMEM: 256 columns per CTA (S0, S1, O).
 //
-// Every wait is bounded (mbarrier polls); on expiry the CTA records
-// kStatusWaitTimeout, drains its copies and MMAs (bounded), frees TMEM and
-// returns.
+// Every wait is bounded (mbarrier polls that also watch a CTA abort flag);
+// on expiry the CTA records kStatusWaitTimeout, drains its MMAs and copies
+// (bounded), frees TMEM and returns.
 #include <algorithm>
 #include <cstdlib>
 #include <mutex>
@@ -134,50 +136,106 @@ struct Prefill5Params {
   float qscale;
 };
 
+template <int D> struct Ring5 {
+  static constexpr int kHalf = kKeys * 128;                 // 64 keys x 64 dims (one 128-byte row per key)
+  static constexpr int kTile = (D / 64) * kHalf;            // one K or V tile
+  static constexpr int kSlots = D == 128 ? 4 : 8;
+  static constexpr int kSmem = 1024 + (D / 64) * kRows * 128 + kSlots * kTile;  // + alignment slack
+};
+
+// Tile i of the ring order K0 K1 V0 K2 V1 ... K(n-1) V(n-2) V(n-1) (the order
+// the MMA thread consumes them); returns the group, sets is_v.
+__device__ __forceinline__ int ring_tile(int i, int n, bool &is_v) {
+  if (i == 0) { is_v = false; return 0; }
+  if (i == 2 * n - 1) { is_v = true; return n - 1; }
+  if (i & 1) { is_v = false; return (i + 1) >> 1; }
+  is_v = true;
+  return (i - 2) >> 1;
+}
+
+// Bounded mbarrier wait that gives up early once another role set `abort`.
+__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort) {
+  for (int i = 0; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 63 && *abort) return false;
+  }
+  return false;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// O (TMEM, M 128 x N) += P (TMEM, 128 x 16, two values per column) * B (shared-memory descriptor)
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+}
+__device__ __forceinline__ void tmem_st32u(uint32_t addr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(addr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+constexpr int kThreads5 = 192;  // 4 softmax warps, the MMA warp, the TMA warp
+
 template <typename T, int D, int G>
-__global__ void __launch_bounds__(kRows) paged_prefill_tc5_kernel(const __grid_constant__ CUtensorMap kmap,
-                                                                  const __grid_constant__ CUtensorMap vmap,
-                                                                  Prefill5Params p) {
+__global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                                         const __grid_constant__ CUtensorMap vmap,
+                                                                         Prefill5Params p) {
   constexpr int RPT = RowsPerTok5<G>::value;
-  constexpr int NDH = D / 64;                          // 64-dim (128-byte) halves
-  constexpr int QHALF = kRows * 128;                   // one 64-dim half of the Q tile
-  constexpr int KVHALF = kKeys * 128;                  // one 64-dim half of a 64-key K or V tile
-  constexpr int KV_BYTES = NDH * KVHALF;
-  constexpr int KP_BYTES = KV_BYTES > kRows * 128 ? KV_BYTES : kRows * 128;  // K tile, then P (128 x 64 keys)
-  constexpr int STAGE_BYTES = KP_BYTES + KV_BYTES;     // K/P tile, V tile
-  constexpr int PAGE_HALF = kBS * 128;                 // one TMA box: 16 keys x 64 dims
-  constexpr int TMEM_COLS = kKeys + D <= 128 ? 128 : 256;  // S, then O
+  constexpr int NDH = D / 64;          // 64-dim (128-byte) halves
+  constexpr int QHALF = kRows * 128;   // one 64-dim half of the Q tile
+  constexpr int HALF = Ring5<D>::kHalf, TILE = Ring5<D>::kTile, NSLOT = Ring5<D>::kSlots;
+  constexpr int PAGE_HALF = kBS * 128; // one TMA box: 16 keys x 64 dims
+  constexpr int TMEM_COLS = 256;       // S0 [0, 64), S1 [64, 128), O [128, 128 + D)
 
   extern __shared__ unsigned char smem_dyn[];
   unsigned char *smem =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-  unsigned char *sq = smem;                            // Q: NDH halves of 128 rows x 128 B
-  unsigned char *stages = smem + NDH * QHALF;
-  __shared__ uint64_t full[2], s_done, o_done, drain;
+  unsigned char *sq = smem;  // Q: NDH halves of 128 rows x 128 B
+  unsigned char *ring = smem + NDH * QHALF;
+  __shared__ uint64_t full[NSLOT], empty[NSLOT], s_full[2], p_ready[2], pv_done, drain;
   __shared__ uint32_t tmem_base;
-  __shared__ int failed_s;
+  __shared__ volatile int abort_s;
+  __shared__ int mma_landed_s, issued_s;
 
   const int tile = blockIdx.x, kvh = blockIdx.y;
-  const int t = threadIdx.x, warp = t >> 5;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int row0 = p.tiles[tile * 4 + 0], nrows = p.tiles[tile * 4 + 1];
   const int pos0 = p.tiles[tile * 4 + 2], trow = p.tiles[tile * 4 + 3];
   const int32_t *table = p.block_tables + size_t(trow) * p.max_blocks_per_seq;
   const int kv_len = pos0 + nrows;
   const int npages = (kv_len + kBS - 1) / kBS;
   const int ngroups = (kv_len + kKeys - 1) / kKeys;
-
-  // this thread's query row
-  const int tok = t / RPT, head = t % RPT;
-  const bool rvalid = head < G && tok < nrows;
-  const int pos = rvalid ? pos0 + tok : -1;
+  const int ntiles = 2 * ngroups;
 
   if (t == 0) {
-    mbar_init(&full[0], 1);
-    mbar_init(&full[1], 1);
-    mbar_init(&s_done, 1);
-    mbar_init(&o_done, 1);
+    for (int i = 0; i < NSLOT; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_ready[i], kRows);
+    }
+    mbar_init(&pv_done, 1);
     mbar_init(&drain, 1);
-    failed_s = 0;
+    abort_s = 0;
+    mma_landed_s = 0;
+    issued_s = 0;
     fence_barrier_init();
   }
   if (warp == 0) {
@@ -185,24 +243,10 @@ __global__ void __launch_bounds__(kRows) paged_prefill_tc5_kernel(const __grid_c
                  "r"(TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
-
-  auto issue = [&](int grp) {  // thread 0: the group's existing pages into stage grp & 1
-    const int s = grp & 1;
-    unsigned char *kst = stages + size_t(s) * STAGE_BYTES, *vst = kst + KP_BYTES;
-    const int first = grp * (kKeys / kBS), n = min(kKeys / kBS, npages - first);
-    mbar_expect_tx(&full[s], uint32_t(n) * 2 * NDH * PAGE_HALF);
-    for (int j = 0; j < n; ++j) {
-      const int tl = table[first + j] * p.num_kv_heads + kvh;
-#pragma unroll
-      for (int dh = 0; dh < NDH; ++dh) {
-        tma_load_4d(kst + dh * KVHALF + j * PAGE_HALF, &kmap, 0, dh, 0, tl, &full[s]);
-        tma_load_4d(vst + dh * KVHALF + j * PAGE_HALF, &vmap, 0, dh, 0, tl, &full[s]);
-      }
-    }
-  };
-
   // Q row t -> K-major swizzled tile (zeros for padding rows)
-  {
+  const int tok = t / RPT, head = t % RPT;
+  const bool rvalid = t < kRows && head < G && tok < nrows;
+  if (t < kRows) {
     const T *qr = static_cast<const T *>(p.q) +
                   ((size_t(row0) + (rvalid ? tok : 0)) * p.num_kv_heads * G + size_t(kvh) * G + (rvalid ? head : 0)) * D;
 #pragma unroll
@@ -218,152 +262,201 @@ __global__ void __launch_bounds__(kRows) paged_prefill_tc5_kernel(const __grid_c
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
-  const uint32_t tm_s = tmem, tm_o = tmem + kKeys;  // S columns [0, 64), O columns [64, 64 + D)
-  (void)failed_s;
-  const uint32_t lane_off = uint32_t(warp * 32) << 16;
-  if (t == 0) {
-    issue(0);
-    if (ngroups > 1) issue(1);
-  }
+  const uint32_t tm_o = tmem + 2 * kKeys;
 
-  const uint32_t id_s = umma_idesc<T>(kRows, kKeys, 0), id_o = umma_idesc<T>(kRows, D, 1);
-  float m_run = -INFINITY, l_run = 0.f;
-  bool failed = false;
-  int issued_groups = min(2, ngroups), landed = 0;  // (thread 0) groups issued / seen landed
-  for (int g = 0; g < ngroups; ++g) {
-    const int s = g & 1;
-    unsigned char *kst = stages + size_t(s) * STAGE_BYTES, *vst = kst + KP_BYTES;
-    const int key0 = g * kKeys;
-    // 1. S = Q K^T (thread 0), after the stage landed
-    if (t == 0) {
-      if (mbar_wait_bounded(&full[s], (g >> 1) & 1)) {
-        landed = g + 1;
-        tc_fence_after();
+  float l_run = 0.f;
+  if (warp < 4) {
+    // ---- softmax: row t ----
+    const uint32_t lane_off = uint32_t(warp * 32) << 16;
+    const int pos = rvalid ? pos0 + tok : pos0;  // padding rows copy the first row's mask
+    const float c = p.qscale;
+    float m_run = -INFINITY;
+    for (int g = 0; g < ngroups; ++g) {
+      const uint32_t tm_s = tmem + (g & 1) * kKeys;
+      if (!__all_sync(kFull, wait_or_abort(&s_full[g & 1], (g >> 1) & 1, &abort_s))) {
+        abort_s = 1;
+        break;
+      }
+      tc_fence_after();
+      float sv[kKeys];
+      {
+        float a[32];
+        tmem_ld32(tm_s + lane_off, a);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk & 3) * 32;  // 16 dims further within the 128-byte row
-          const uint64_t a = umma_desc_sw128(smem_addr(sq + (kk >> 2) * QHALF) + off, 16, 1024);
-          const uint64_t b = umma_desc_sw128(smem_addr(kst + (kk >> 2) * KVHALF) + off, 16, 1024);
-          umma(tm_s, a, b, id_s, kk > 0);
+        for (int i = 0; i < 32; ++i) sv[i] = a[i];
+        tmem_ld32(tm_s + lane_off + 32, a);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[32 + i] = a[i];
+      }
+      const int key0 = g * kKeys;
+      float mt = -INFINITY;
+      if (key0 + kKeys - 1 > pos0) {  // the group reaches past the tile's first position: causal mask
+#pragma unroll
+        for (int i = 0; i < kKeys; ++i) {
+          sv[i] = (key0 + i <= pos) ? sv[i] : -INFINITY;
+          mt = fmaxf(mt, sv[i]);
         }
       } else {
-        failed_s = 1;
+#pragma unroll
+        for (int i = 0; i < kKeys; ++i) mt = fmaxf(mt, sv[i]);
       }
-      umma_commit(&s_done);
-    }
-    if (!mbar_wait_bounded(&s_done, g & 1)) failed = true;
-    tc_fence_after();
-    if (__syncthreads_or(failed || failed_s)) {
-      failed = true;
-      break;
-    }
-    // the PV MMA of group g - 1 is complete (issued before this S): refill its stage
-    if (t == 0 && g >= 1 && g + 1 < ngroups) {
-      fence_proxy_async();
-      issue(g + 1);
-      issued_groups = g + 2;
-    }
-    // 2. softmax on this thread's row
-    float sv[kKeys];
-    {
-      float a[32];
-      tmem_ld32(tm_s + lane_off, a);
+      const float mts = mt * c;
+      const bool grow = mts > m_run + kRescale;  // m_run = -inf: any finite max
+      float alpha = 1.f;
+      if (grow) {
+        alpha = ex2_approx(m_run - mts);
+        m_run = mts;
+      }
+      if (g > 0 && __any_sync(kFull, grow)) {
+        // O is being accumulated by PV(g - 1): wait for it, then rescale this warp's rows
+        if (!__all_sync(kFull, wait_or_abort(&pv_done, (g - 1) & 1, &abort_s))) {
+          abort_s = 1;
+          break;
+        }
+        tc_fence_after();
 #pragma unroll
-      for (int i = 0; i < 32; ++i) sv[i] = a[i];
-      tmem_ld32(tm_s + lane_off + 32, a);
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          float o[32];
+          tmem_ld32(tm_o + lane_off + c0, o);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) sv[32 + i] = a[i];
-    }
-    float mt = -INFINITY;
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(tm_o + lane_off + c0, o);
+        }
+      }
+      const float negm = -m_run;
+      float psum = 0.f;
+      uint32_t pk[32];
 #pragma unroll
-    for (int i = 0; i < kKeys; ++i) {
-      sv[i] = (key0 + i <= pos) ? sv[i] * p.qscale : -INFINITY;  // causal (and length: pos < kv_len)
-      mt = fmaxf(mt, sv[i]);
+      for (int i = 0; i < 32; ++i) {
+        const float a = ex2_approx(fmaf(sv[2 * i], c, negm)), b = ex2_approx(fmaf(sv[2 * i + 1], c, negm));
+        psum += a;
+        psum += b;
+        pk[i] = pack_pair<T>(a, b);
+      }
+      l_run = l_run * alpha + psum;
+      tmem_st32u(tm_s + lane_off, pk);  // P over the first 32 columns of S(g)
+      // the last group's V rows past the sequence (stale, or pages never loaded) -> 0
+      const int vk = kv_len - key0;
+      if (g == ngroups - 1 && vk < kKeys) {
+        const int iv = ntiles - 1;
+        if (!__all_sync(kFull, wait_or_abort(&full[iv % NSLOT], (iv / NSLOT) & 1, &abort_s))) {
+          abort_s = 1;
+          break;
+        }
+        unsigned char *vst = ring + (iv % NSLOT) * TILE;
+        for (int i = t; i < (kKeys - vk) * 8 * NDH; i += kRows) {
+          const int dh = i / ((kKeys - vk) * 8), rem = i % ((kKeys - vk) * 8);
+          *reinterpret_cast<uint4 *>(vst + dh * HALF + (vk + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
+        }
+        fence_proxy_async();
+      }
+      tc_fence_before();
+      mbar_arrive(&p_ready[g & 1]);
     }
-    const bool grow = mt > m_run + kRescale || (m_run == -INFINITY && mt > -INFINITY);
-    float alpha = 1.f;
-    if (grow) {
-      alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - mt);
-      m_run = mt;
+  } else if (warp == 4) {
+    // ---- MMA issue ----
+    if (lane == 0) {
+      const uint32_t id_s = umma_idesc<T>(kRows, kKeys, 0), id_o = umma_idesc<T>(kRows, D, 1);
+      int landed = 0;
+      for (int i = 0; i < ntiles; ++i) {
+        bool is_v;
+        const int grp = ring_tile(i, ngroups, is_v);
+        const int slot = i % NSLOT;
+        if (is_v && !wait_or_abort(&p_ready[grp & 1], (grp >> 1) & 1, &abort_s)) {
+          abort_s = 1;
+          break;
+        }
+        if (!wait_or_abort(&full[slot], (i / NSLOT) & 1, &abort_s)) {
+          abort_s = 1;
+          break;
+        }
+        landed = i + 1;
+        tc_fence_after();
+        unsigned char *tl = ring + slot * TILE;
+        if (!is_v) {
+          const uint32_t tm_s = tmem + (grp & 1) * kKeys;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk & 3) * 32;  // 16 dims further within the 128-byte row
+            const uint64_t a = umma_desc_sw128(smem_addr(sq + (kk >> 2) * QHALF) + off, 16, 1024);
+            const uint64_t b = umma_desc_sw128(smem_addr(tl + (kk >> 2) * HALF) + off, 16, 1024);
+            umma(tm_s, a, b, id_s, kk > 0);
+          }
+          umma_commit(&s_full[grp & 1]);
+        } else {
+          const uint32_t tm_p = tmem + (grp & 1) * kKeys;
+#pragma unroll
+          for (int kk = 0; kk < kKeys / 16; ++kk) {
+            const uint64_t b = umma_desc_sw128(smem_addr(tl) + kk * 2048, HALF, 1024);
+            umma_ts(tm_o, tm_p + kk * 8, b, id_o, (grp > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&pv_done);
+        }
+        umma_commit(&empty[slot]);
+      }
+      mma_landed_s = landed;
     }
-    // rescale O in TMEM (warp-collective) when any row of the warp moved its max after O started
-    if (g > 0 && __any_sync(kFull, grow && alpha != 1.f)) {
+  } else {
+    // ---- TMA: tiles in ring order ----
+    if (lane == 0) {
+      int issued = 0;
+      for (int i = 0; i < ntiles; ++i) {
+        const int slot = i % NSLOT;
+        if (i >= NSLOT && !wait_or_abort(&empty[slot], ((i / NSLOT) - 1) & 1, &abort_s)) {
+          abort_s = 1;
+          break;
+        }
+        bool is_v;
+        const int grp = ring_tile(i, ngroups, is_v);
+        const int first = grp * (kKeys / kBS), n = min(kKeys / kBS, npages - first);
+        unsigned char *dst = ring + slot * TILE;
+        mbar_expect_tx(&full[slot], uint32_t(n) * NDH * PAGE_HALF);
+        for (int j = 0; j < n; ++j) {
+          const int tl = table[first + j] * p.num_kv_heads + kvh;
+#pragma unroll
+          for (int dh = 0; dh < NDH; ++dh)
+            tma_load_4d(dst + dh * HALF + j * PAGE_HALF, is_v ? &vmap : &kmap, 0, dh, 0, tl, &full[slot]);
+        }
+        issued = i + 1;
+      }
+      issued_s = issued;
+    }
+  }
+
+  // join: every role has left its loop; then drain MMAs and copies in flight
+  __syncthreads();
+  bool ok_end = !abort_s;
+  if (warp == 4 && lane == 0) {
+    umma_commit(&drain);
+    if (!mbar_wait_bounded(&drain, 0)) ok_end = false;
+  } else if (warp == 5 && lane == 0) {
+    for (int i = mma_landed_s; i < issued_s; ++i)
+      if (!mbar_wait_bounded(&full[i % NSLOT], (i / NSLOT) & 1)) ok_end = false;
+  }
+  tc_fence_before();
+  const bool all_ok = __syncthreads_and(ok_end);
+  tc_fence_after();
+  if (all_ok) {
+    if (warp < 4) {
+      // O row / l -> out; every softmax thread takes part in the warp-collective TMEM loads
+      const uint32_t lane_off = uint32_t(warp * 32) << 16;
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      T *orow = static_cast<T *>(p.out) +
+                ((size_t(row0) + (rvalid ? tok : 0)) * p.num_kv_heads * G + size_t(kvh) * G + (rvalid ? head : 0)) * D;
 #pragma unroll
       for (int c0 = 0; c0 < D; c0 += 32) {
         float o[32];
         tmem_ld32(tm_o + lane_off + c0, o);
+        if (rvalid) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] *= alpha;
-        tmem_st32(tm_o + lane_off + c0, o);
-      }
-    }
-    float psum = 0.f;
-#pragma unroll
-    for (int i = 0; i < kKeys; ++i) {
-      sv[i] = (sv[i] == -INFINITY) ? 0.f : exp2f(sv[i] - m_run);
-      psum += sv[i];
-    }
-    l_run = l_run * alpha + psum;
-    // 3. P over the consumed K tile (64 keys = one 128-byte row per query row)
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      uint4 w;
-      w.x = pack_pair<T>(sv[8 * c + 0], sv[8 * c + 1]);
-      w.y = pack_pair<T>(sv[8 * c + 2], sv[8 * c + 3]);
-      w.z = pack_pair<T>(sv[8 * c + 4], sv[8 * c + 5]);
-      w.w = pack_pair<T>(sv[8 * c + 6], sv[8 * c + 7]);
-      *reinterpret_cast<uint4 *>(kst + t * 128 + ((c ^ (t & 7)) << 4)) = w;
-    }
-    // V rows of keys past the sequence (stale, or pages never loaded) -> 0
-    const int vk = kv_len - key0;  // valid keys of this group
-    if (vk < kKeys)
-      for (int i = t; i < (kKeys - vk) * 8 * NDH; i += kRows) {
-        const int dh = i / ((kKeys - vk) * 8), rem = i % ((kKeys - vk) * 8);
-        *reinterpret_cast<uint4 *>(vst + dh * KVHALF + (vk + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
-      }
-    fence_proxy_async();
-    tc_fence_before();
-    __syncthreads();
-    // 4. O += P V (thread 0)
-    if (t == 0) {
-      tc_fence_after();
-#pragma unroll
-      for (int kk = 0; kk < kKeys / 16; ++kk) {
-        const uint64_t a = umma_desc_sw128(smem_addr(kst) + kk * 32, 16, 1024);
-        const uint64_t b = umma_desc_sw128(smem_addr(vst) + kk * 2048, KVHALF, 1024);
-        umma(tm_o, a, b, id_o, (g > 0 || kk > 0) ? 1u : 0u);
-      }
-      umma_commit(&o_done);
-    }
-  }
-
-  // drain: every MMA issued by thread 0 and every copy issued is complete
-  bool ok_end = !failed;
-  if (t == 0) {
-    umma_commit(&drain);
-    for (int g = landed; g < issued_groups; ++g)
-      if (!mbar_wait_bounded(&full[g & 1], (g >> 1) & 1)) ok_end = false;
-  }
-  if (!mbar_wait_bounded(&drain, 0)) ok_end = false;
-  tc_fence_after();
-  if (__syncthreads_and(ok_end)) {
-    // O row / l -> out; every thread takes part in the warp-collective TMEM loads
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-    T *orow = static_cast<T *>(p.out) +
-              ((size_t(row0) + (rvalid ? tok : 0)) * p.num_kv_heads * G + size_t(kvh) * G + (rvalid ? head : 0)) * D;
-#pragma unroll
-    for (int c0 = 0; c0 < D; c0 += 32) {
-      float o[32];
-      tmem_ld32(tm_o + lane_off + c0, o);
-      if (rvalid) {
-#pragma unroll
-        for (int i = 0; i < 32; i += 8) {
-          uint4 w;
-          w.x = pack_pair<T>(o[i] * inv, o[i + 1] * inv);
-          w.y = pack_pair<T>(o[i + 2] * inv, o[i + 3] * inv);
-          w.z = pack_pair<T>(o[i + 4] * inv, o[i + 5] * inv);
-          w.w = pack_pair<T>(o[i + 6] * inv, o[i + 7] * inv);
-          *reinterpret_cast<uint4 *>(orow + c0 + i) = w;
+          for (int i = 0; i < 32; i += 8) {
+            uint4 w;
+            w.x = pack_pair<T>(o[i] * inv, o[i + 1] * inv);
+            w.y = pack_pair<T>(o[i + 2] * inv, o[i + 3] * inv);
+            w.z = pack_pair<T>(o[i + 4] * inv, o[i + 5] * inv);
+            w.w = pack_pair<T>(o[i + 6] * inv, o[i + 7] * inv);
+            *reinterpret_cast<uint4 *>(orow + c0 + i) = w;
+          }
         }
       }
     }
@@ -379,10 +472,7 @@ template <typename T, int D, int G>
 cudaError_t launch_t5(const Prefill5Params &p, const CUtensorMap &km, const CUtensorMap &vm, int num_tiles,
                       cudaStream_t stream) {
   auto kern = paged_prefill_tc5_kernel<T, D, G>;
-  constexpr int NDH = D / 64;
-  constexpr int KV_BYTES = NDH * kKeys * 128;
-  constexpr int KP_BYTES = KV_BYTES > kRows * 128 ? KV_BYTES : kRows * 128;
-  const size_t smem = 1024 + size_t(NDH) * kRows * 128 + 2 * size_t(KP_BYTES + KV_BYTES);
+  const size_t smem = Ring5<D>::kSmem;
   static bool attr_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -392,7 +482,7 @@ cudaError_t launch_t5(const Prefill5Params &p, const CUtensorMap &km, const CUte
     attr_done[dev] = true;
   }
   dim3 grid(num_tiles, p.num_kv_heads);
-  kern<<<grid, kRows, smem, stream>>>(km, vm, p);
+  kern<<<grid, kThreads5, smem, stream>>>(km, vm, p);
   return cudaGetLastError();
 }
 
