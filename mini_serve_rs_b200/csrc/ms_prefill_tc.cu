@@ -285,7 +285,7 @@ bool prefill_tc5_enabled();
 int prefill_tc5_tokens_per_tile(int group);
 cudaError_t launch_prefill_tc5(const void *q, void *out, const int32_t *block_tables, int max_blocks_per_seq,
                                const int32_t *tiles, int num_tiles, int num_kv_heads, int group, int head_dim,
-                               float scale, unsigned *status, int dtype, const CUtensorMap &km, const CUtensorMap &vm,
+                               float scale, unsigned *status, int dtype, const void *k_pool, const void *v_pool,
                                cudaStream_t stream);
 }  // namespace attn
 
@@ -302,6 +302,17 @@ cudaError_t launch_paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
     return cudaErrorInvalidValue;
   const int group = a.num_heads / a.num_kv_heads;
   if (!attn::attention_tc_supported(a.dtype, a.head_dim, group)) return cudaErrorInvalidValue;
+  unsigned *status = a.status;
+  if (!status) {
+    void *sp = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&sp, attn::g_prefill_status);
+    if (e != cudaSuccess) return e;
+    status = static_cast<unsigned *>(sp);
+  }
+  if (attn::prefill_tc5_enabled())
+    return attn::launch_prefill_tc5(a.q, a.out, a.block_tables, a.max_blocks_per_seq, a.tiles, a.num_tiles,
+                                    a.num_kv_heads, group, a.head_dim, a.scale, status, a.dtype, a.k_pool, a.v_pool,
+                                    stream);
   CUtensorMap km, vm;
   const int64_t tiles = a.pool_tiles > 0 ? a.pool_tiles : (int64_t(1) << 31) - 1;
   if (a.k_map) km = *static_cast<const CUtensorMap *>(a.k_map);
@@ -316,16 +327,7 @@ cudaError_t launch_paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
   p.max_blocks_per_seq = a.max_blocks_per_seq;
   p.num_kv_heads = a.num_kv_heads;
   p.qscale = a.scale * attn::kLog2e;
-  p.status = a.status;
-  if (!p.status) {
-    void *sp = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&sp, attn::g_prefill_status);
-    if (e != cudaSuccess) return e;
-    p.status = static_cast<unsigned *>(sp);
-  }
-  if (attn::prefill_tc5_enabled())
-    return attn::launch_prefill_tc5(a.q, a.out, a.block_tables, a.max_blocks_per_seq, a.tiles, a.num_tiles,
-                                    a.num_kv_heads, group, a.head_dim, a.scale, p.status, a.dtype, km, vm, stream);
+  p.status = status;
   if (a.dtype == MS_DTYPE_BF16) {
     return a.head_dim == 128 ? attn::prefill_group<__nv_bfloat16, 128>(p, km, vm, group, a.num_tiles, stream)
                              : attn::prefill_group<__nv_bfloat16, 64>(p, km, vm, group, a.num_tiles, stream);

@@ -113,6 +113,20 @@ __device__ __forceinline__ void tmem_st32(uint32_t addr, const float (&v)[32]) {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// 32 consecutive 32-bit columns of this thread's TMEM lane, without waiting
+// (tcgen05.wait::ld before the registers are read).
+__device__ __forceinline__ void tmem_ld32_async(uint32_t addr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(addr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 template <typename T> __device__ __forceinline__ uint32_t pack_pair(float a, float b);
 template <> __device__ __forceinline__ uint32_t pack_pair<__nv_bfloat16>(float a, float b) {
   __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
@@ -127,6 +141,8 @@ template <int G> struct RowsPerTok5 { static constexpr int value = G <= 1 ? 1 : 
 
 struct Prefill5Params {
   const void *q;
+  const void *k_pool;  // [pool_blocks][Hkv][16][D]
+  const void *v_pool;
   void *out;
   const int32_t *block_tables;
   const int32_t *tiles;  // [num_tiles][4]: first packed row, rows, position of first row, table row
@@ -164,6 +180,14 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, vo
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
+__device__ __forceinline__ void cp_async16(void *dst_smem, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst_smem)), "l"(src) : "memory");
+}
+// arrive on `bar` (without raising its expected count) once this thread's earlier cp.async copies completed
+__device__ __forceinline__ void cp_async_arrive_on(uint64_t *bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -192,14 +216,11 @@ __device__ __forceinline__ void tmem_st32u(uint32_t addr, const uint32_t (&v)[32
 constexpr int kThreads5 = 192;  // 4 softmax warps, the MMA warp, the TMA warp
 
 template <typename T, int D, int G>
-__global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(const __grid_constant__ CUtensorMap kmap,
-                                                                         const __grid_constant__ CUtensorMap vmap,
-                                                                         Prefill5Params p) {
+__global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(Prefill5Params p) {
   constexpr int RPT = RowsPerTok5<G>::value;
   constexpr int NDH = D / 64;          // 64-dim (128-byte) halves
   constexpr int QHALF = kRows * 128;   // one 64-dim half of the Q tile
   constexpr int HALF = Ring5<D>::kHalf, TILE = Ring5<D>::kTile, NSLOT = Ring5<D>::kSlots;
-  constexpr int PAGE_HALF = kBS * 128; // one TMA box: 16 keys x 64 dims
   constexpr int TMEM_COLS = 256;       // S0 [0, 64), S1 [64, 128), O [128, 128 + D)
 
   extern __shared__ unsigned char smem_dyn[];
@@ -224,7 +245,7 @@ __global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(const _
 
   if (t == 0) {
     for (int i = 0; i < NSLOT; ++i) {
-      mbar_init(&full[i], 1);
+      mbar_init(&full[i], 32);  // the copy warp's lanes
       mbar_init(&empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -280,26 +301,28 @@ __global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(const _
       tc_fence_after();
       float sv[kKeys];
       {
-        float a[32];
-        tmem_ld32(tm_s + lane_off, a);
+        uint32_t a[32], b[32];
+        tmem_ld32_async(tm_s + lane_off, a);
+        tmem_ld32_async(tm_s + lane_off + 32, b);
+        tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) sv[i] = a[i];
-        tmem_ld32(tm_s + lane_off + 32, a);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) sv[32 + i] = a[i];
+        for (int i = 0; i < 32; ++i) {
+          sv[i] = __uint_as_float(a[i]);
+          sv[32 + i] = __uint_as_float(b[i]);
+        }
       }
       const int key0 = g * kKeys;
-      float mt = -INFINITY;
       if (key0 + kKeys - 1 > pos0) {  // the group reaches past the tile's first position: causal mask
 #pragma unroll
-        for (int i = 0; i < kKeys; ++i) {
-          sv[i] = (key0 + i <= pos) ? sv[i] : -INFINITY;
-          mt = fmaxf(mt, sv[i]);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < kKeys; ++i) mt = fmaxf(mt, sv[i]);
+        for (int i = 0; i < kKeys; ++i) sv[i] = (key0 + i <= pos) ? sv[i] : -INFINITY;
       }
+      // row max with 8 independent chains
+      float mx[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) mx[j] = sv[j];
+#pragma unroll
+      for (int i = 8; i < kKeys; ++i) mx[i & 7] = fmaxf(mx[i & 7], sv[i]);
+      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       const float mts = mt * c;
       const bool grow = mts > m_run + kRescale;  // m_run = -inf: any finite max
       float alpha = 1.f;
@@ -324,15 +347,15 @@ __global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(const _
         }
       }
       const float negm = -m_run;
-      float psum = 0.f;
+      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       uint32_t pk[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const float a = ex2_approx(fmaf(sv[2 * i], c, negm)), b = ex2_approx(fmaf(sv[2 * i + 1], c, negm));
-        psum += a;
-        psum += b;
+        ps[i & 7] += a + b;
         pk[i] = pack_pair<T>(a, b);
       }
+      const float psum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       l_run = l_run * alpha + psum;
       tmem_st32u(tm_s + lane_off, pk);  // P over the first 32 columns of S(g)
       // the last group's V rows past the sequence (stale, or pages never loaded) -> 0
@@ -371,6 +394,7 @@ __global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(const _
           break;
         }
         landed = i + 1;
+        fence_proxy_async();  // the copies were generic-proxy writes
         tc_fence_after();
         unsigned char *tl = ring + slot * TILE;
         if (!is_v) {
@@ -397,30 +421,58 @@ __global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(const _
       mma_landed_s = landed;
     }
   } else {
-    // ---- TMA: tiles in ring order ----
-    if (lane == 0) {
-      int issued = 0;
-      for (int i = 0; i < ntiles; ++i) {
-        const int slot = i % NSLOT;
-        if (i >= NSLOT && !wait_or_abort(&empty[slot], ((i / NSLOT) - 1) & 1, &abort_s)) {
-          abort_s = 1;
-          break;
-        }
-        bool is_v;
-        const int grp = ring_tile(i, ngroups, is_v);
-        const int first = grp * (kKeys / kBS), n = min(kKeys / kBS, npages - first);
-        unsigned char *dst = ring + slot * TILE;
-        mbar_expect_tx(&full[slot], uint32_t(n) * NDH * PAGE_HALF);
-        for (int j = 0; j < n; ++j) {
-          const int tl = table[first + j] * p.num_kv_heads + kvh;
-#pragma unroll
-          for (int dh = 0; dh < NDH; ++dh)
-            tma_load_4d(dst + dh * HALF + j * PAGE_HALF, is_v ? &vmap : &kmap, 0, dh, 0, tl, &full[slot]);
-        }
-        issued = i + 1;
+    // ---- copies: tiles in ring order, 16 bytes per lane per instruction ----
+    // Lane l holds page id (32 w + l) of the current window w of each stream
+    // (K and V visit the groups in order), and the next window is loaded as
+    // soon as the current one is taken, so no tile waits on a table read.
+    // A page of one kv head is 16 rows of D elements, contiguous in the pool;
+    // lane l always copies 16-byte column l % CPR of rows l / CPR, l / CPR +
+    // RPI, ... into the swizzled operand layout.  After a tile's copies each
+    // lane arms an arrive on the slot's full barrier that fires when they
+    // complete (cp.async.mbarrier.arrive.noinc); the MMA thread makes them
+    // visible to the tensor core (fence.proxy.async) after its wait.
+    constexpr int CPR = D / 8, RPI = 32 / CPR, IPP = kBS / RPI;  // chunks per row, rows per instruction, per page
+    const int cc = lane % CPR, dh = cc >> 3, ch = cc & 7, r0 = lane / CPR;
+    auto table_at = [&](int i) { return i < npages ? table[i] : 0; };
+    int kw = 0, vw = 0;
+    int kcur = table_at(lane), vcur = kcur, knxt = table_at(32 + lane), vnxt = knxt;
+    int issued = 0;
+    for (int i = 0; i < ntiles; ++i) {
+      const int slot = i % NSLOT;
+      if (i >= NSLOT && !__all_sync(kFull, wait_or_abort(&empty[slot], ((i / NSLOT) - 1) & 1, &abort_s))) {
+        abort_s = 1;
+        break;
       }
-      issued_s = issued;
+      bool is_v;
+      const int grp = ring_tile(i, ngroups, is_v);
+      const int first = grp * (kKeys / kBS), n = min(kKeys / kBS, npages - first);
+      const int w = first >> 5;
+      int &cw = is_v ? vw : kw, &cur = is_v ? vcur : kcur, &nxt = is_v ? vnxt : knxt;
+      if (w != cw) {  // groups advance one at a time, so w == cw + 1
+        cur = nxt;
+        cw = w;
+        nxt = table_at(32 * (w + 1) + lane);
+      }
+      const T *pool = static_cast<const T *>(is_v ? p.v_pool : p.k_pool);
+      unsigned char *dst = ring + slot * TILE + dh * HALF;
+#pragma unroll
+      for (int j = 0; j < kKeys / kBS; ++j) {
+        const int pid = __shfl_sync(kFull, cur, (first & 31) + j);
+        if (j < n) {
+          const T *src = pool + (size_t(pid) * p.num_kv_heads + kvh) * (kBS * D) + cc * 8;
+#pragma unroll
+          for (int k = 0; k < IPP; ++k) {
+            const int r = r0 + k * RPI;          // row within the page
+            const int kr = j * kBS + r;          // key row within the tile
+            cp_async16(dst + kr * 128 + ((ch ^ (kr & 7)) << 4), src + r * D);
+          }
+        }
+      }
+      cp_async_arrive_on(&full[slot]);
+      issued = i + 1;
     }
+    cp_async_wait_all();
+    if (lane == 0) issued_s = issued;
   }
 
   // join: every role has left its loop; then drain MMAs and copies in flight
@@ -430,6 +482,7 @@ __global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(const _
     umma_commit(&drain);
     if (!mbar_wait_bounded(&drain, 0)) ok_end = false;
   } else if (warp == 5 && lane == 0) {
+    // the copies are complete (cp.async.wait_all); their barrier arrives must land before the CTA exits
     for (int i = mma_landed_s; i < issued_s; ++i)
       if (!mbar_wait_bounded(&full[i % NSLOT], (i / NSLOT) & 1)) ok_end = false;
   }
@@ -469,8 +522,7 @@ __global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(const _
 }
 
 template <typename T, int D, int G>
-cudaError_t launch_t5(const Prefill5Params &p, const CUtensorMap &km, const CUtensorMap &vm, int num_tiles,
-                      cudaStream_t stream) {
+cudaError_t launch_t5(const Prefill5Params &p, int num_tiles, cudaStream_t stream) {
   auto kern = paged_prefill_tc5_kernel<T, D, G>;
   const size_t smem = Ring5<D>::kSmem;
   static bool attr_done[64] = {false};
@@ -482,19 +534,18 @@ cudaError_t launch_t5(const Prefill5Params &p, const CUtensorMap &km, const CUte
     attr_done[dev] = true;
   }
   dim3 grid(num_tiles, p.num_kv_heads);
-  kern<<<grid, kThreads5, smem, stream>>>(km, vm, p);
+  kern<<<grid, kThreads5, smem, stream>>>(p);
   return cudaGetLastError();
 }
 
 template <typename T, int D>
-cudaError_t t5_group(const Prefill5Params &p, const CUtensorMap &km, const CUtensorMap &vm, int group, int num_tiles,
-                     cudaStream_t stream) {
+cudaError_t t5_group(const Prefill5Params &p, int group, int num_tiles, cudaStream_t stream) {
   switch (group) {
-    case 1: return launch_t5<T, D, 1>(p, km, vm, num_tiles, stream);
-    case 2: return launch_t5<T, D, 2>(p, km, vm, num_tiles, stream);
-    case 4: return launch_t5<T, D, 4>(p, km, vm, num_tiles, stream);
-    case 7: return launch_t5<T, D, 7>(p, km, vm, num_tiles, stream);
-    case 8: return launch_t5<T, D, 8>(p, km, vm, num_tiles, stream);
+    case 1: return launch_t5<T, D, 1>(p, num_tiles, stream);
+    case 2: return launch_t5<T, D, 2>(p, num_tiles, stream);
+    case 4: return launch_t5<T, D, 4>(p, num_tiles, stream);
+    case 7: return launch_t5<T, D, 7>(p, num_tiles, stream);
+    case 8: return launch_t5<T, D, 8>(p, num_tiles, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -518,10 +569,13 @@ int prefill_tc5_tokens_per_tile(int group) {
 
 cudaError_t launch_prefill_tc5(const void *q, void *out, const int32_t *block_tables, int max_blocks_per_seq,
                                const int32_t *tiles, int num_tiles, int num_kv_heads, int group, int head_dim,
-                               float scale, unsigned *status, int dtype, const CUtensorMap &km, const CUtensorMap &vm,
+                               float scale, unsigned *status, int dtype, const void *k_pool, const void *v_pool,
                                cudaStream_t stream) {
+  if ((reinterpret_cast<uintptr_t>(k_pool) | reinterpret_cast<uintptr_t>(v_pool)) & 15) return cudaErrorInvalidValue;
   Prefill5Params p;
   p.q = q;
+  p.k_pool = k_pool;
+  p.v_pool = v_pool;
   p.out = out;
   p.block_tables = block_tables;
   p.tiles = tiles;
@@ -530,11 +584,11 @@ cudaError_t launch_prefill_tc5(const void *q, void *out, const int32_t *block_ta
   p.num_kv_heads = num_kv_heads;
   p.qscale = scale * kLog2e;
   if (dtype == MS_DTYPE_BF16) {
-    if (head_dim == 128) return t5_group<__nv_bfloat16, 128>(p, km, vm, group, num_tiles, stream);
-    if (head_dim == 64) return t5_group<__nv_bfloat16, 64>(p, km, vm, group, num_tiles, stream);
+    if (head_dim == 128) return t5_group<__nv_bfloat16, 128>(p, group, num_tiles, stream);
+    if (head_dim == 64) return t5_group<__nv_bfloat16, 64>(p, group, num_tiles, stream);
   } else if (dtype == MS_DTYPE_F16) {
-    if (head_dim == 128) return t5_group<__half, 128>(p, km, vm, group, num_tiles, stream);
-    if (head_dim == 64) return t5_group<__half, 64>(p, km, vm, group, num_tiles, stream);
+    if (head_dim == 128) return t5_group<__half, 128>(p, group, num_tiles, stream);
+    if (head_dim == 64) return t5_group<__half, 64>(p, group, num_tiles, stream);
   }
   return cudaErrorInvalidValue;
 }
