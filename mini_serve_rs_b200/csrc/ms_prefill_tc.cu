@@ -12,6 +12,8 @@
 // skipped by that warp.  Stale keys past the sequence's length in its last
 // page are masked in S and their V fragments zeroed in registers.
 #include <algorithm>
+#include <array>
+#include <vector>
 #include <mutex>
 
 #include "ms_attention_common.cuh"
@@ -336,21 +338,25 @@ cudaError_t launch_paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
                            : attn::prefill_group<__half, 64>(p, km, vm, group, a.num_tiles, stream);
 }
 
+// Tiles in decreasing order of their causal range (position of the first row
+// + rows), ties in input order: the CTAs that sweep the most keys start
+// first, so short tiles fill the last wave.
 int build_prefill_tiles(const int32_t *seq_row0, const int32_t *seq_ntok, const int32_t *seq_start,
                         const int32_t *seq_trow, int num_seqs, int group, int32_t *tiles_out, int capacity) {
   const int tpb = prefill_tokens_per_tile(group);
-  int n = 0;
+  std::vector<std::array<int32_t, 4>> tl;
   for (int i = 0; i < num_seqs; ++i) {
     for (int j = 0; j < seq_ntok[i]; j += tpb) {
-      if (n >= capacity) return -1;
-      tiles_out[4 * n + 0] = seq_row0[i] + j;
-      tiles_out[4 * n + 1] = std::min(tpb, seq_ntok[i] - j);
-      tiles_out[4 * n + 2] = seq_start[i] + j;
-      tiles_out[4 * n + 3] = seq_trow[i];
-      ++n;
+      if (int(tl.size()) >= capacity) return -1;
+      tl.push_back({seq_row0[i] + j, std::min(tpb, seq_ntok[i] - j), seq_start[i] + j, seq_trow[i]});
     }
   }
-  return n;
+  std::stable_sort(tl.begin(), tl.end(), [](const std::array<int32_t, 4> &a, const std::array<int32_t, 4> &b) {
+    return a[2] + a[1] > b[2] + b[1];
+  });
+  for (size_t n = 0; n < tl.size(); ++n)
+    for (int k = 0; k < 4; ++k) tiles_out[4 * n + k] = tl[n][k];
+  return int(tl.size());
 }
 
 }  // namespace ms

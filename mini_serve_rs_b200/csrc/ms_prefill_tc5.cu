@@ -46,7 +46,7 @@ namespace attn {
 namespace {
 
 constexpr int kRows = 128;     // query rows per CTA = TMEM lanes
-constexpr int kKeys = 64;      // keys per group (4 pages)
+constexpr int kKeys = 128;     // keys per group (8 pages): the S MMA is M 128 x N 128
 constexpr float kRescale = 8.0f;  // move the running max only when it grows by more than 2^8
 
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
@@ -152,22 +152,15 @@ struct Prefill5Params {
   float qscale;
 };
 
+constexpr int kHalves = 2;  // query halves of 128 rows per CTA, sharing every K/V tile
+
 template <int D> struct Ring5 {
-  static constexpr int kHalf = kKeys * 128;                 // 64 keys x 64 dims (one 128-byte row per key)
+  static constexpr int kHalf = kKeys * 128;                 // 128 keys x 64 dims (one 128-byte row per key)
   static constexpr int kTile = (D / 64) * kHalf;            // one K or V tile
   static constexpr int kSlots = D == 128 ? 4 : 8;
-  static constexpr int kSmem = 1024 + (D / 64) * kRows * 128 + kSlots * kTile;  // + alignment slack
+  static constexpr int kQ = (D / 64) * kRows * 128;         // one query half
+  static constexpr int kSmem = 1024 + kHalves * kQ + kSlots * kTile;  // + alignment slack
 };
-
-// Tile i of the ring order K0 K1 V0 K2 V1 ... K(n-1) V(n-2) V(n-1) (the order
-// the MMA thread consumes them); returns the group, sets is_v.
-__device__ __forceinline__ int ring_tile(int i, int n, bool &is_v) {
-  if (i == 0) { is_v = false; return 0; }
-  if (i == 2 * n - 1) { is_v = true; return n - 1; }
-  if (i & 1) { is_v = false; return (i + 1) >> 1; }
-  is_v = true;
-  return (i - 2) >> 1;
-}
 
 // Bounded mbarrier wait that gives up early once another role set `abort`.
 __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort) {
@@ -188,6 +181,26 @@ __device__ __forceinline__ void cp_async_arrive_on(uint64_t *bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// max of three (sm_100 three-input max.f32)
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// (d0, d1) = (a0, a1) * b + c, one packed f32x2 FMA (each lane rounded once, as fmaf)
+__device__ __forceinline__ void ffma2(float &d0, float &d1, float a0, float a1, float b, float c) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\t"
+      "mov.b64 rc, {%5, %5};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b), "f"(c));
+}
+// (d0, d1) += (a0, a1), one packed f32x2 add
+__device__ __forceinline__ void fadd2(float &d0, float &d1, float a0, float a1) {
+  asm("{\n\t.reg .b64 ra, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rd, {%0, %1};\n\t"
+      "add.rn.f32x2 rd, rd, ra;\n\tmov.b64 {%0, %1}, rd;\n}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1));
+}
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -213,27 +226,38 @@ __device__ __forceinline__ void tmem_st32u(uint32_t addr, const uint32_t (&v)[32
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-constexpr int kThreads5 = 192;  // 4 softmax warps, the MMA warp, the TMA warp
+__device__ __forceinline__ void tmem_st16u(uint32_t addr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(addr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+constexpr int kThreads5 = 320;  // 2 x 4 softmax warps (one group of 4 per query half), the MMA warp, the copy warp
 
 template <typename T, int D, int G>
-__global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(Prefill5Params p) {
+__global__ void __launch_bounds__(kThreads5, 1) paged_prefill_tc5_kernel(Prefill5Params p) {
   constexpr int RPT = RowsPerTok5<G>::value;
+  constexpr int TPH = kRows / RPT;     // tokens per query half
   constexpr int NDH = D / 64;          // 64-dim (128-byte) halves
-  constexpr int QHALF = kRows * 128;   // one 64-dim half of the Q tile
-  constexpr int HALF = Ring5<D>::kHalf, TILE = Ring5<D>::kTile, NSLOT = Ring5<D>::kSlots;
-  constexpr int TMEM_COLS = 256;       // S0 [0, 64), S1 [64, 128), O [128, 128 + D)
+  constexpr int QHALF = kRows * 128;   // one 64-dim half of a query half
+  constexpr int HALF = Ring5<D>::kHalf, TILE = Ring5<D>::kTile, NSLOT = Ring5<D>::kSlots, QB = Ring5<D>::kQ;
+  constexpr int PAGES = kKeys / kBS;   // pages per group
+  constexpr int TMEM_COLS = 512;       // query half h: S (then P) at 256 h + [0, 128), O at 256 h + [128, 128 + D)
 
   extern __shared__ unsigned char smem_dyn[];
   unsigned char *smem =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-  unsigned char *sq = smem;  // Q: NDH halves of 128 rows x 128 B
-  unsigned char *ring = smem + NDH * QHALF;
-  __shared__ uint64_t full[NSLOT], empty[NSLOT], s_full[2], p_ready[2], pv_done, drain;
+  unsigned char *sq = smem;  // query half h at h * QB: NDH 64-dim halves of 128 rows x 128 B
+  unsigned char *ring = smem + kHalves * QB;
+  __shared__ uint64_t full[NSLOT], empty[NSLOT], s_full[kHalves], p_ready[kHalves], pv_done[kHalves], drain;
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_s;
   __shared__ int mma_landed_s, issued_s;
 
-  const int tile = blockIdx.x, kvh = blockIdx.y;
+  const int kvh = blockIdx.x, tile = blockIdx.y;  // kv heads vary fastest: a tile's heads start together
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int row0 = p.tiles[tile * 4 + 0], nrows = p.tiles[tile * 4 + 1];
   const int pos0 = p.tiles[tile * 4 + 2], trow = p.tiles[tile * 4 + 3];
@@ -241,18 +265,25 @@ __global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(Prefill
   const int kv_len = pos0 + nrows;
   const int npages = (kv_len + kBS - 1) / kBS;
   const int ngroups = (kv_len + kKeys - 1) / kKeys;
-  const int ntiles = 2 * ngroups;
+  const int ntiles = 2 * ngroups;  // ring order K0 V0 K1 V1 ...: K(g) is tile 2g, V(g) tile 2g + 1
+  // groups each query half attends to (its last token's causal range); half 1 may be empty
+  int ng[kHalves];
+#pragma unroll
+  for (int h = 0; h < kHalves; ++h) {
+    const int last = min(nrows, (h + 1) * TPH);  // tokens up to the end of half h
+    ng[h] = last > h * TPH ? (pos0 + last + kKeys - 1) / kKeys : 0;
+  }
 
   if (t == 0) {
     for (int i = 0; i < NSLOT; ++i) {
       mbar_init(&full[i], 32);  // the copy warp's lanes
       mbar_init(&empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_ready[i], kRows);
+    for (int h = 0; h < kHalves; ++h) {
+      mbar_init(&s_full[h], 1);
+      mbar_init(&p_ready[h], kRows);
+      mbar_init(&pv_done[h], 1);
     }
-    mbar_init(&pv_done, 1);
     mbar_init(&drain, 1);
     abort_s = 0;
     mma_landed_s = 0;
@@ -264,10 +295,12 @@ __global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(Prefill
                  "r"(TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
-  // Q row t -> K-major swizzled tile (zeros for padding rows)
-  const int tok = t / RPT, head = t % RPT;
-  const bool rvalid = t < kRows && head < G && tok < nrows;
-  if (t < kRows) {
+  // softmax thread t: query half qh = warp / 4, row rt = t % 128 of that half (TMEM lane rt)
+  const int qh = warp >> 2, rt = t & (kRows - 1);
+  const int tok = qh * TPH + rt / RPT, head = rt % RPT;
+  const bool rvalid = warp < 4 * kHalves && head < G && tok < nrows;
+  const int ng_q = qh == 0 ? ng[0] : ng[1];  // groups of this thread's half (softmax warps)
+  if (warp < 4 * kHalves) {  // Q row -> K-major swizzled tile (zeros for padding rows)
     const T *qr = static_cast<const T *>(p.q) +
                   ((size_t(row0) + (rvalid ? tok : 0)) * p.num_kv_heads * G + size_t(kvh) * G + (rvalid ? head : 0)) * D;
 #pragma unroll
@@ -275,7 +308,7 @@ __global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(Prefill
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         const uint4 v = rvalid ? reinterpret_cast<const uint4 *>(qr + dh * 64)[c] : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4 *>(sq + dh * QHALF + t * 128 + ((c ^ (t & 7)) << 4)) = v;
+        *reinterpret_cast<uint4 *>(sq + qh * QB + dh * QHALF + rt * 128 + ((c ^ (rt & 7)) << 4)) = v;
       }
   }
   fence_proxy_async();
@@ -283,46 +316,51 @@ __global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(Prefill
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
-  const uint32_t tm_o = tmem + 2 * kKeys;
 
   float l_run = 0.f;
-  if (warp < 4) {
-    // ---- softmax: row t ----
-    const uint32_t lane_off = uint32_t(warp * 32) << 16;
-    const int pos = rvalid ? pos0 + tok : pos0;  // padding rows copy the first row's mask
+  if (warp < 4 * kHalves) {
+    // ---- softmax: row rt of query half qh ----
+    const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
+    const uint32_t tm_s = tmem + qh * 256, tm_o = tm_s + kKeys;
+    const int pos_first = pos0 + qh * TPH;            // first position of this half
+    const int pos = rvalid ? pos0 + tok : pos_first;  // padding rows copy the half's first row mask
     const float c = p.qscale;
+    // the lowest half that attends to the last group zeroes its V rows past the sequence
+    const bool zeroes_v = ng_q == ngroups && (qh == 0 || ng[0] < ngroups);
     float m_run = -INFINITY;
-    for (int g = 0; g < ngroups; ++g) {
-      const uint32_t tm_s = tmem + (g & 1) * kKeys;
-      if (!__all_sync(kFull, wait_or_abort(&s_full[g & 1], (g >> 1) & 1, &abort_s))) {
+    for (int g = 0; g < ng_q; ++g) {
+      if (!__all_sync(kFull, wait_or_abort(&s_full[qh], g & 1, &abort_s))) {
         abort_s = 1;
         break;
       }
       tc_fence_after();
-      float sv[kKeys];
-      {
-        uint32_t a[32], b[32];
-        tmem_ld32_async(tm_s + lane_off, a);
-        tmem_ld32_async(tm_s + lane_off + 32, b);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          sv[i] = __uint_as_float(a[i]);
-          sv[32 + i] = __uint_as_float(b[i]);
-        }
-      }
+      // S is read from TMEM twice, 32 columns at a time (the next chunk loads while one is used):
+      // pass 1 takes the row max, pass 2 turns the scores into P.  Only groups that reach past
+      // the half's first position take the causal mask (a CTA-uniform branch).
       const int key0 = g * kKeys;
-      if (key0 + kKeys - 1 > pos0) {  // the group reaches past the tile's first position: causal mask
+      const bool diag = key0 + kKeys - 1 > pos_first;
+      constexpr int NC = kKeys / 32;
+      auto score = [&](auto masked, const uint32_t *cur, int k, int i) {
+        const float v = __uint_as_float(cur[i]);
+        if constexpr (decltype(masked)::value) return key0 + 32 * k + i <= pos ? v : -INFINITY;
+        return v;
+      };
+      auto row_max = [&](auto masked) {
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        uint32_t ca[32], cb[32];
+        tmem_ld32_async(tm_s + lane_off, ca);
 #pragma unroll
-        for (int i = 0; i < kKeys; ++i) sv[i] = (key0 + i <= pos) ? sv[i] : -INFINITY;
-      }
-      // row max with 8 independent chains
-      float mx[8];
+        for (int k = 0; k < NC; ++k) {
+          tmem_wait_ld();
+          const uint32_t *cur = (k & 1) ? cb : ca;
+          if (k + 1 < NC) tmem_ld32_async(tm_s + lane_off + 32 * (k + 1), (k & 1) ? ca : cb);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) mx[j] = sv[j];
-#pragma unroll
-      for (int i = 8; i < kKeys; ++i) mx[i & 7] = fmaxf(mx[i & 7], sv[i]);
-      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+          for (int i = 0; i < 16; ++i)
+            mx[i & 3] = max3f(mx[i & 3], score(masked, cur, k, 2 * i), score(masked, cur, k, 2 * i + 1));
+        }
+        return fmaxf(max3f(mx[0], mx[1], mx[2]), mx[3]);
+      };
+      const float mt = diag ? row_max(std::true_type{}) : row_max(std::false_type{});
       const float mts = mt * c;
       const bool grow = mts > m_run + kRescale;  // m_run = -inf: any finite max
       float alpha = 1.f;
@@ -332,7 +370,7 @@ __global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(Prefill
       }
       if (g > 0 && __any_sync(kFull, grow)) {
         // O is being accumulated by PV(g - 1): wait for it, then rescale this warp's rows
-        if (!__all_sync(kFull, wait_or_abort(&pv_done, (g - 1) & 1, &abort_s))) {
+        if (!__all_sync(kFull, wait_or_abort(&pv_done[qh], (g - 1) & 1, &abort_s))) {
           abort_s = 1;
           break;
         }
@@ -348,76 +386,115 @@ __global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(Prefill
       }
       const float negm = -m_run;
       float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[32];
+      // P of chunk k (16 columns of value pairs) goes to columns [16k, 16k + 16): over S chunks
+      // already read, never over the chunk loading next.  Two scores per packed FMA and add.
+      auto make_p = [&](auto masked) {
+        uint32_t ca[32], cb[32];
+        tmem_ld32_async(tm_s + lane_off, ca);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const float a = ex2_approx(fmaf(sv[2 * i], c, negm)), b = ex2_approx(fmaf(sv[2 * i + 1], c, negm));
-        ps[i & 7] += a + b;
-        pk[i] = pack_pair<T>(a, b);
-      }
+        for (int k = 0; k < NC; ++k) {
+          tmem_wait_ld();
+          const uint32_t *cur = (k & 1) ? cb : ca;
+          if (k + 1 < NC) tmem_ld32_async(tm_s + lane_off + 32 * (k + 1), (k & 1) ? ca : cb);
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float x0, x1;
+            ffma2(x0, x1, score(masked, cur, k, 2 * i), score(masked, cur, k, 2 * i + 1), c, negm);
+            const float a = ex2_approx(x0), b = ex2_approx(x1);
+            fadd2(ps[2 * (i & 3)], ps[2 * (i & 3) + 1], a, b);
+            pk[i] = pack_pair<T>(a, b);
+          }
+          tmem_st16u(tm_s + lane_off + 16 * k, pk);
+        }
+      };
+      if (diag) make_p(std::true_type{});
+      else make_p(std::false_type{});
       const float psum = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       l_run = l_run * alpha + psum;
-      tmem_st32u(tm_s + lane_off, pk);  // P over the first 32 columns of S(g)
       // the last group's V rows past the sequence (stale, or pages never loaded) -> 0
       const int vk = kv_len - key0;
-      if (g == ngroups - 1 && vk < kKeys) {
-        const int iv = ntiles - 1;
+      if (zeroes_v && g == ngroups - 1 && vk < kKeys) {
+        const int iv = 2 * g + 1;
         if (!__all_sync(kFull, wait_or_abort(&full[iv % NSLOT], (iv / NSLOT) & 1, &abort_s))) {
           abort_s = 1;
           break;
         }
         unsigned char *vst = ring + (iv % NSLOT) * TILE;
-        for (int i = t; i < (kKeys - vk) * 8 * NDH; i += kRows) {
+        for (int i = rt; i < (kKeys - vk) * 8 * NDH; i += kRows) {
           const int dh = i / ((kKeys - vk) * 8), rem = i % ((kKeys - vk) * 8);
           *reinterpret_cast<uint4 *>(vst + dh * HALF + (vk + rem / 8) * 128 + (rem % 8) * 16) = make_uint4(0, 0, 0, 0);
         }
         fence_proxy_async();
       }
       tc_fence_before();
-      mbar_arrive(&p_ready[g & 1]);
+      mbar_arrive(&p_ready[qh]);
     }
-  } else if (warp == 4) {
-    // ---- MMA issue ----
+  } else if (warp == 4 * kHalves) {
+    // ---- MMA issue, one thread: S_A(0) S_B(0) | PV_A(g) S_A(g+1) PV_B(g) S_B(g+1) | ... ----
+    // Each half's S overwrites its P only after its PV (MMAs of a thread run in order), and
+    // one half's softmax overlaps the other half's MMAs.
     if (lane == 0) {
       const uint32_t id_s = umma_idesc<T>(kRows, kKeys, 0), id_o = umma_idesc<T>(kRows, D, 1);
-      int landed = 0;
-      for (int i = 0; i < ntiles; ++i) {
-        bool is_v;
-        const int grp = ring_tile(i, ngroups, is_v);
-        const int slot = i % NSLOT;
-        if (is_v && !wait_or_abort(&p_ready[grp & 1], (grp >> 1) & 1, &abort_s)) {
-          abort_s = 1;
-          break;
+      int landed = 0;  // tiles [0, landed) seen complete, in ring order
+      auto wait_tile = [&](int i) {
+        for (; landed <= i; ++landed) {
+          if (!wait_or_abort(&full[landed % NSLOT], (landed / NSLOT) & 1, &abort_s)) return false;
+          fence_proxy_async();  // the copies were generic-proxy writes
         }
-        if (!wait_or_abort(&full[slot], (i / NSLOT) & 1, &abort_s)) {
-          abort_s = 1;
-          break;
-        }
-        landed = i + 1;
-        fence_proxy_async();  // the copies were generic-proxy writes
         tc_fence_after();
-        unsigned char *tl = ring + slot * TILE;
-        if (!is_v) {
-          const uint32_t tm_s = tmem + (grp & 1) * kKeys;
+        return true;
+      };
+      auto issue_s = [&](int h, int g) {
+        unsigned char *qb = sq + h * QB, *kt = ring + ((2 * g) % NSLOT) * TILE;
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk & 3) * 32;  // 16 dims further within the 128-byte row
-            const uint64_t a = umma_desc_sw128(smem_addr(sq + (kk >> 2) * QHALF) + off, 16, 1024);
-            const uint64_t b = umma_desc_sw128(smem_addr(tl + (kk >> 2) * HALF) + off, 16, 1024);
-            umma(tm_s, a, b, id_s, kk > 0);
-          }
-          umma_commit(&s_full[grp & 1]);
-        } else {
-          const uint32_t tm_p = tmem + (grp & 1) * kKeys;
-#pragma unroll
-          for (int kk = 0; kk < kKeys / 16; ++kk) {
-            const uint64_t b = umma_desc_sw128(smem_addr(tl) + kk * 2048, HALF, 1024);
-            umma_ts(tm_o, tm_p + kk * 8, b, id_o, (grp > 0 || kk > 0) ? 1u : 0u);
-          }
-          umma_commit(&pv_done);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk & 3) * 32;  // 16 dims further within the 128-byte row
+          const uint64_t a = umma_desc_sw128(smem_addr(qb + (kk >> 2) * QHALF) + off, 16, 1024);
+          const uint64_t b = umma_desc_sw128(smem_addr(kt + (kk >> 2) * HALF) + off, 16, 1024);
+          umma(tmem + h * 256, a, b, id_s, kk > 0);
         }
-        umma_commit(&empty[slot]);
+        umma_commit(&s_full[h]);
+      };
+      auto issue_pv = [&](int h, int g) {
+        unsigned char *vt = ring + ((2 * g + 1) % NSLOT) * TILE;
+#pragma unroll
+        for (int kk = 0; kk < kKeys / 16; ++kk) {
+          const uint64_t b = umma_desc_sw128(smem_addr(vt) + kk * 2048, HALF, 1024);
+          umma_ts(tmem + h * 256 + kKeys, tmem + h * 256 + kk * 8, b, id_o, (g > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&pv_done[h]);
+      };
+      bool ok = wait_tile(0);
+      if (ok) {
+#pragma unroll
+        for (int h = 0; h < kHalves; ++h)
+          if (ng[h] > 0) issue_s(h, 0);
+        umma_commit(&empty[0]);
       }
+      for (int g = 0; g < ngroups && ok; ++g) {
+#pragma unroll
+        for (int h = 0; h < kHalves && ok; ++h) {
+          if (g < ng[h]) {
+            if (!wait_or_abort(&p_ready[h], g & 1, &abort_s) || !wait_tile(2 * g + 1)) {
+              ok = false;
+              break;
+            }
+            issue_pv(h, g);
+          }
+          if (g + 1 < ng[h]) {
+            if (!wait_tile(2 * g + 2)) {
+              ok = false;
+              break;
+            }
+            issue_s(h, g + 1);
+          }
+        }
+        if (!ok) break;
+        umma_commit(&empty[(2 * g + 1) % NSLOT]);                      // V(g): its PVs are issued
+        if (g + 1 < ngroups) umma_commit(&empty[(2 * g + 2) % NSLOT]);  // K(g+1): its S MMAs are issued
+      }
+      if (!ok) abort_s = 1;
       mma_landed_s = landed;
     }
   } else {
@@ -443,9 +520,9 @@ __global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(Prefill
         abort_s = 1;
         break;
       }
-      bool is_v;
-      const int grp = ring_tile(i, ngroups, is_v);
-      const int first = grp * (kKeys / kBS), n = min(kKeys / kBS, npages - first);
+      const bool is_v = i & 1;
+      const int grp = i >> 1;
+      const int first = grp * PAGES, n = min(PAGES, npages - first);
       const int w = first >> 5;
       int &cw = is_v ? vw : kw, &cur = is_v ? vcur : kcur, &nxt = is_v ? vnxt : knxt;
       if (w != cw) {  // groups advance one at a time, so w == cw + 1
@@ -456,14 +533,14 @@ __global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(Prefill
       const T *pool = static_cast<const T *>(is_v ? p.v_pool : p.k_pool);
       unsigned char *dst = ring + slot * TILE + dh * HALF;
 #pragma unroll
-      for (int j = 0; j < kKeys / kBS; ++j) {
+      for (int j = 0; j < PAGES; ++j) {
         const int pid = __shfl_sync(kFull, cur, (first & 31) + j);
         if (j < n) {
           const T *src = pool + (size_t(pid) * p.num_kv_heads + kvh) * (kBS * D) + cc * 8;
 #pragma unroll
           for (int k = 0; k < IPP; ++k) {
-            const int r = r0 + k * RPI;          // row within the page
-            const int kr = j * kBS + r;          // key row within the tile
+            const int r = r0 + k * RPI;  // row within the page
+            const int kr = j * kBS + r;  // key row within the tile
             cp_async16(dst + kr * 128 + ((ch ^ (kr & 7)) << 4), src + r * D);
           }
         }
@@ -478,10 +555,10 @@ __global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(Prefill
   // join: every role has left its loop; then drain MMAs and copies in flight
   __syncthreads();
   bool ok_end = !abort_s;
-  if (warp == 4 && lane == 0) {
+  if (warp == 4 * kHalves && lane == 0) {
     umma_commit(&drain);
     if (!mbar_wait_bounded(&drain, 0)) ok_end = false;
-  } else if (warp == 5 && lane == 0) {
+  } else if (warp == 4 * kHalves + 1 && lane == 0) {
     // the copies are complete (cp.async.wait_all); their barrier arrives must land before the CTA exits
     for (int i = mma_landed_s; i < issued_s; ++i)
       if (!mbar_wait_bounded(&full[i % NSLOT], (i / NSLOT) & 1)) ok_end = false;
@@ -490,9 +567,10 @@ __global__ void __launch_bounds__(kThreads5, 2) paged_prefill_tc5_kernel(Prefill
   const bool all_ok = __syncthreads_and(ok_end);
   tc_fence_after();
   if (all_ok) {
-    if (warp < 4) {
-      // O row / l -> out; every softmax thread takes part in the warp-collective TMEM loads
-      const uint32_t lane_off = uint32_t(warp * 32) << 16;
+    if (warp < 4 * kHalves && ng_q > 0) {
+      // O row / l -> out; every thread of the half takes part in the warp-collective TMEM loads
+      const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
+      const uint32_t tm_o = tmem + qh * 256 + kKeys;
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
       T *orow = static_cast<T *>(p.out) +
                 ((size_t(row0) + (rvalid ? tok : 0)) * p.num_kv_heads * G + size_t(kvh) * G + (rvalid ? head : 0)) * D;
@@ -533,7 +611,8 @@ cudaError_t launch_t5(const Prefill5Params &p, int num_tiles, cudaStream_t strea
     if (e != cudaSuccess) return e;
     attr_done[dev] = true;
   }
-  dim3 grid(num_tiles, p.num_kv_heads);
+  if (num_tiles > 65535) return cudaErrorInvalidValue;
+  dim3 grid(p.num_kv_heads, num_tiles);
   kern<<<grid, kThreads5, smem, stream>>>(p);
   return cudaGetLastError();
 }
@@ -564,7 +643,7 @@ bool prefill_tc5_enabled() {
 
 int prefill_tc5_tokens_per_tile(int group) {
   const int rpt = group <= 1 ? 1 : group <= 2 ? 2 : group <= 4 ? 4 : 8;
-  return kRows / rpt;
+  return kHalves * kRows / rpt;
 }
 
 cudaError_t launch_prefill_tc5(const void *q, void *out, const int32_t *block_tables, int max_blocks_per_seq,
