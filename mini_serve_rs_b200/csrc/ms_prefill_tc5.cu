@@ -47,7 +47,8 @@ namespace {
 
 constexpr int kRows = 128;     // query rows per CTA = TMEM lanes
 constexpr int kKeys = 128;     // keys per group (8 pages): the S MMA is M 128 x N 128
-constexpr float kRescale = 8.0f;  // move the running max only when it grows by more than 2^8
+constexpr float kRescale = 8.0f;
+constexpr int kExp2OnFma = 3;  // of every 8 score pairs, this many take 2^x on the FMA pipe (exp2_poly2)  // move the running max only when it grows by more than 2^8
 
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
   uint64_t d = uint64_t((addr >> 4) & 0x3fff);
@@ -201,6 +202,41 @@ __device__ __forceinline__ void fadd2(float &d0, float &d1, float a0, float a1) 
       : "+f"(d0), "+f"(d1)
       : "f"(a0), "f"(a1));
 }
+// (d0, d1) = (a0, a1) + (b0, b1) and (d0, d1) = (a0, a1) * (b0, b1) + (c0, c1), packed f32x2
+__device__ __forceinline__ void add2(float &d0, float &d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void fma2(float &d0, float &d1, float a0, float a1, float b0, float b1, float c0,
+                                     float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+// 2^x for two x <= 8 on the FMA and integer pipes instead of the transcendental unit
+// (Cody and Waite's argument split): j = rint(x) by adding and subtracting 1.5 * 2^23,
+// f = x - j in [-0.5, 0.5], 2^f by a cubic fitted here for relative error on [-0.5, 0.5]
+// (7.5e-5 at most in f32 Horner form), and j added to the exponent field.  x is clamped at
+// -126 so the exponent never underflows into the sign (masked scores give ~1e-38, not 0).
+__device__ __forceinline__ void exp2_poly2(float &y0, float &y1, float x0, float x1) {
+  constexpr float kR = 12582912.f;  // 1.5 * 2^23: adding it rounds to an integer in the low mantissa bits
+  constexpr float c0 = 0.99992812f, c1 = 0.69326097f, c2 = 0.24261054f, c3 = 0.05517132f;
+  x0 = fmaxf(x0, -126.f);
+  x1 = fmaxf(x1, -126.f);
+  float t0, t1, j0, j1, f0, f1, p0, p1;
+  add2(t0, t1, x0, x1, kR, kR);
+  add2(j0, j1, t0, t1, -kR, -kR);
+  add2(f0, f1, x0, x1, -j0, -j1);
+  fma2(p0, p1, f0, f1, c3, c3, c2, c2);
+  fma2(p0, p1, p0, p1, f0, f1, c1, c1);
+  fma2(p0, p1, p0, p1, f0, f1, c0, c0);
+  // bits(t) = bits(1.5 * 2^23) + j, whose low 9 bits are zero: bits(t) << 23 == j << 23 (mod 2^32)
+  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -281,7 +317,7 @@ __global__ void __launch_bounds__(kThreads5, 1) paged_prefill_tc5_kernel(Prefill
     }
     for (int h = 0; h < kHalves; ++h) {
       mbar_init(&s_full[h], 1);
-      mbar_init(&p_ready[h], kRows);
+      mbar_init(&p_ready[h], 4);  // one arrive per softmax warp of the half
       mbar_init(&pv_done[h], 1);
     }
     mbar_init(&drain, 1);
@@ -399,9 +435,14 @@ __global__ void __launch_bounds__(kThreads5, 1) paged_prefill_tc5_kernel(Prefill
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            float x0, x1;
+            float x0, x1, a, b;
             ffma2(x0, x1, score(masked, cur, k, 2 * i), score(masked, cur, k, 2 * i + 1), c, negm);
-            const float a = ex2_approx(x0), b = ex2_approx(x1);
+            if ((i & 7) < kExp2OnFma) {  // a share of the exponentials off the transcendental unit
+              exp2_poly2(a, b, x0, x1);
+            } else {
+              a = ex2_approx(x0);
+              b = ex2_approx(x1);
+            }
             fadd2(ps[2 * (i & 3)], ps[2 * (i & 3) + 1], a, b);
             pk[i] = pack_pair<T>(a, b);
           }
@@ -428,7 +469,8 @@ __global__ void __launch_bounds__(kThreads5, 1) paged_prefill_tc5_kernel(Prefill
         fence_proxy_async();
       }
       tc_fence_before();
-      mbar_arrive(&p_ready[qh]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_ready[qh]);
     }
   } else if (warp == 4 * kHalves) {
     // ---- MMA issue, one thread: S_A(0) S_B(0) | PV_A(g) S_A(g+1) PV_B(g) S_B(g+1) | ... ----
@@ -445,24 +487,28 @@ __global__ void __launch_bounds__(kThreads5, 1) paged_prefill_tc5_kernel(Prefill
         tc_fence_after();
         return true;
       };
+      // Descriptors are built once; an operand at byte offset o from a base is the base
+      // descriptor + (o >> 4) (the 14-bit start field cannot carry: shared addresses are < 256 KiB),
+      // so the MMAs below issue back to back.
+      const uint64_t dq = umma_desc_sw128(smem_addr(sq), 16, 1024);         // Q, K-major
+      const uint64_t dk = umma_desc_sw128(smem_addr(ring), 16, 1024);       // K tiles, K-major
+      const uint64_t dv = umma_desc_sw128(smem_addr(ring), HALF, 1024);     // V tiles, MN-major
       auto issue_s = [&](int h, int g) {
-        unsigned char *qb = sq + h * QB, *kt = ring + ((2 * g) % NSLOT) * TILE;
+        const uint64_t a0 = dq + uint64_t((h * QB) >> 4), b0 = dk + uint64_t((((2 * g) % NSLOT) * TILE) >> 4);
+        const uint32_t d = tmem + h * 256;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk & 3) * 32;  // 16 dims further within the 128-byte row
-          const uint64_t a = umma_desc_sw128(smem_addr(qb + (kk >> 2) * QHALF) + off, 16, 1024);
-          const uint64_t b = umma_desc_sw128(smem_addr(kt + (kk >> 2) * HALF) + off, 16, 1024);
-          umma(tmem + h * 256, a, b, id_s, kk > 0);
+          const uint32_t off = (((kk >> 2) * QHALF + (kk & 3) * 32) >> 4), offk = (((kk >> 2) * HALF + (kk & 3) * 32) >> 4);
+          umma(d, a0 + off, b0 + offk, id_s, kk > 0);
         }
         umma_commit(&s_full[h]);
       };
       auto issue_pv = [&](int h, int g) {
-        unsigned char *vt = ring + ((2 * g + 1) % NSLOT) * TILE;
+        const uint64_t b0 = dv + uint64_t((((2 * g + 1) % NSLOT) * TILE) >> 4);
+        const uint32_t d = tmem + h * 256 + kKeys, a = tmem + h * 256;
+        const uint32_t acc0 = g > 0 ? 1u : 0u;
 #pragma unroll
-        for (int kk = 0; kk < kKeys / 16; ++kk) {
-          const uint64_t b = umma_desc_sw128(smem_addr(vt) + kk * 2048, HALF, 1024);
-          umma_ts(tmem + h * 256 + kKeys, tmem + h * 256 + kk * 8, b, id_o, (g > 0 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < kKeys / 16; ++kk) umma_ts(d, a + kk * 8, b0 + uint64_t((kk * 2048) >> 4), id_o, kk > 0 ? 1u : acc0);
         umma_commit(&pv_done[h]);
       };
       bool ok = wait_tile(0);
