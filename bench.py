@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--requests", type=int, default=1024, help="requests in the --config4 trace")
     ap.add_argument("--token-budget", type=int, default=2048, help="packed tokens per step for --config4")
     ap.add_argument("--max-active", type=int, default=512, help="concurrent requests per replica for --config4")
+    ap.add_argument("--http", action="store_true",
+                    help="--config4 through the HTTP/SSE driver: each replica serves /v1/completions and an "
+                         "in-process client replays the trace (examples/bench.rs metrics)")
     ap.add_argument("--kernel", choices=["attention", "norm_rope", "sample", "prefill"], default=None,
                     help="time one kernel in isolation (BASELINE config 2 for attention) instead of the step")
     return ap.parse_args()
@@ -440,13 +443,27 @@ def run_config4(args, rank, world, local):
     warm.run([Request(rid=10_000_000 + k, prompt=list(range(100 + 37 * k)), max_tokens=8) for k in range(4)])
     pages.close()
     pages = E.Pages(pool_blocks, 16, max_chunks=pool_blocks // 2)
-    loop = ServingLoop(eng, pages, max_active, args.token_budget)
-    if world > 1:
-        dist.barrier()
-    with ClockSampler(local) as clk:
-        elapsed = loop.run(reqs, timeout_s=900.0)
-    summ = summarize(loop.finished, elapsed)
-    summ["steps"] = loop.steps
+    if args.http:
+        from mini_serve_rs_b200.http_driver import BackgroundHttp, ServingServer, run_trace_process, summarize_http
+        srv = ServingServer(eng, pages, model="qwen3-0.6b-arch", max_active=max_active,
+                            token_budget=args.token_budget).start()
+        http = BackgroundHttp(srv).start()
+        if world > 1:
+            dist.barrier()
+        with ClockSampler(local) as clk:
+            results, elapsed = run_trace_process(http.url, "qwen3-0.6b-arch", reqs, timeout_s=900.0)
+        http.stop()
+        srv.stop()
+        summ = summarize_http(results, elapsed)
+        summ["steps"] = srv.steps
+    else:
+        loop = ServingLoop(eng, pages, max_active, args.token_budget)
+        if world > 1:
+            dist.barrier()
+        with ClockSampler(local) as clk:
+            elapsed = loop.run(reqs, timeout_s=900.0)
+        summ = summarize(loop.finished, elapsed)
+        summ["steps"] = loop.steps
     summ["prefix"] = pages.stats()
     summ["clocks"] = clk.summary()
     summ["gpu_launches"] = eng.profile()[0]
@@ -460,13 +477,16 @@ def run_config4(args, rank, world, local):
         span = max(x["elapsed_s"] for x in alls)
         agg = tokens / span
         print(json.dumps({
-            "metric": "serving trace decode tokens/s (BASELINE config 4)", "value": agg, "unit": UNIT,
+            "metric": "serving trace decode tokens/s (BASELINE config 4)" + (" via HTTP/SSE" if args.http else ""),
+            "value": agg, "unit": UNIT,
             "n_gpus": world, "higher_is_better": True, "scaling": "weak", "dtype": "bf16",
             "data": "synthetic seeded trace (random-init Qwen3-0.6B-arch weights)",
             "config": {"workload": "BASELINE config 4", "requests": args.requests, "arrival_rate_per_s": 64,
                        "prompt": "lognormal median 512 sigma 1.0 clipped [16,8192], 30% shared 1024-token prefix",
                        "output": "uniform[32,1024]", "token_budget": args.token_budget, "max_active": max_active,
-                       "sampling": "greedy", "routing": "round-robin over replicas"},
+                       "sampling": "greedy", "routing": "round-robin over replicas",
+                       "driver": ("POST /v1/completions stream=true, trace client in its own process"
+                                  if args.http else "ServingLoop in process")},
             "tokens_per_s_per_gpu": agg / world, "tokens": tokens, "elapsed_s": span,
             "ttft_ms_p50": alls[0]["ttft_ms_p50"], "ttft_ms_p90": alls[0]["ttft_ms_p90"],
             "ttft_ms_p99": alls[0]["ttft_ms_p99"], "per_rank": alls}), flush=True)
