@@ -96,3 +96,58 @@ def test_prefill_matches_fp32_causal_reference(group, head_dim, dt):
 
 def test_prefill_long_chunk_with_prefix():
     assert _case(2, 128, torch.bfloat16, [(1000, 300), (0, 700)], seed=5, pool=256) <= 2e-2
+
+
+def _case_large(group, head_dim, dt, chunks, seed, hkv=2):
+    """As _case at bench scale: pages in a random permutation of a NaN-filled
+    pool, fp32 reference computed with torch on the GPU (masked softmax per
+    chunk and kv head)."""
+    lib = E.lib()
+    gen = torch.Generator(device=DEV).manual_seed(seed)
+    hq = hkv * group
+    T = sum(n for _, n in chunks)
+    mb = max((st + n + 15) // 16 for st, n in chunks)
+    pool = sum((st + n + 15) // 16 for st, n in chunks) + 7
+    perm = torch.randperm(pool, device=DEV, generator=gen)
+    tables = torch.zeros(len(chunks), mb, dtype=torch.int32, device=DEV)
+    kp = torch.full((pool, hkv, 16, head_dim), float("nan"), dtype=dt, device=DEV)
+    vp = torch.full_like(kp, float("nan"))
+    q = torch.randn(T, hq, head_dim, generator=gen, device=DEV).to(dt)
+    want = torch.empty(T, hq, head_dim, device=DEV)
+    scale = 1.0 / math.sqrt(head_dim)
+    off = r = 0
+    for i, (st, n) in enumerate(chunks):
+        L = st + n
+        nb = (L + 15) // 16
+        tables[i, :nb] = perm[off:off + nb].to(torch.int32)
+        off += nb
+        k = torch.randn(L, hkv, head_dim, generator=gen, device=DEV).to(dt)
+        v = torch.randn(L, hkv, head_dim, generator=gen, device=DEV).to(dt)
+        pos = torch.arange(L, device=DEV)
+        pages = tables[i, pos // 16].long()
+        kp[pages, :, pos % 16] = k
+        vp[pages, :, pos % 16] = v
+        qpos = st + torch.arange(n, device=DEV)
+        mask = torch.arange(L, device=DEV)[None, :] > qpos[:, None]  # (n, L): key after the row's position
+        for h in range(hkv):
+            qh = q[r:r + n, h * group:(h + 1) * group].float()                 # (n, G, D)
+            s = torch.einsum("ngd,ld->ngl", qh, k[:, h].float()) * scale
+            s = s.masked_fill(mask[:, None, :], float("-inf"))
+            want[r:r + n, h * group:(h + 1) * group] = torch.einsum("ngl,ld->ngd", torch.softmax(s, -1),
+                                                                    v[:, h].float())
+        r += n
+    tiles, nt = _tiles(lib, chunks, hq, hkv)
+    out = torch.full((T, hq, head_dim), float("nan"), dtype=dt, device=DEV)
+    sync_ok(lib.ms_launch_paged_prefill(ptr(q), ptr(kp), ptr(vp), ptr(tables), mb, ptr(tiles), nt, ptr(out), hq,
+                                        hkv, head_dim, 16, scale, E.torch_dtype_code(q), None), "prefill")
+    assert torch.isfinite(out).all()
+    return float((out.float() - want).abs().max())
+
+
+@pytest.mark.parametrize("group,head_dim,dt", [(2, 128, torch.bfloat16), (7, 128, torch.bfloat16),
+                                               (1, 64, torch.float16)])
+def test_prefill_4096_token_prompts_against_torch_fp32(group, head_dim, dt):
+    # a full 4096-token prompt, cached prefixes at offsets that are not multiples of 128 (or 16),
+    # a chunk that starts past a page boundary: up to 257 key pages, ~36 tiles per sequence
+    chunks = [(0, 4096), (513, 1536), (3001, 999), (16, 240)]
+    assert _case_large(group, head_dim, dt, chunks, seed=group + head_dim) <= 2e-2
