@@ -47,8 +47,8 @@ namespace {
 
 constexpr int kRows = 128;     // query rows per CTA = TMEM lanes
 constexpr int kKeys = 128;     // keys per group (8 pages): the S MMA is M 128 x N 128
-constexpr float kRescale = 8.0f;
-constexpr int kExp2OnFma = 3;  // of every 8 score pairs, this many take 2^x on the FMA pipe (exp2_poly2)  // move the running max only when it grows by more than 2^8
+constexpr float kRescale = 8.0f;  // move the running max only when it grows by more than 2^8
+constexpr int kExp2OnFma = 3;     // of every 8 score pairs, this many take 2^x on the FMA pipe (exp2_poly2)
 
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
   uint64_t d = uint64_t((addr >> 4) & 0x3fff);
