@@ -238,6 +238,7 @@ class ServingServer:
         self._idle = idle_wait_s
         self.healthy = True
         self.steps = 0
+        self.cancelled = 0
         self._pending: Dict[asyncio.AbstractEventLoop, List] = {}
         self._thread = threading.Thread(target=self._run, name="ms-engine", daemon=True)
 
@@ -268,6 +269,10 @@ class ServingServer:
         self._inbox.put(_Sub(aloop, q, r))
         return rid
 
+    def cancel(self, rid: int):
+        """The client went away: drop the request, or release its sequence and pages."""
+        self._inbox.put(rid)
+
     # -- engine thread
     def _post(self, sub: _Sub, ev: Tuple):
         """Queue an event; _flush hands each event loop its events in one wake-up."""
@@ -284,13 +289,32 @@ class ServingServer:
         except queue.Empty:
             return
         while True:
-            sub.req.arrival = self.sl.clock()
-            self.sl.submit(sub.req)
-            self._subs[sub.req.rid] = sub
+            if isinstance(sub, _Sub):
+                sub.req.arrival = self.sl.clock()
+                self.sl.submit(sub.req)
+                self._subs[sub.req.rid] = sub
+            else:
+                self._cancel(sub)
             try:
                 sub = self._inbox.get_nowait()
             except queue.Empty:
                 return
+
+    def _cancel(self, rid: int):
+        sl = self.sl
+        sub = self._subs.pop(rid, None)
+        if sub is None:  # already finished
+            return
+        r = sub.req
+        if r in sl.queue:
+            sl.queue.remove(r)
+        elif r in sl.active:
+            sl.active.remove(r)
+            sl.eng.release(rid)
+            sl.pages.release(rid)
+        r.error = "Request cancelled: client disconnected"
+        r.done_at = sl.clock()
+        self.cancelled += 1
 
     def _publish(self):
         for rid in list(self._subs):
@@ -364,7 +388,7 @@ def make_app(server: ServingServer):
             stream = bool(body.get("stream", False))
             model = str(body.get("model", server.model))
             q: asyncio.Queue = asyncio.Queue()
-            server.submit(prompt, max_tokens, temperature, top_p, asyncio.get_running_loop(), q)
+            rid = server.submit(prompt, max_tokens, temperature, top_p, asyncio.get_running_loop(), q)
         except ApiError as e:
             return e.response()
         except (TypeError, ValueError) as e:
@@ -386,22 +410,34 @@ def make_app(server: ServingServer):
             pre, post = head.split("\\u0000")
             pre = "data: " + pre + " "
             post = post + "\n\n"
-            while True:
-                ev = await q.get()
-                if ev[0] == "token":
-                    await resp.write(f"{pre}{ev[1]}{post}".encode())
-                elif ev[0] == "done":
-                    await resp.write(f"data: {json.dumps(chunk('', ev[1], ev[2]))}\n\ndata: [DONE]\n\n".encode())
-                    break
-                else:
-                    err = {"error": {"message": ev[1], "type": "server_error", "code": 500}}
-                    await resp.write(f"data: {json.dumps(err)}\n\n".encode())
-                    break
-            await resp.write_eof()
+            finished = False
+            try:
+                while True:
+                    ev = await q.get()
+                    if ev[0] == "token":
+                        await resp.write(f"{pre}{ev[1]}{post}".encode())
+                    elif ev[0] == "done":
+                        finished = True
+                        await resp.write(f"data: {json.dumps(chunk('', ev[1], ev[2]))}\n\ndata: [DONE]\n\n".encode())
+                        break
+                    else:
+                        finished = True
+                        err = {"error": {"message": ev[1], "type": "server_error", "code": 500}}
+                        await resp.write(f"data: {json.dumps(err)}\n\n".encode())
+                        break
+                await resp.write_eof()
+            except (ConnectionError, asyncio.CancelledError):
+                if not finished:  # the client went away mid-stream
+                    server.cancel(rid)
+                raise
             return resp
         text = []
         while True:
-            ev = await q.get()
+            try:
+                ev = await q.get()
+            except asyncio.CancelledError:  # the client went away
+                server.cancel(rid)
+                raise
             if ev[0] == "token":
                 text.append(f" {ev[1]}")
             elif ev[0] == "done":

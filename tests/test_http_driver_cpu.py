@@ -207,3 +207,31 @@ def test_trace_client_in_its_own_process(served):
     for q, r in zip(reqs, results):
         assert [int(x) for x in r.text.split()] == [expected_token(q.prompt, t) for t in range(4)]
     assert summarize_http(results, elapsed)["failed"] == 0
+
+
+def test_client_disconnect_cancels_the_request(served):
+    """A client that drops its stream mid-way releases the request's sequence
+    and pages (the reference's RequestCancelled path) instead of generating
+    to max_tokens."""
+    url, srv, eng, pages = served
+
+    async def go():
+        async with aiohttp.ClientSession() as s:
+            resp = await s.post(f"{url}/v1/completions", json={"prompt": list(range(1, 30)), "max_tokens": 900,
+                                                               "temperature": 0, "stream": True})
+            assert resp.status == 200
+            got = 0
+            async for _ in resp.content.iter_any():
+                got += 1
+                if got >= 3:
+                    break
+            resp.close()  # drop the connection mid-stream
+
+    asyncio.run(go())
+    deadline = time.time() + 10
+    while time.time() < deadline and (eng.seqs or srv.cancelled == 0):
+        time.sleep(0.01)
+    assert srv.cancelled == 1 and not eng.seqs
+    st = pages.stats()
+    assert st["free_blocks"] + st["cache_only_blocks"] == 512, st
+    assert eng.steps < 600  # stopped long before 900 tokens
