@@ -362,6 +362,10 @@ class ServingServer:
                 self.healthy = False
                 self._fail_all(str(e))
                 continue
+            except Exception as e:  # a host-side failure must not leave handlers waiting for ever
+                self.healthy = False
+                self._fail_all(f"serving loop failed: {e!r}")
+                continue
             if ran:
                 self.steps += 1
             self._publish()

@@ -235,3 +235,15 @@ def test_client_disconnect_cancels_the_request(served):
     st = pages.stats()
     assert st["free_blocks"] + st["cache_only_blocks"] == 512, st
     assert eng.steps < 600  # stopped long before 900 tokens
+
+
+def test_host_failure_in_the_loop_fails_requests_instead_of_hanging(served):
+    url, srv, eng, pages = served
+
+    def boom(*a, **k):
+        raise RuntimeError("host-side bug")
+    eng.step = boom
+    st, _, raw = asyncio.run(_post(url, {"prompt": [4, 5], "max_tokens": 3}))
+    assert st == 500 and "serving loop failed" in json.loads(raw)["error"]["message"]
+    st, ready = asyncio.run(_get(url, "/ready"))
+    assert st == 503
