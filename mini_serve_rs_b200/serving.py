@@ -88,10 +88,12 @@ class ServingLoop:
     def _grow(self, now: float):
         failed = []
         for r in self.active:
-            c = self.eng.cached_tokens(r.rid)
             if r.prefilled:
-                reach = c + 1
+                # the cache holds the prompt and every generated token but the last (the next
+                # input): no engine call per decoding request per step
+                reach = len(r.prompt) + len(r.out)
             else:
+                c = self.eng.cached_tokens(r.rid)
                 rem = len(r.prompt) - c
                 reach = c + (min(rem, self.token_budget) if self.token_budget else rem)
             try:
