@@ -3,33 +3,38 @@
 //
 // Same contract as the mma.sync build (ms_prefill_tc.cu; the prefill branch
 // of Attention::forward, src/backends/qwen2.rs:329-345, causal mask of
-// :476-503 incl. the offset columns of a cached prefix), but a CTA takes 128
-// query rows: TPB = 128 / RPT tokens x the G query heads of one KV head
-// (RPT = G rounded up to 1, 2, 4 or 8; padding rows are computed like the
-// tile's first row and not stored).  Softmax thread t owns row t, which is
-// TMEM lane t, so the softmax needs no shuffles.
+// :476-503 incl. the offset columns of a cached prefix).  A CTA takes 256
+// query rows of one KV head in two halves of 128 (the TMEM lanes), TPH = 128
+// / RPT tokens x the G query heads each (RPT = G rounded up to 1, 2, 4 or 8;
+// padding rows are computed like the half's first row and not stored).  The
+// halves share every K/V tile.  Softmax thread t owns row t % 128 of its
+// half, which is its TMEM lane, so the softmax needs no shuffles.  Grid: (KV
+// heads, tiles); the host lists tiles longest first.
 //
-// Keys go in groups of 64 (4 pages).  The CTA has three roles that meet only
+// Keys go in groups of 128 (8 pages).  The CTA has three roles that meet only
 // at mbarriers:
-//   * warps 0-3, softmax: for group g, wait until S(g) is in TMEM, tcgen05.ld
-//     the row, mask causally (only groups that reach past the tile's first
-//     position), and run the online softmax in base 2 with the scale folded
-//     into one FMA before ex2.  The running max moves only when the group's
-//     max exceeds it by more than 8 (then the warp rescales its O rows in
-//     TMEM after the previous PV finished), so P = 2^(s - m) stays <= 256.
-//     P, rounded to the K/V type, is stored back over S(g)'s own TMEM columns
-//     (two 16-bit values per column) and the warp arrives on p_ready;
-//   * warp 4, one thread, MMAs in the order S0 S1 PV0 S2 PV1 ... : S(g) = Q
-//     K(g)^T (D/16 MMAs, M 128, N 64, K-major Q and K from shared memory)
-//     into S buffer g & 1, so S(g+1) runs while the softmax works on S(g);
-//     O += P(g) V(g) (4 MMAs, M 128, N D, A = P read from TMEM, V an MN-major
-//     operand).  MMAs of one thread run in order, so S(g+2) overwrites the
-//     buffer only after PV(g) read P(g) from it;
-//   * warp 5, one thread, TMA: the K and V tiles (16 KB each for D = 128) in
-//     the order the MMAs consume them, through a ring of shared-memory slots
-//     freed by tcgen05.commit of the consuming MMA.
-// Shared memory: Q (128 x D) + 4 slots = 96 KiB for D = 128, so two CTAs
-// share an SM; TMEM: 256 columns per CTA (S0, S1, O).
+//   * warps 0-7, softmax, 4 per half: for group g, wait until S(g) is in
+//     TMEM, read the row twice, 32 columns at a time (row max, then P), mask
+//     causally (only groups that reach past the half's first position), and
+//     run the online softmax in base 2 with the scale folded into one FMA
+//     before 2^x.  The running max moves only when the group's max exceeds it
+//     by more than 8 (then the warp rescales its O rows in TMEM), so
+//     P = 2^(s - m) stays <= 256.  P, rounded to the K/V type, is stored over
+//     S(g)'s own TMEM columns (two 16-bit values per column) and the warp
+//     arrives on p_ready;
+//   * warp 8, one thread, MMAs in the order S_A(0) S_B(0) | PV_A(g) S_A(g+1)
+//     PV_B(g) S_B(g+1) | ...: S = Q K(g)^T (M 128, N 128, K-major Q and K from
+//     shared memory), O += P(g) V(g) (A = P read from TMEM, V an MN-major
+//     operand).  MMAs of one thread run in order, so S(g+1) overwrites P(g)
+//     only after PV(g) read it, and one half's softmax overlaps the other
+//     half's MMAs;
+//   * warp 9, copies: the K and V tiles (32 KB each for D = 128) by cp.async
+//     in the order the MMAs consume them, through a ring of shared-memory
+//     slots freed by tcgen05.commit of the consuming MMAs; each lane arrives
+//     on the slot's barrier once its copies complete.
+// Shared memory: Q (2 x 128 x D) + 4 slots of 32 KB = 193 KiB for D = 128
+// (8 slots of 16 KB for D = 64), one CTA per SM; TMEM: 512 columns (per half
+// S/P 128 + O D).
 //
 // Every wait is bounded (mbarrier polls that also watch a CTA abort flag);
 // on expiry the CTA records kStatusWaitTimeout, drains its MMAs and copies
