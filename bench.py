@@ -54,8 +54,11 @@ def parse():
     ap.add_argument("--token-budget", type=int, default=2048, help="packed tokens per step for --config4")
     ap.add_argument("--max-active", type=int, default=512, help="concurrent requests per replica for --config4")
     ap.add_argument("--http", action="store_true",
-                    help="--config4 through the HTTP/SSE driver: each replica serves /v1/completions and an "
-                         "in-process client replays the trace (examples/bench.rs metrics)")
+                    help="--config4 through the HTTP/SSE driver: each replica serves /v1/completions and a "
+                         "client process replays the trace (examples/bench.rs metrics)")
+    ap.add_argument("--http-frontend", choices=["process", "thread"], default="process",
+                    help="with --http: the aiohttp front-end in its own process (default) or on a thread of "
+                         "the engine process")
     ap.add_argument("--kernel", choices=["attention", "norm_rope", "sample", "prefill"], default=None,
                     help="time one kernel in isolation (BASELINE config 2 for attention) instead of the step")
     return ap.parse_args()
@@ -444,10 +447,11 @@ def run_config4(args, rank, world, local):
     pages.close()
     pages = E.Pages(pool_blocks, 16, max_chunks=pool_blocks // 2)
     if args.http:
-        from mini_serve_rs_b200.http_driver import BackgroundHttp, ServingServer, run_trace_process, summarize_http
+        from mini_serve_rs_b200.http_driver import (BackgroundHttp, HttpFrontendProcess, ServingServer,
+                                                    run_trace_process, summarize_http)
         srv = ServingServer(eng, pages, model="qwen3-0.6b-arch", max_active=max_active,
                             token_budget=args.token_budget).start()
-        http = BackgroundHttp(srv).start()
+        http = (HttpFrontendProcess if args.http_frontend == "process" else BackgroundHttp)(srv).start()
         if world > 1:
             dist.barrier()
         with ClockSampler(local) as clk:
@@ -485,8 +489,8 @@ def run_config4(args, rank, world, local):
                        "prompt": "lognormal median 512 sigma 1.0 clipped [16,8192], 30% shared 1024-token prefix",
                        "output": "uniform[32,1024]", "token_budget": args.token_budget, "max_active": max_active,
                        "sampling": "greedy", "routing": "round-robin over replicas",
-                       "driver": ("POST /v1/completions stream=true, trace client in its own process"
-                                  if args.http else "ServingLoop in process")},
+                       "driver": (f"POST /v1/completions stream=true, HTTP front-end: {args.http_frontend}, "
+                                  "trace client in its own process" if args.http else "ServingLoop in process")},
             "tokens_per_s_per_gpu": agg / world, "tokens": tokens, "elapsed_s": span,
             "ttft_ms_p50": alls[0]["ttft_ms_p50"], "ttft_ms_p90": alls[0]["ttft_ms_p90"],
             "ttft_ms_p99": alls[0]["ttft_ms_p99"], "per_rank": alls}), flush=True)

@@ -20,7 +20,11 @@ start second in "created" (the reference stamps each chunk).
 
 One engine thread owns the ServingLoop (continuous batching: admission,
 growth, one ragged ms_step per iteration) and posts each new token to the
-waiting handler's asyncio queue.
+waiting handler's asyncio queue.  The aiohttp front-end runs either on a
+thread of the engine's process (BackgroundHttp) or in a process of its own
+(HttpFrontendProcess), which keeps the per-token SSE work out of the engine
+process's interpreter: one pipe message per engine step carries every new
+token, and the reference's single tokio process has no such contention.
 
 Client: CompletionStream restates the reference's incremental SSE parser
 (src/sse.rs:1-131); stream_completion measures one request as
@@ -205,6 +209,16 @@ def parse_prompt(prompt, vocab_size: int) -> List[int]:
     return ids
 
 
+def _admission_check(healthy: bool, max_context: int, prompt: List[int], max_tokens: int):
+    """The checks a submission passes before it reaches the engine."""
+    if not healthy:
+        raise ApiError("NoHealthyWorkers", "the engine is quarantined")
+    if max_tokens < 1:
+        raise ApiError("InvalidRequest", "max_tokens must be at least 1")
+    if len(prompt) + max_tokens > max_context:
+        raise ApiError("TokenLimitExceeded", f"prompt ({len(prompt)}) + max_tokens ({max_tokens}) > {max_context}")
+
+
 def _deliver(evs):
     for q, ev in evs:
         q.put_nowait(ev)
@@ -239,8 +253,13 @@ class ServingServer:
         self.healthy = True
         self.steps = 0
         self.cancelled = 0
-        self._pending: Dict[asyncio.AbstractEventLoop, List] = {}
+        self._pending: Dict[Optional[asyncio.AbstractEventLoop], List] = {}
         self._thread = threading.Thread(target=self._run, name="ms-engine", daemon=True)
+        # a front-end in another process (HttpFrontendProcess): its requests' events go
+        # out as one pipe message per flush, under a lock shared with stop messages
+        self._remote = None
+        self._remote_lock = threading.Lock()
+        self._remote_healthy = True
 
     # -- any thread
     def start(self):
@@ -254,13 +273,7 @@ class ServingServer:
 
     def submit(self, prompt: List[int], max_tokens: int, temperature: float, top_p: float,
                aloop: asyncio.AbstractEventLoop, q: asyncio.Queue) -> int:
-        if not self.healthy:
-            raise ApiError("NoHealthyWorkers", "the engine is quarantined")
-        if max_tokens < 1:
-            raise ApiError("InvalidRequest", "max_tokens must be at least 1")
-        if len(prompt) + max_tokens > self.max_context:
-            raise ApiError("TokenLimitExceeded",
-                           f"prompt ({len(prompt)}) + max_tokens ({max_tokens}) > {self.max_context}")
+        _admission_check(self.healthy, self.max_context, prompt, max_tokens)
         with self._rid_lock:
             self._rid += 1
             rid = self._rid
@@ -279,9 +292,47 @@ class ServingServer:
         self._pending.setdefault(sub.aloop, []).append((sub.q, ev))
 
     def _flush(self):
+        remote = self._pending.pop(None, [])
         for aloop, evs in self._pending.items():
             aloop.call_soon_threadsafe(_deliver, evs)
         self._pending = {}
+        if self._remote is not None and (remote or self.healthy != self._remote_healthy):
+            self._remote_healthy = self.healthy
+            self._remote_send(("ev", self.healthy, remote))
+
+    # -- a front-end process (HttpFrontendProcess)
+    def attach_remote(self, conn):
+        """Serve the front-end at the other end of `conn` (a duplex multiprocessing
+        pipe): it sends ("submit", rid, prompt, max_tokens, temperature, top_p) and
+        ("cancel", rid); it receives ("ev", healthy, [(rid, event), ...]) per flush."""
+        self._remote = conn
+        threading.Thread(target=self._remote_reader, args=(conn,), name="ms-frontend-rx", daemon=True).start()
+
+    def _remote_send(self, msg) -> bool:
+        with self._remote_lock:
+            conn = self._remote
+            if conn is None:
+                return False
+            try:
+                conn.send(msg)
+                return True
+            except (OSError, EOFError, ValueError):  # the front-end is gone
+                self._remote = None
+                return False
+
+    def _remote_reader(self, conn):
+        while True:
+            try:
+                msg = conn.recv()
+            except (OSError, EOFError):
+                return
+            if msg[0] == "submit":
+                _, rid, prompt, max_tokens, temperature, top_p = msg
+                r = Request(rid, list(prompt), int(max_tokens), temperature=float(temperature), top_p=float(top_p),
+                            seed=rid)
+                self._inbox.put(_Sub(None, rid, r))
+            elif msg[0] == "cancel":
+                self._inbox.put(msg[1])
 
     def _drain_inbox(self, block: bool):
         try:
@@ -511,6 +562,132 @@ class BackgroundHttp:
         asyncio.run_coroutine_threadsafe(down(), self._loop).result(30)
         self._loop.call_soon_threadsafe(self._loop.stop)
         self._thread.join(30)
+
+
+class _RemoteEngine:
+    """The front-end process's view of the ServingServer in the engine process:
+    the attributes and calls make_app uses, over a duplex pipe.  Submissions are
+    checked here (the same checks and messages as ServingServer.submit); one
+    reader thread hands each flush's events to the event loop in one wake-up."""
+
+    def __init__(self, conn, model: str, vocab_size: int, max_context: int):
+        self.conn, self.model, self.vocab_size, self.max_context = conn, model, vocab_size, max_context
+        self.healthy = True
+        self._rid = 1 << 32  # apart from the ids of in-process submissions
+        self._subs: Dict[int, asyncio.Queue] = {}
+        self._loop: Optional[asyncio.AbstractEventLoop] = None
+        self.stopped: Optional[asyncio.Event] = None
+
+    def start(self, loop: asyncio.AbstractEventLoop):
+        self._loop = loop
+        self.stopped = asyncio.Event()
+        threading.Thread(target=self._reader, name="ms-frontend-rx", daemon=True).start()
+
+    def submit(self, prompt: List[int], max_tokens: int, temperature: float, top_p: float,
+               aloop: asyncio.AbstractEventLoop, q: asyncio.Queue) -> int:
+        _admission_check(self.healthy, self.max_context, prompt, max_tokens)
+        self._rid += 1
+        rid = self._rid
+        self._subs[rid] = q
+        try:
+            self.conn.send(("submit", rid, list(prompt), int(max_tokens), float(temperature), float(top_p)))
+        except (OSError, ValueError):
+            self._subs.pop(rid, None)
+            raise ApiError("NoHealthyWorkers", "the engine process is gone") from None
+        return rid
+
+    def cancel(self, rid: int):
+        if self._subs.pop(rid, None) is not None:
+            try:
+                self.conn.send(("cancel", rid))
+            except (OSError, ValueError):
+                pass
+
+    def _reader(self):
+        while True:
+            try:
+                msg = self.conn.recv()
+            except (OSError, EOFError):
+                msg = ("stop",)
+            self._loop.call_soon_threadsafe(self._on_message, msg)
+            if msg[0] == "stop":
+                return
+
+    def _on_message(self, msg):
+        if msg[0] == "stop":
+            self.healthy = False
+            for q in self._subs.values():
+                q.put_nowait(("error", "server shutting down"))
+            self._subs.clear()
+            self.stopped.set()
+            return
+        _, self.healthy, evs = msg
+        for rid, ev in evs:
+            q = self._subs.get(rid)
+            if q is not None:
+                q.put_nowait(ev)
+                if ev[0] != "token":
+                    del self._subs[rid]
+
+
+def _frontend_main(conn, model: str, vocab_size: int, max_context: int, host: str, port: int):
+    """Entry point of the front-end process: serve make_app over the pipe until
+    the engine side sends ("stop",) or closes it."""
+    from aiohttp import web
+
+    async def serve():
+        eng = _RemoteEngine(conn, model, vocab_size, max_context)
+        eng.start(asyncio.get_running_loop())
+        runner = web.AppRunner(make_app(eng), access_log=None)
+        await runner.setup()
+        site = web.TCPSite(runner, host, port)
+        await site.start()
+        sock = site._server.sockets[0]
+        conn.send(("ready", f"http://{host}:{sock.getsockname()[1]}"))
+        await eng.stopped.wait()
+        await runner.cleanup()
+
+    asyncio.run(serve())
+    conn.close()
+
+
+class HttpFrontendProcess:
+    """The aiohttp app in a separate (spawned) process, talking to `server` over
+    a pipe.  The engine process then runs no HTTP or SSE code: its interpreter
+    is left to the engine thread, which sends one message per step with every
+    new token, and per request only a submit or cancel crosses the pipe."""
+
+    def __init__(self, server: ServingServer, host: str = "127.0.0.1", port: int = 0):
+        self.server, self.host, self.port = server, host, port
+        self._proc = None
+        self.url = ""
+
+    def start(self, timeout: float = 120.0):
+        import multiprocessing as mp
+        ctx = mp.get_context("spawn")
+        mine, theirs = ctx.Pipe(duplex=True)
+        s = self.server
+        self._proc = ctx.Process(target=_frontend_main, name="ms-http-frontend", daemon=True,
+                                 args=(theirs, s.model, s.vocab_size, s.max_context, self.host, self.port))
+        self._proc.start()
+        theirs.close()
+        if not mine.poll(timeout):
+            self._proc.kill()
+            raise RuntimeError("HTTP front-end process did not start")
+        kind, self.url = mine.recv()
+        assert kind == "ready"
+        s.attach_remote(mine)
+        return self
+
+    def stop(self, timeout: float = 30.0):
+        s = self.server
+        s._remote_send(("stop",))
+        with s._remote_lock:
+            s._remote = None
+        self._proc.join(timeout)
+        if self._proc.is_alive():
+            self._proc.kill()
+            self._proc.join(5)
 
 
 # ---------------------------------------------------------------------------------------

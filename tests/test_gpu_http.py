@@ -9,7 +9,8 @@ import numpy as np
 import pytest
 
 from mini_serve_rs_b200 import engine as E
-from mini_serve_rs_b200.http_driver import BackgroundHttp, ServingServer, StreamResult, run_trace, summarize_http
+from mini_serve_rs_b200.http_driver import (BackgroundHttp, HttpFrontendProcess, ServingServer, StreamResult,
+                                            run_trace, summarize_http)
 from mini_serve_rs_b200.serving import Request
 from oracle.qwen_ref import QwenRef, SeqState, random_weights
 from tests.golden.golden_cases import MODEL_CASES
@@ -27,7 +28,8 @@ def _oracle_greedy(cfg, w, prompt, n):
     return toks
 
 
-def test_http_trace_streams_the_oracle_greedy_tokens():
+@pytest.mark.parametrize("frontend", [BackgroundHttp, HttpFrontendProcess], ids=["thread", "process"])
+def test_http_trace_streams_the_oracle_greedy_tokens(frontend):
     need_gpu()
     pytest.importorskip("aiohttp")
     case = MODEL_CASES[1]  # Qwen3 miniature: QK-norm, tied embeddings
@@ -45,7 +47,7 @@ def test_http_trace_streams_the_oracle_greedy_tokens():
     eng.load_weights(w)
     pages = E.Pages(160, 16, max_chunks=32)
     srv = ServingServer(eng, pages, model="qwen3-mini", max_active=6, token_budget=40).start()
-    http = BackgroundHttp(srv).start()
+    http = frontend(srv).start()
     try:
         results, elapsed = run_trace(http.url, "qwen3-mini", reqs, timeout_s=300.0)
     finally:

@@ -16,8 +16,8 @@ import pytest
 aiohttp = pytest.importorskip("aiohttp")
 
 from mini_serve_rs_b200 import engine as E  # noqa: E402
-from mini_serve_rs_b200.http_driver import (BackgroundHttp, ServingServer, StreamResult, run_trace,  # noqa: E402
-                                            stream_completion, summarize_http)
+from mini_serve_rs_b200.http_driver import (BackgroundHttp, HttpFrontendProcess, ServingServer,  # noqa: E402
+                                            StreamResult, run_trace, stream_completion, summarize_http)
 from mini_serve_rs_b200.serving import Request  # noqa: E402
 
 VOCAB = 1000
@@ -82,12 +82,14 @@ class FakeEngine:
         return np.array(toks, np.int32), np.array(fl, np.int32)
 
 
-@pytest.fixture
-def served():
+@pytest.fixture(params=["thread", "process"])
+def served(request):
+    """The server with its HTTP front-end on a thread of this process, or in a
+    process of its own (HttpFrontendProcess) talking to the engine over a pipe."""
     eng = FakeEngine()
     pages = E.Pages(512, 16, max_chunks=128)
     srv = ServingServer(eng, pages, model="fake", max_active=8, token_budget=64).start()
-    http = BackgroundHttp(srv).start()
+    http = (BackgroundHttp if request.param == "thread" else HttpFrontendProcess)(srv).start()
     yield http.url, srv, eng, pages
     http.stop()
     srv.stop()
