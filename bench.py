@@ -301,6 +301,7 @@ def run_decode(args, rank, world, local, cfg, ctx, seed, tp_rank=0, tp_size=1, c
     barrier()
     torch.cuda.synchronize()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0 = eng.graph_stats()
     f0.record(stream)
     for _ in range(K):
         host_toks, _ = eng.step(ids, host_toks, pos)
@@ -308,6 +309,7 @@ def run_decode(args, rank, world, local, cfg, ctx, seed, tp_rank=0, tp_size=1, c
     f1.record(stream)
     f1.synchronize()
     ms_e2e = f0.elapsed_time(f1)
+    g1 = eng.graph_stats()
     barrier()
 
     t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=f"cuda:{local}")
@@ -318,7 +320,8 @@ def run_decode(args, rank, world, local, cfg, ctx, seed, tp_rank=0, tp_size=1, c
         "ms": ms, "ms_e2e": ms_e2e, "gpu_launches": gpu_launches, "clocks": clk.summary(),
         "attn_launches": alaunch, "attn_ms": attn_ms, "attn_bytes": attn_bytes,
         "h2d": (4 + 7 * B) * 4, "d2h": B * 4 + 4, "ctx_mean": float(np.mean(ctx)),
-        "graphs": {"captured": graphs[0], "replayed": graphs[1]}, "kp": KP, "tp_fused": eng.tp_fused(),
+        "graphs": {"captured": graphs[0], "replayed": graphs[1],
+                   "e2e_captured": g1[0] - g0[0], "e2e_replayed": g1[1] - g0[1]}, "kp": KP, "tp_fused": eng.tp_fused(),
         "memory": eng.memory(),
     }
     eng.close()
