@@ -31,7 +31,11 @@
 //   * warp 9, copies: the K and V tiles (32 KB each for D = 128) by cp.async
 //     in the order the MMAs consume them, through a ring of shared-memory
 //     slots freed by tcgen05.commit of the consuming MMAs; each lane arrives
-//     on the slot's barrier once its copies complete.
+//     on the slot's barrier once its copies complete.  It starts while the
+//     softmax warps load Q; the MMA thread waits for Q on q_full.
+// Softmax warp w owns tile rows [32 w, 32 w + 32), its TMEM lanes: it loads
+// those Q rows, and stores their O rows (staged through the freed Q tile), by
+// whole lines, 16 lanes x 16 bytes per 256-byte row.
 // Shared memory: Q (2 x 128 x D) + 4 slots of 32 KB = 193 KiB for D = 128
 // (8 slots of 16 KB for D = 64), one CTA per SM; TMEM: 512 columns (per half
 // S/P 128 + O D).
@@ -293,7 +297,7 @@ __global__ void __launch_bounds__(kThreads5, 1) paged_prefill_tc5_kernel(Prefill
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   unsigned char *sq = smem;  // query half h at h * QB: NDH 64-dim halves of 128 rows x 128 B
   unsigned char *ring = smem + kHalves * QB;
-  __shared__ uint64_t full[NSLOT], empty[NSLOT], s_full[kHalves], p_ready[kHalves], pv_done[kHalves], drain;
+  __shared__ uint64_t full[NSLOT], empty[NSLOT], s_full[kHalves], p_ready[kHalves], pv_done[kHalves], drain, q_full;
   __shared__ uint32_t tmem_base;
   __shared__ volatile int abort_s;
   __shared__ int mma_landed_s, issued_s;
@@ -326,6 +330,7 @@ __global__ void __launch_bounds__(kThreads5, 1) paged_prefill_tc5_kernel(Prefill
       mbar_init(&pv_done[h], 1);
     }
     mbar_init(&drain, 1);
+    mbar_init(&q_full, 4 * kHalves);  // one arrive per softmax warp once its Q rows are in shared memory
     abort_s = 0;
     mma_landed_s = 0;
     issued_s = 0;
@@ -341,22 +346,36 @@ __global__ void __launch_bounds__(kThreads5, 1) paged_prefill_tc5_kernel(Prefill
   const int tok = qh * TPH + rt / RPT, head = rt % RPT;
   const bool rvalid = warp < 4 * kHalves && head < G && tok < nrows;
   const int ng_q = qh == 0 ? ng[0] : ng[1];  // groups of this thread's half (softmax warps)
-  if (warp < 4 * kHalves) {  // Q row -> K-major swizzled tile (zeros for padding rows)
-    const T *qr = static_cast<const T *>(p.q) +
-                  ((size_t(row0) + (rvalid ? tok : 0)) * p.num_kv_heads * G + size_t(kvh) * G + (rvalid ? head : 0)) * D;
-#pragma unroll
-    for (int dh = 0; dh < NDH; ++dh)
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 v = rvalid ? reinterpret_cast<const uint4 *>(qr + dh * 64)[c] : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4 *>(sq + qh * QB + dh * QHALF + rt * 128 + ((c ^ (rt & 7)) << 4)) = v;
-      }
-  }
-  fence_proxy_async();
+  // the CTA starts here: the copy warp's first K/V tiles overlap the Q load below
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base;
+  // Rows by whole lines: RPI rows of the tile per warp instruction, CPR lanes x 16 bytes each.
+  // Softmax warp w owns tile rows [32 w, 32 w + 32) (its TMEM lanes), so it loads Q and
+  // stores O for exactly those rows.
+  constexpr int CPR = D / 8, RPI = 32 / CPR;
+  if (warp < 4 * kHalves) {
+    // Q rows -> K-major swizzled tile (zeros for padding rows), all loads before the stores
+    const int cc = lane % CPR, sub = lane / CPR;
+    uint4 qv[32 / RPI];
+#pragma unroll
+    for (int i = 0; i < 32 / RPI; ++i) {
+      const int r = (warp & 3) * 32 + i * RPI + sub;  // row within the half
+      const int tk = qh * TPH + r / RPT, hd = r % RPT;
+      const T *src = static_cast<const T *>(p.q) +
+                     ((size_t(row0) + tk) * p.num_kv_heads * G + size_t(kvh) * G + hd) * D + cc * 8;
+      qv[i] = hd < G && tk < nrows ? __ldg(reinterpret_cast<const uint4 *>(src)) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < 32 / RPI; ++i) {
+      const int r = (warp & 3) * 32 + i * RPI + sub, dh = cc >> 3, c = cc & 7;
+      *reinterpret_cast<uint4 *>(sq + qh * QB + dh * QHALF + r * 128 + ((c ^ (r & 7)) << 4)) = qv[i];
+    }
+    fence_proxy_async();  // the MMAs read Q through the async proxy
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&q_full);
+  }
 
   float l_run = 0.f;
   if (warp < 4 * kHalves) {
@@ -516,7 +535,7 @@ __global__ void __launch_bounds__(kThreads5, 1) paged_prefill_tc5_kernel(Prefill
         for (int kk = 0; kk < kKeys / 16; ++kk) umma_ts(d, a + kk * 8, b0 + uint64_t((kk * 2048) >> 4), id_o, kk > 0 ? 1u : acc0);
         umma_commit(&pv_done[h]);
       };
-      bool ok = wait_tile(0);
+      bool ok = wait_or_abort(&q_full, 0, &abort_s) && wait_tile(0);
       if (ok) {
 #pragma unroll
         for (int h = 0; h < kHalves; ++h)
@@ -619,26 +638,39 @@ __global__ void __launch_bounds__(kThreads5, 1) paged_prefill_tc5_kernel(Prefill
   tc_fence_after();
   if (all_ok) {
     if (warp < 4 * kHalves && ng_q > 0) {
-      // O row / l -> out; every thread of the half takes part in the warp-collective TMEM loads
+      // O row / l -> shared memory (the Q tile is free once the MMAs drained): tile row
+      // R = 32 warp + lane, D * 2 bytes, 16-byte chunk c at c ^ (R & 7); then this warp's 32
+      // rows -> out by whole lines.  Every thread of the half takes part in the warp-collective
+      // TMEM loads.
       const uint32_t lane_off = uint32_t((warp & 3) * 32) << 16;
       const uint32_t tm_o = tmem + qh * 256 + kKeys;
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      T *orow = static_cast<T *>(p.out) +
-                ((size_t(row0) + (rvalid ? tok : 0)) * p.num_kv_heads * G + size_t(kvh) * G + (rvalid ? head : 0)) * D;
+      unsigned char *stage = sq + size_t(warp * 32) * (D * 2);
 #pragma unroll
       for (int c0 = 0; c0 < D; c0 += 32) {
         float o[32];
         tmem_ld32(tm_o + lane_off + c0, o);
-        if (rvalid) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 w;
-            w.x = pack_pair<T>(o[i] * inv, o[i + 1] * inv);
-            w.y = pack_pair<T>(o[i + 2] * inv, o[i + 3] * inv);
-            w.z = pack_pair<T>(o[i + 4] * inv, o[i + 5] * inv);
-            w.w = pack_pair<T>(o[i + 6] * inv, o[i + 7] * inv);
-            *reinterpret_cast<uint4 *>(orow + c0 + i) = w;
-          }
+        for (int i = 0; i < 32; i += 8) {
+          uint4 w;
+          w.x = pack_pair<T>(o[i] * inv, o[i + 1] * inv);
+          w.y = pack_pair<T>(o[i + 2] * inv, o[i + 3] * inv);
+          w.z = pack_pair<T>(o[i + 4] * inv, o[i + 5] * inv);
+          w.w = pack_pair<T>(o[i + 6] * inv, o[i + 7] * inv);
+          *reinterpret_cast<uint4 *>(stage + lane * (D * 2) + ((((c0 + i) >> 3) ^ (lane & 7)) << 4)) = w;
+        }
+      }
+      __syncwarp();
+      const int cc = lane % CPR, sub = lane / CPR;
+#pragma unroll
+      for (int i = 0; i < 32 / RPI; ++i) {
+        const int r = i * RPI + sub;                  // row within this warp's 32
+        const int rh = (warp & 3) * 32 + r;           // row within the half
+        const int tk = qh * TPH + rh / RPT, hd = rh % RPT;
+        if (hd < G && tk < nrows) {
+          const uint4 v = *reinterpret_cast<const uint4 *>(stage + r * (D * 2) + ((cc ^ (r & 7)) << 4));
+          *reinterpret_cast<uint4 *>(static_cast<T *>(p.out) +
+                                     ((size_t(row0) + tk) * p.num_kv_heads * G + size_t(kvh) * G + hd) * D + cc * 8) = v;
         }
       }
     }

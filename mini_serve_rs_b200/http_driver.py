@@ -671,10 +671,14 @@ class HttpFrontendProcess:
                                  args=(theirs, s.model, s.vocab_size, s.max_context, self.host, self.port))
         self._proc.start()
         theirs.close()
-        if not mine.poll(timeout):
+        try:
+            if not mine.poll(timeout):
+                raise EOFError
+            kind, self.url = mine.recv()
+        except EOFError:  # no answer, or the process died first (e.g. the port is taken; see its stderr)
             self._proc.kill()
-            raise RuntimeError("HTTP front-end process did not start")
-        kind, self.url = mine.recv()
+            self._proc.join(5)
+            raise RuntimeError(f"HTTP front-end process did not start on {self.host}:{self.port}") from None
         assert kind == "ready"
         s.attach_remote(mine)
         return self
