@@ -271,6 +271,16 @@ __device__ __forceinline__ void tmem_st32u(uint32_t addr, const uint32_t (&v)[32
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// 16 columns of this thread's TMEM lane, without waiting: tcgen05.wait::st before another
+// thread or the tensor core may read them
+__device__ __forceinline__ void tmem_st16u_async(uint32_t addr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(addr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_st16u(uint32_t addr, const uint32_t (&v)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(addr),
@@ -470,8 +480,9 @@ __global__ void __launch_bounds__(kThreads5, 1) paged_prefill_tc5_kernel(Prefill
             fadd2(ps[2 * (i & 3)], ps[2 * (i & 3) + 1], a, b);
             pk[i] = pack_pair<T>(a, b);
           }
-          tmem_st16u(tm_s + lane_off + 16 * k, pk);
+          tmem_st16u_async(tm_s + lane_off + 16 * k, pk);  // over S columns this thread has read
         }
+        tmem_wait_st();  // once, before the p_ready arrive hands P to the tensor core
       };
       if (diag) make_p(std::true_type{});
       else make_p(std::false_type{});
