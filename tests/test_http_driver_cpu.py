@@ -249,3 +249,21 @@ def test_host_failure_in_the_loop_fails_requests_instead_of_hanging(served):
     assert st == 500 and "serving loop failed" in json.loads(raw)["error"]["message"]
     st, ready = asyncio.run(_get(url, "/ready"))
     assert st == 503
+
+
+def test_frontend_process_that_cannot_bind_reports_it():
+    """A front-end process that dies before serving (here: its port is taken) is a
+    clear start-up error, not a hang or a bare EOFError."""
+    import socket
+    eng = FakeEngine()
+    pages = E.Pages(64, 16, max_chunks=16)
+    srv = ServingServer(eng, pages, model="fake", max_active=2, token_budget=64).start()
+    busy = socket.socket()
+    busy.bind(("127.0.0.1", 0))
+    busy.listen(1)
+    try:
+        with pytest.raises(RuntimeError, match="did not start"):
+            HttpFrontendProcess(srv, port=busy.getsockname()[1]).start(timeout=60)
+    finally:
+        busy.close()
+        srv.stop()
