@@ -48,6 +48,10 @@ def parse():
     ap.add_argument("--config5", action="store_true",
                     help="BASELINE config 5: Qwen2.5-7B arch, 256 seqs x ctx U[1024,32768], tensor parallel")
     ap.add_argument("--tp", type=int, default=2, help="tensor-parallel size for --config5")
+    ap.add_argument("--tp-max-ctx", type=int, default=None,
+                    help="cap config 5's context range (default: the full U[1024, 32768 - steps])")
+    ap.add_argument("--no-tp", action="store_true",
+                    help="with N >= 2: skip the tensor-parallel record (golden parity + config-5 decode)")
     ap.add_argument("--config4", action="store_true",
                     help="BASELINE config 4: serving trace (1024 Poisson arrivals at 64 req/s), one replica per GPU")
     ap.add_argument("--requests", type=int, default=1024, help="requests in the --config4 trace")
@@ -196,12 +200,13 @@ def cudart():
 
 
 def fill_pool(eng, cfg, pool_blocks, device, seed, kv_heads=None):
-    """Seeded N(0,1) bf16 K/V in every page: one random chunk copied over each
-    layer's K and V pool (the contents do not change the kernel's traffic)."""
+    """Seeded N(0,1) bf16 K/V in every page: one random 64 MB chunk copied over
+    each layer's K and V pool (the contents do not change the kernel's traffic;
+    the chunk stays in L2, so the fill is bound by HBM writes alone)."""
     import torch
     rt = cudart()
     layer_bytes = pool_blocks * (kv_heads or cfg.num_key_value_heads) * 16 * cfg.hd() * 2
-    chunk = min(layer_bytes, 512 << 20)
+    chunk = min(layer_bytes, 64 << 20)
     g = torch.Generator(device=f"cuda:{device}").manual_seed(seed)
     src = torch.randn(chunk // 2, generator=g, dtype=torch.bfloat16, device=f"cuda:{device}")
     torch.cuda.synchronize()
@@ -234,7 +239,7 @@ def run_decode(args, rank, world, local, cfg, ctx, seed, tp_rank=0, tp_size=1, c
     torch.cuda.set_device(local)
     B, K, W = len(ctx), args.steps, args.warmup
     KP = min(K, 10)
-    extra = W + 2 * K + KP + 2
+    extra = decode_extra(args, tp_size)
     need = [(int(c) + extra + 15) // 16 for c in ctx]
     pool_blocks = int(sum(need) * 1.02) + 64
     mbps = (max(int(c) for c in ctx) + extra + 15) // 16 + 1
@@ -290,13 +295,44 @@ def run_decode(args, rank, world, local, cfg, ctx, seed, tp_rank=0, tp_size=1, c
         eng.step_launch(ids, None, None, E.MS_STEP_TOKENS_FROM_DEVICE)
         toks, _ = eng.step_wait()
     _, alaunch, attn_ms, attn_bytes = eng.profile()
+    ar_calls, ar_ms = eng.profile_allreduce()
     eng.set_profiling(False)
     torch.cuda.synchronize()
     barrier()
 
+    # ---- tensor parallelism: the same steps with the all-reduces through
+    # NCCL + K4 instead of the fused peer-memory kernel (every rank switches)
+    nccl = None
+    fused = eng.tp_fused()
+    if tp_size > 1 and fused:
+        eng.set_tp_fused(False)
+        barrier()
+        torch.cuda.synchronize()
+        n0, n1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n0.record(stream)
+        for _ in range(K):
+            eng.step_launch(ids, None, None, E.MS_STEP_TOKENS_FROM_DEVICE)
+            toks, _ = eng.step_wait()
+        n1.record(stream)
+        n1.synchronize()
+        nccl_ms = n0.elapsed_time(n1)
+        eng.profile()
+        eng.set_profiling(True)
+        for _ in range(KP):
+            eng.step_launch(ids, None, None, E.MS_STEP_TOKENS_FROM_DEVICE)
+            toks, _ = eng.step_wait()
+        eng.profile()
+        nccl_calls, nccl_ar_ms = eng.profile_allreduce()
+        eng.set_profiling(False)
+        eng.set_tp_fused(True)
+        nccl = {"ms": nccl_ms, "ar_calls": nccl_calls, "ar_ms": nccl_ar_ms}
+        torch.cuda.synchronize()
+        barrier()
+
     # ---- e2e: through the public step call with host token arrays
     # step 1 replayed the last cached prompt token; every later step added one
-    pos = np.array([int(c) + W + K + KP - 1 for c in ctx], dtype=np.int32)
+    done = W + K + KP + (K + KP if nccl else 0)
+    pos = np.array([int(c) + done - 1 for c in ctx], dtype=np.int32)
     host_toks = np.asarray(toks, dtype=np.uint32)
     barrier()
     torch.cuda.synchronize()
@@ -312,13 +348,16 @@ def run_decode(args, rank, world, local, cfg, ctx, seed, tp_rank=0, tp_size=1, c
     g1 = eng.graph_stats()
     barrier()
 
-    t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=f"cuda:{local}")
+    t = torch.tensor([ms, ms_e2e, nccl["ms"] if nccl else 0.0], dtype=torch.float64, device=f"cuda:{local}")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms, ms_e2e = float(t[0]), float(t[1])
+    if nccl:
+        nccl["ms"] = float(t[2])
     res = {
         "ms": ms, "ms_e2e": ms_e2e, "gpu_launches": gpu_launches, "clocks": clk.summary(),
         "attn_launches": alaunch, "attn_ms": attn_ms, "attn_bytes": attn_bytes,
+        "ar_calls": ar_calls, "ar_ms": ar_ms, "nccl": nccl,
         "h2d": (4 + 7 * B) * 4, "d2h": B * 4 + 4, "ctx_mean": float(np.mean(ctx)),
         "graphs": {"captured": graphs[0], "replayed": graphs[1],
                    "e2e_captured": g1[0] - g0[0], "e2e_replayed": g1[1] - g0[1]}, "kp": KP, "tp_fused": eng.tp_fused(),
@@ -326,6 +365,13 @@ def run_decode(args, rank, world, local, cfg, ctx, seed, tp_rank=0, tp_size=1, c
     }
     eng.close()
     return res
+
+
+def decode_extra(args, tp_size: int = 1) -> int:
+    """Decode steps run_decode takes beyond each sequence's admitted context
+    (warm-up, timed, profiled and e2e steps; under TP also the NCCL pass)."""
+    K, KP = args.steps, min(args.steps, 10)
+    return args.warmup + 2 * K + KP + 2 + (K + KP if tp_size > 1 else 0)
 
 
 def run_ours(args, rank, world, local):
@@ -422,15 +468,21 @@ def config4_trace(n_req: int, vocab: int, seed: int = 4):
 
 
 def run_config4(args, rank, world, local):
-    """One replica per GPU (one process each).  Requests go round-robin over
-    replicas, which is what the router's score (router.rs:23-30, (queue +
-    active + 1) x latency) gives for identical replicas under one trace.  Each
-    replica runs the continuous-batching loop (serving.ServingLoop) in real
-    time; rank 0 reports aggregate and per-GPU token rates and TTFT."""
+    """One replica per GPU (one process each).  A dispatcher thread on rank 0
+    routes every request at its arrival time to the replica with the lowest
+    router.rs score, (queue + active + 1) x max(avg latency, 1 ms), among
+    those with capacity (mini_serve_rs_b200/router.py); replicas publish their
+    metrics through a TCPStore after every step.  Each replica runs the
+    continuous-batching loop (serving.ServingLoop) in real time; rank 0
+    reports aggregate and per-GPU token rates and TTFT.  With --http the trace
+    client deals requests round-robin over the replicas' HTTP servers."""
+    import time as _time
+
     import torch
     import torch.distributed as dist
     from mini_serve_rs_b200 import engine as E
     from mini_serve_rs_b200.config import iter_random_device_weights, qwen3_0_6b
+    from mini_serve_rs_b200.router import Dispatcher, ReplicaLink, router_stores, summarize_routing
     from mini_serve_rs_b200.serving import ServingLoop, summarize
     torch.cuda.set_device(local)
     cfg = qwen3_0_6b()
@@ -442,16 +494,18 @@ def run_config4(args, rank, world, local):
                    dtype=E.MS_DTYPE_BF16)
     eng.load_weights(iter_random_device_weights(cfg, SEED, device=f"cuda:{local}"))
     pages = E.Pages(pool_blocks, 16, max_chunks=pool_blocks // 2)
-    reqs = [r for r in config4_trace(args.requests, cfg.vocab_size) if (r.rid - 1) % world == rank]
+    trace = config4_trace(args.requests, cfg.vocab_size)
     # warm-up: a few requests outside the trace (first-launch costs, library heuristics)
     warm = ServingLoop(eng, pages, max_active, args.token_budget)
     from mini_serve_rs_b200.serving import Request
     warm.run([Request(rid=10_000_000 + k, prompt=list(range(100 + 37 * k)), max_tokens=8) for k in range(4)])
     pages.close()
     pages = E.Pages(pool_blocks, 16, max_chunks=pool_blocks // 2)
+    routing = None
     if args.http:
         from mini_serve_rs_b200.http_driver import (BackgroundHttp, HttpFrontendProcess, ServingServer,
                                                     run_trace_process, summarize_http)
+        reqs = [r for r in trace if (r.rid - 1) % world == rank]
         srv = ServingServer(eng, pages, model="qwen3-0.6b-arch", max_active=max_active,
                             token_budget=args.token_budget).start()
         http = (HttpFrontendProcess if args.http_frontend == "process" else BackgroundHttp)(srv).start()
@@ -464,13 +518,24 @@ def run_config4(args, rank, world, local):
         summ = summarize_http(results, elapsed)
         summ["steps"] = srv.steps
     else:
+        master, store, dstore = router_stores(rank, world)
         loop = ServingLoop(eng, pages, max_active, args.token_budget)
+        disp = Dispatcher(dstore, world, trace) if rank == 0 else None
         if world > 1:
             dist.barrier()
+        if disp:
+            disp.start(t0=_time.time() + 0.2)
         with ClockSampler(local) as clk:
-            elapsed = loop.run(reqs, timeout_s=900.0)
+            elapsed = loop.run_routed(ReplicaLink(store, rank), {r.rid: r for r in trace}, timeout_s=900.0)
+        if disp:
+            disp.join(60)
+            routing = summarize_routing(disp.choices, world)
+            routing["unrouted"] = len(disp.failed)
         summ = summarize(loop.finished, elapsed)
         summ["steps"] = loop.steps
+        if world > 1:
+            dist.barrier()  # the store's host (rank 0) outlives every client
+        del store, dstore, master
     summ["prefix"] = pages.stats()
     summ["clocks"] = clk.summary()
     summ["gpu_launches"] = eng.profile()[0]
@@ -483,6 +548,12 @@ def run_config4(args, rank, world, local):
         tokens = sum(x["tokens"] for x in alls)
         span = max(x["elapsed_s"] for x in alls)
         agg = tokens / span
+        # TTFT percentiles over every request of the trace
+        ttfts = sorted(t for x in alls for t in x.get("ttft_ms_all", []))
+
+        def pct(q):
+            return ttfts[min(len(ttfts) - 1, int(q * len(ttfts)))] if ttfts else None
+
         print(json.dumps({
             "metric": "serving trace decode tokens/s (BASELINE config 4)" + (" via HTTP/SSE" if args.http else ""),
             "value": agg, "unit": UNIT,
@@ -491,12 +562,164 @@ def run_config4(args, rank, world, local):
             "config": {"workload": "BASELINE config 4", "requests": args.requests, "arrival_rate_per_s": 64,
                        "prompt": "lognormal median 512 sigma 1.0 clipped [16,8192], 30% shared 1024-token prefix",
                        "output": "uniform[32,1024]", "token_budget": args.token_budget, "max_active": max_active,
-                       "sampling": "greedy", "routing": "round-robin over replicas",
+                       "sampling": "greedy",
+                       "routing": ("round-robin over replicas (HTTP trace client)" if args.http else
+                                   "router.rs latency-aware score, dispatcher on rank 0"),
                        "driver": (f"POST /v1/completions stream=true, HTTP front-end: {args.http_frontend}, "
                                   "trace client in its own process" if args.http else "ServingLoop in process")},
+            "note": "arrival-bound: the trace offers 64 req/s whatever N is, so tokens/s grows with N only while "
+                    "one replica cannot keep up with the arrivals",
             "tokens_per_s_per_gpu": agg / world, "tokens": tokens, "elapsed_s": span,
-            "ttft_ms_p50": alls[0]["ttft_ms_p50"], "ttft_ms_p90": alls[0]["ttft_ms_p90"],
-            "ttft_ms_p99": alls[0]["ttft_ms_p99"], "per_rank": alls}), flush=True)
+            "ttft_ms_p50": pct(0.5), "ttft_ms_p90": pct(0.9), "ttft_ms_p99": pct(0.99),
+            "routing": routing,
+            "per_rank": [{k: v for k, v in x.items() if k != "ttft_ms_all"} for x in alls]}), flush=True)
+
+
+def tp_group_comm(rank, world, local, tp):
+    """NCCL communicator of this rank's tensor-parallel group (ranks
+    [g*tp, (g+1)*tp)); the unique id travels over the torch process group."""
+    import torch.distributed as dist
+    from mini_serve_rs_b200 import engine as E
+    group, tp_rank = rank // tp, rank % tp
+    uid = E.nccl_unique_id() if tp_rank == 0 else None
+    uids = [None] * world
+    dist.all_gather_object(uids, uid)
+    return group, tp_rank, E.nccl_comm_init(tp, uids[group * tp], tp_rank, local)
+
+
+def tp_parity_cfg():
+    """The committed golden case "qwen2_kv4": Qwen2.5-7B's attention shape
+    (hidden 3584, 28 query / 4 KV heads x 128, q/k/v bias, untied lm_head) on
+    two layers, vocabulary 512, MLP 1024, weights host_random_weights(seed 7007)."""
+    from mini_serve_rs_b200.config import ModelConfig
+    return ModelConfig(512, 3584, 1024, 2, 28, 4, 4096, 128, 1e6, 1e-6, False, True, False)
+
+
+def tp_parity(local, tp_rank, tp, comm):
+    """One tensor-parallel group runs the golden case in f32 -- three prompts
+    prefilled in one packed step, then six decode steps fed the golden greedy
+    tokens -- first with the fused peer-memory all-reduce, then through NCCL.
+    Every step's logits are compared with the committed transformers outputs
+    (tests/golden/golden.npz, max-abs 2e-4, the f32 tolerance of the GPU
+    parity tests) and its greedy tokens must be equal."""
+    import numpy as np
+    from mini_serve_rs_b200 import engine as E
+    from mini_serve_rs_b200.config import host_random_weights
+    cfg = tp_parity_cfg()
+    with np.load(ROOT / "tests" / "golden" / "golden.npz") as z:
+        g = {k: z[k] for k in z.files if k.startswith("qwen2_kv4/")}
+    prompts = [g[f"qwen2_kv4/p{i}/prompt"].tolist() for i in range(3)]
+    steps = g["qwen2_kv4/p0/tokens"].shape[0] - 1
+    eng = E.Engine(cfg, device=local, pool_blocks=64, max_seqs=4, max_tokens_per_step=256, max_blocks_per_seq=16,
+                   dtype=E.MS_DTYPE_F32, tp_rank=tp_rank, tp_size=tp, nccl_comm=comm)
+    eng.load_weights(host_random_weights(cfg, 7007))
+    out = {}
+    modes = [True, False] if eng.tp_fused() else [False]
+    for fused in modes:
+        if eng.tp_fused() != fused:
+            eng.set_tp_fused(fused)
+        ids = [1, 2, 3]
+        for k, (sid, p) in enumerate(zip(ids, prompts)):
+            eng.admit(sid, p, list(range(16 * k, 16 * k + 8)))
+        worst, bad = 0.0, 0
+        toks, _ = eng.step(ids, flags=E.MS_STEP_KEEP_LOGITS)
+        for s in range(steps + 1):
+            lg = eng.logits(len(ids))
+            for i in range(len(ids)):
+                worst = max(worst, float(np.abs(lg[i] - g[f"qwen2_kv4/p{i}/logits"][s]).max()))
+                bad += int(toks[i]) != int(g[f"qwen2_kv4/p{i}/tokens"][s])
+            if s == steps:
+                break
+            inputs = [int(g[f"qwen2_kv4/p{i}/tokens"][s]) for i in range(len(ids))]
+            toks, _ = eng.step(ids, inputs, [len(p) + s for p in prompts], flags=E.MS_STEP_KEEP_LOGITS)
+        for sid in ids:
+            eng.release(sid)
+        out["fused" if fused else "nccl"] = {"max_abs_logits": worst, "token_mismatches": bad,
+                                             "ok": worst <= 2e-4 and bad == 0}
+    eng.close()
+    return out
+
+
+def tp_decode_record(args, r, tp, world, cfg, ctx_desc):
+    """The config-5 numbers of one run_decode result (rank 0's view; times
+    are already the max over ranks)."""
+    replicas = world // tp
+    K, KP = args.steps, r["kp"]
+    value = replicas * args.batch * K / (r["ms"] / 1000.0)
+    per_launch_ms = r["attn_ms"] / max(1, r["attn_launches"])
+    per_launch_bytes = r["attn_bytes"] / max(1, r["attn_launches"])
+    achieved = per_launch_bytes / (per_launch_ms / 1000.0) / 1e9
+    peak, kind = peaks()
+    step_ms = r["ms"] / K
+    rec = {
+        "value": value, "unit": UNIT, "ms_per_step": step_ms, "tokens_per_s_per_gpu": value / world,
+        "e2e": {"value": replicas * args.batch * K / (r["ms_e2e"] / 1000.0), "unit": UNIT,
+                "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
+        "config": ctx_desc,
+        "attention": {"kernel": "paged_attention_tc_kernel (per rank: its KV heads)", "achieved_gbs": achieved,
+                      "peak_gbs": peak, "frac": achieved / peak, "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({kind})",
+                      "ms_per_launch": per_launch_ms, "share_of_step": (r["attn_ms"] / KP) / step_ms},
+        "allreduce": {"path": ("fused peer-memory all-reduce + residual add + RMSNorm (NVLink, CUDA IPC)"
+                               if r["tp_fused"] else "NCCL all-reduce + K4"),
+                      "calls_per_step": r["ar_calls"] / max(1, KP), "ms_per_step": r["ar_ms"] / max(1, KP),
+                      "share_of_step": (r["ar_ms"] / max(1, KP)) / step_ms},
+        "gpu_launches": r["gpu_launches"], "clocks": r["clocks"], "memory_bytes": r["memory"],
+    }
+    if r.get("nccl"):
+        n = r["nccl"]
+        rec["nccl_allreduce"] = {"ms_per_step": n["ms"] / K, "value": replicas * args.batch * K / (n["ms"] / 1000.0),
+                                 "allreduce_ms_per_step": n["ar_ms"] / max(1, KP),
+                                 "allreduce_share_of_step": (n["ar_ms"] / max(1, KP)) / (n["ms"] / K)}
+    return rec
+
+
+def config5_contexts(args, tp, group, max_ctx=None):
+    """Per-replica config-5 contexts: U[1024, min(max_ctx, 32768 - extra)]."""
+    import numpy as np
+    from mini_serve_rs_b200.config import qwen2_5_7b
+    cfg = qwen2_5_7b()
+    hi = cfg.max_position_embeddings - decode_extra(args, tp)
+    if max_ctx:
+        hi = min(hi, max_ctx)
+    rng = np.random.Generator(np.random.PCG64(SEED + group))
+    return cfg, rng.integers(1024, hi + 1, args.batch), hi
+
+
+def run_tp(args, rank, world, local):
+    """The tensor-parallel record added to the headline line when N >= 2:
+    TP=2 at N=2, TP=4 at N=4, two TP=4 replicas at N=8.  First the golden
+    parity case on every rank (fused and NCCL all-reduce), then BASELINE
+    config 5's decode (Qwen2.5-7B arch, 256 sequences per replica, contexts
+    U[1024, 32768 - steps], bf16), timed with the fused all-reduce and again
+    with NCCL on the same engines."""
+    import torch
+    import torch.distributed as dist
+    from mini_serve_rs_b200 import engine as E
+    tp = 2 if world == 2 or world % 4 else 4
+    torch.cuda.empty_cache()
+    group, tp_rank, comm = tp_group_comm(rank, world, local, tp)
+    try:
+        par = tp_parity(local, tp_rank, tp, comm)
+    except Exception as e:  # a failure is reported, and every rank still takes the same collective steps
+        par = {"error": repr(e)}
+    pars = [None] * world
+    dist.all_gather_object(pars, par)
+    parity_ok = all("error" not in p and all(v["ok"] for v in p.values()) and "fused" in p for p in pars)
+    cfg, ctx, hi = config5_contexts(args, tp, group, args.tp_max_ctx)
+    r = run_decode(args, rank, world, local, cfg, ctx, SEED + group, tp_rank, tp, comm)
+    E.nccl_comm_destroy(comm)
+    desc = {"workload": "BASELINE config 5 decode (Qwen2.5-7B arch, TP by KV head)", "tp": tp,
+            "replicas": world // tp, "seqs_per_replica": args.batch, "ctx": f"uniform[1024,{hi}]",
+            "ctx_mean": r["ctx_mean"], "steps": args.steps}
+    rec = tp_decode_record(args, r, tp, world, cfg, desc)
+    worst = max((v["max_abs_logits"] for p in pars if "error" not in p for v in p.values()), default=None)
+    rec = {"parity": parity_ok,
+           "parity_check": {"case": "tests/golden/golden.npz qwen2_kv4 (transformers, f32): 3 prompts, "
+                                    "prefill + 6 decode steps on every rank, logits max-abs <= 2e-4, tokens equal",
+                            "paths": sorted({k for p in pars for k in p}), "max_abs_logits": worst,
+                            "per_rank": pars},
+           **rec}
+    return rec
 
 
 def run_config5(args, rank, world, local):
@@ -504,49 +727,22 @@ def run_config5(args, rank, world, local):
     head over `--tp` GPUs per replica (world / tp replicas), 256 sequences per
     replica with contexts U[1024, 32768 - steps] (the model's 32768 positions
     bound the last decode step), bf16.  Prints its own JSON line."""
-    import numpy as np
-    import torch.distributed as dist
-
     from mini_serve_rs_b200 import engine as E
-    from mini_serve_rs_b200.config import qwen2_5_7b
     tp = args.tp
     if world < 2 or world % tp != 0:
         raise SystemExit("--config5 runs under torchrun with a multiple of --tp ranks (TP=1 does not fit 248 GB of KV)")
-    group, tp_rank = rank // tp, rank % tp
-    uid = E.nccl_unique_id() if tp_rank == 0 else None
-    uids = [None] * world
-    dist.all_gather_object(uids, uid)
-    comm = E.nccl_comm_init(tp, uids[group * tp], tp_rank, local)
-    cfg = qwen2_5_7b()
-    extra = args.warmup + 2 * args.steps + min(args.steps, 10) + 2
-    rng = np.random.Generator(np.random.PCG64(SEED + group))
-    ctx = rng.integers(1024, cfg.max_position_embeddings - extra + 1, args.batch)
+    group, tp_rank, comm = tp_group_comm(rank, world, local, tp)
+    cfg, ctx, hi = config5_contexts(args, tp, group, args.tp_max_ctx)
     r = run_decode(args, rank, world, local, cfg, ctx, SEED + group, tp_rank, tp, comm)
     E.nccl_comm_destroy(comm)
     if rank == 0:
-        replicas = world // tp
-        value = replicas * args.batch * args.steps / (r["ms"] / 1000.0)
-        e2e = replicas * args.batch * args.steps / (r["ms_e2e"] / 1000.0)
-        per_launch_ms = r["attn_ms"] / max(1, r["attn_launches"])
-        per_launch_bytes = r["attn_bytes"] / max(1, r["attn_launches"])
-        achieved = per_launch_bytes / (per_launch_ms / 1000.0) / 1e9
-        peak, kind = peaks()
-        print(json.dumps({
-            "metric": "decode tokens/s (Qwen2.5-7B arch, TP by KV head)", "value": value, "unit": UNIT,
-            "n_gpus": world, "tp": tp, "replicas": replicas, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": r["ms"] / args.steps, "tokens_per_s_per_gpu": value / world, "dtype": "bf16",
-            "data": "synthetic (seeded random-init weights, N(0,1) KV)",
-            "config": {"workload": "BASELINE config 5", "seqs_per_replica": args.batch,
-                       "ctx": f"uniform[1024,{cfg.max_position_embeddings - extra}]", "ctx_mean": r["ctx_mean"]},
-            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
-            "gpu_launches": r["gpu_launches"], "clocks": r["clocks"],
-            "roofline": {"kernel": "paged_attention_tc_kernel (per rank: its KV heads)", "bound": "hbm",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({kind})", "ms_per_launch": per_launch_ms,
-                         "share_of_step": (r["attn_ms"] / r["kp"]) / (r["ms"] / args.steps)},
-            "tp_allreduce": ("fused peer-memory all-reduce + residual add + RMSNorm (NVLink, CUDA IPC)"
-                             if r["tp_fused"] else "NCCL all-reduce + K4"),
-            "cuda_graphs": r["graphs"], "memory_bytes": r["memory"]}), flush=True)
+        desc = {"workload": "BASELINE config 5", "seqs_per_replica": args.batch, "ctx": f"uniform[1024,{hi}]",
+                "ctx_mean": r["ctx_mean"]}
+        rec = tp_decode_record(args, r, tp, world, cfg, desc)
+        print(json.dumps({"metric": "decode tokens/s (Qwen2.5-7B arch, TP by KV head)", "n_gpus": world, "tp": tp,
+                          "replicas": world // tp, "steps": args.steps, "warmup": args.warmup, "dtype": "bf16",
+                          "data": "synthetic (seeded random-init weights, N(0,1) KV)",
+                          "cuda_graphs": r["graphs"], **rec}), flush=True)
 
 
 def run_norm_rope_kernels(args, local):
@@ -809,6 +1005,9 @@ def main():
             dist.destroy_process_group()
         return
     r = run_ours(args, rank, world, local)
+    tp_rec = None
+    if world > 1 and not args.no_tp:
+        tp_rec = run_tp(args, rank, world, local)
     if rank == 0:
         B, K = args.batch, args.steps
         value = n * B * K / (r["ms"] / 1000.0)
@@ -820,8 +1019,9 @@ def main():
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": n, "steps": K, "warmup": args.warmup,
                 "ms_per_step": r["ms"] / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "bf16", "data": "synthetic (seeded random-init weights, N(0,1) KV)", "config": cfg_desc,
+                "tokens_per_s_per_gpu": value / n,
                 "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"],
-                        "ms_per_step": r["ms_e2e"] / K},
+                        "ms_per_step": r["ms_e2e"] / K, "tokens_per_s_per_gpu": e2e / n},
                 "gpu_launches": r["gpu_launches"], "clocks": r["clocks"],
                 "roofline": {"kernel": "paged_attention_kernel (K3 split-K GQA decode + combine)", "bound": "hbm",
                              "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
@@ -833,6 +1033,8 @@ def main():
         if world <= 1 and not args.no_cpu_baseline:
             tps, cores, desc = cpu_sample(8, 2, 1)
             line["cpu_baseline"] = {"value": tps, "unit": UNIT, "cores": cores, "kind": "port", "sample": desc}
+        if tp_rec is not None:
+            line["tp"] = tp_rec
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -257,6 +257,12 @@ int ms_engine_stream(const ms_engine *eng, void **stream_out);
 int ms_engine_set_profiling(ms_engine *eng, int32_t on);
 int ms_engine_profile(ms_engine *eng, int64_t *kernel_launches, int64_t *attn_launches,
                       double *attn_ms_total, double *attn_bytes_total);
+/* Under tensor parallelism with profiling on, CUDA events also bracket each
+ * all-reduce section after o_proj and down_proj (the fused peer-memory
+ * all-reduce + residual add + RMSNorm kernel, or NCCL all-reduce + K4):
+ * returns how many sections were bracketed and their summed duration, then
+ * clears that log. */
+int ms_engine_profile_allreduce(ms_engine *eng, int64_t *calls, double *ms_total);
 
 /* ---- CUDA graphs of decode steps (no counterpart in the reference) -------
  * Steps with one token per sequence, at most num_seqs new block-table
@@ -276,6 +282,11 @@ int ms_engine_graph_stats(const ms_engine *eng, int64_t *captures, int64_t *repl
  * through NCCL (tp_size 1, MS_TP_FUSED=0, or a rank that could not map its
  * peers -- all ranks then agree on NCCL).  No reference counterpart. */
 int ms_engine_tp_fused(const ms_engine *eng, int32_t *fused);
+/* Selects the all-reduce path of later steps: on = 1 the fused peer-memory
+ * kernel (only where creation set it up, else MS_E_INVALID), on = 0 NCCL
+ * all-reduce + K4.  Every rank of the tensor-parallel group must switch
+ * between the same two steps.  No reference counterpart. */
+int ms_engine_set_tp_fused(ms_engine *eng, int32_t on);
 
 /* ---- health (traits.rs:175-180, candle.rs:324-335) --------------------- */
 int ms_is_healthy(const ms_engine *eng);

@@ -60,6 +60,27 @@ def weight_shapes(cfg) -> Dict[str, tuple]:
     return out
 
 
+def host_random_weights(cfg, seed: int, std: float = 0.02, norm_std: float = 0.0):
+    """Seeded random-init weights on the host, regenerable on any machine:
+    one numpy PCG64 stream walked in sorted-name order; matrices and biases
+    N(0, std) in f32, norm weights 1 (+ N(0, norm_std)).  The committed
+    transformers golden vectors were computed from weights drawn this way."""
+    import numpy as np
+    import torch
+    rng = np.random.Generator(np.random.PCG64(seed))
+    out = {}
+    for name in sorted(weight_shapes(cfg)):
+        shape = weight_shapes(cfg)[name]
+        if name.endswith("norm.weight"):
+            w = np.ones(shape, np.float32)
+            if norm_std:
+                w = w + rng.standard_normal(shape, dtype=np.float32) * np.float32(norm_std)
+        else:
+            w = rng.standard_normal(shape, dtype=np.float32) * np.float32(std)
+        out[name] = torch.from_numpy(w.astype(np.float32))
+    return out
+
+
 def iter_random_device_weights(cfg, seed: int, device: str = "cuda", std: float = 0.02):
     """As random_device_weights, one tensor at a time (so a 7B model never
     holds a full f32 copy on the device)."""

@@ -205,6 +205,14 @@ extern "C" int ms_engine_tp_fused(const ms_engine *eng, int32_t *fused) {
   return MS_OK;
 }
 
+extern "C" int ms_engine_set_tp_fused(ms_engine *eng, int32_t on) {
+  if (!eng) return MS_E_INVALID;
+  if (eng->pending) return eng->fail(MS_E_INVALID, "ms_engine_set_tp_fused between launch and wait");
+  if (on && !eng->ar_capable) return eng->fail(MS_E_INVALID, "fused all-reduce not set up on this engine");
+  eng->ar_fused = on != 0;
+  return MS_OK;
+}
+
 extern "C" int ms_engine_set_graphs(ms_engine *eng, int32_t on) {
   if (!eng) return MS_E_INVALID;
   if (eng->pending) return eng->fail(MS_E_INVALID, "ms_engine_set_graphs between launch and wait");
@@ -245,6 +253,25 @@ extern "C" int ms_engine_profile(ms_engine *eng, int64_t *kernel_launches, int64
   if (attn_bytes_total) *attn_bytes_total = eng->prof_bytes;
   eng->prof_used = 0;
   eng->prof_bytes = 0.0;
+  return MS_OK;
+}
+
+extern "C" int ms_engine_profile_allreduce(ms_engine *eng, int64_t *calls, double *ms_total) {
+  if (!eng) return MS_E_INVALID;
+  double ms = 0.0;
+  if (eng->prof_ar_used) {
+    cudaError_t e = cudaSetDevice(eng->dev);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(eng->stream);
+    for (size_t i = 0; e == cudaSuccess && i + 1 < eng->prof_ar_used; i += 2) {
+      float t = 0.f;
+      e = cudaEventElapsedTime(&t, eng->prof_ar_ev[i], eng->prof_ar_ev[i + 1]);
+      ms += t;
+    }
+    if (e != cudaSuccess) return eng->fail(MS_E_DEVICE, cudaGetErrorString(e));
+  }
+  if (calls) *calls = int64_t(eng->prof_ar_used / 2);
+  if (ms_total) *ms_total = ms;
+  eng->prof_ar_used = 0;
   return MS_OK;
 }
 

@@ -282,6 +282,7 @@ void destroy_impl(Engine *eng) {
   for (void *p : {(void *)eng->h_in, (void *)eng->h_next, (void *)eng->h_status, (void *)eng->h_gin})
     if (p) cudaFreeHost(p);
   for (cudaEvent_t e : eng->prof_ev) cudaEventDestroy(e);
+  for (cudaEvent_t e : eng->prof_ar_ev) cudaEventDestroy(e);
   if (eng->done_ev) cudaEventDestroy(eng->done_ev);
   if (eng->stream) cudaStreamDestroy(eng->stream);
 }

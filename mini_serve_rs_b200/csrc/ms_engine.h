@@ -119,6 +119,7 @@ struct Engine {
   // tensor parallelism: peer-mapped partial-sum buffers for the fused
   // all-reduce + residual add + RMSNorm (ms_tp_allreduce.cu)
   bool ar_fused = false;
+  bool ar_capable = false;              // the peer mappings exist (fused setup agreed by all ranks)
   void *ar_sym = nullptr;               // own allocation: 2 partial-sum buffers + signal array
   void *ar_buf[2][8] = {};              // [buffer][rank]
   uint32_t *ar_sig[8] = {};             // each rank's signal array
@@ -132,6 +133,10 @@ struct Engine {
   std::vector<cudaEvent_t> prof_ev;  // pairs: start, end
   size_t prof_used = 0;              // events in use (2 per bracketed launch)
   double prof_bytes = 0.0;
+  // tensor parallelism: pairs around each all-reduce + residual add + RMSNorm
+  // (the fused kernel, or NCCL all-reduce + K4)
+  std::vector<cudaEvent_t> prof_ar_ev;
+  size_t prof_ar_used = 0;
 
   // host bookkeeping
   std::unordered_map<uint64_t, Seq> seqs;

@@ -41,15 +41,22 @@ cublasStatus_t linear(Engine *eng, const void *W, const void *X, void *Y, int ou
 }  // namespace
 
 namespace {
-// Records the next profiling event on the engine stream (created on first use).
-cudaError_t prof_mark(Engine *eng) {
-  if (eng->prof_used == eng->prof_ev.size()) {
+// Records the next profiling event of a log on the engine stream (created on
+// first use).
+cudaError_t prof_mark(Engine *eng, std::vector<cudaEvent_t> &log, size_t &used) {
+  if (used == log.size()) {
     cudaEvent_t e;
     cudaError_t err = cudaEventCreate(&e);
     if (err != cudaSuccess) return err;
-    eng->prof_ev.push_back(e);
+    log.push_back(e);
   }
-  return cudaEventRecord(eng->prof_ev[eng->prof_used++], eng->stream);
+  return cudaEventRecord(log[used++], eng->stream);
+}
+cudaError_t prof_mark(Engine *eng) { return prof_mark(eng, eng->prof_ev, eng->prof_used); }
+// Brackets a tensor-parallel all-reduce section when profiling.
+cudaError_t prof_ar_mark(Engine *eng) {
+  if (!eng->profiling || eng->tp <= 1) return cudaSuccess;
+  return prof_mark(eng, eng->prof_ar_ev, eng->prof_ar_used);
 }
 }  // namespace
 
@@ -182,28 +189,35 @@ int enqueue_forward(Engine *eng, const StepPlan &plan) {
     // o_proj, residual add + post-attention norm
     if (eng->ar_fused) {  // partial sums into the peer-mapped buffer, then sum + add + norm in one kernel
       MS_BLAS_TRY(linear(eng, w.w_o, eng->attn, eng->ar_buf[0][eng->rank], eng->H, T, eng->hq * eng->D));
+      MS_CUDA_TRY(prof_ar_mark(eng));
       MS_CUDA_TRY(launch_ar_add_rmsnorm(eng, 0, eng->x_resid, nullptr, w.ln2, eng->x_resid, eng->x_norm, T, st));
+      MS_CUDA_TRY(prof_ar_mark(eng));
     } else {
       MS_BLAS_TRY(linear(eng, w.w_o, eng->attn, eng->x_tmp, eng->H, T, eng->hq * eng->D));
+      MS_CUDA_TRY(prof_ar_mark(eng));
       if (eng->tp > 1 && nccl_allreduce_sum(eng->x_tmp, size_t(T) * eng->H, dt, eng->comm, st) != 0)
         return eng->fail(MS_E_DEVICE, "NCCL all-reduce after o_proj failed");
       MS_CUDA_TRY(launch_add_rmsnorm(eng->x_tmp, eng->x_resid, nullptr, w.ln2, eng->x_resid, eng->x_norm, T,
                                      eng->H, eps, dt, st));
+      MS_CUDA_TRY(prof_ar_mark(eng));
     }
     // MLP
     MS_BLAS_TRY(linear(eng, w.w_gu, eng->x_norm, eng->gu, 2 * eng->I, T, eng->H));
     MS_CUDA_TRY(launch_silu_mul(eng->gu, eng->act, T, eng->I, dt, st));
     if (eng->ar_fused) {
       MS_BLAS_TRY(linear(eng, w.w_down, eng->act, eng->ar_buf[1][eng->rank], eng->H, T, eng->I));
+      MS_CUDA_TRY(prof_ar_mark(eng));
       if (l + 1 < eng->L)
         MS_CUDA_TRY(launch_ar_add_rmsnorm(eng, 1, eng->x_resid, nullptr, eng->layers[l + 1].ln1, eng->x_resid,
                                           eng->x_norm, T, st));
       else  // final norm on each sequence's last row only
         MS_CUDA_TRY(launch_ar_add_rmsnorm(eng, 1, eng->x_resid, eng->d_last_index, eng->final_norm, nullptr,
                                           eng->last_norm, S, st));
+      MS_CUDA_TRY(prof_ar_mark(eng));
       continue;
     }
     MS_BLAS_TRY(linear(eng, w.w_down, eng->act, eng->x_tmp, eng->H, T, eng->I));
+    MS_CUDA_TRY(prof_ar_mark(eng));
     if (eng->tp > 1 && nccl_allreduce_sum(eng->x_tmp, size_t(T) * eng->H, dt, eng->comm, st) != 0)
       return eng->fail(MS_E_DEVICE, "NCCL all-reduce after down_proj failed");
     if (l + 1 < eng->L) {
@@ -214,6 +228,7 @@ int enqueue_forward(Engine *eng, const StepPlan &plan) {
       MS_CUDA_TRY(launch_add_rmsnorm(eng->x_tmp, eng->x_resid, eng->d_last_index, eng->final_norm, nullptr,
                                      eng->last_norm, S, eng->H, eps, dt, st));
     }
+    MS_CUDA_TRY(prof_ar_mark(eng));
   }
   // lm_head in f32 output, greedy argmax, tokens back to the host
   MS_BLAS_TRY(linear(eng, eng->lm_head, eng->last_norm, eng->logits, eng->V, S, eng->H, true));

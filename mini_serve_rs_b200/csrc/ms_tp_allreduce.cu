@@ -219,6 +219,7 @@ int tp_fused_setup(Engine *eng) {
     cudaFree(d_o);
   }
   eng->ar_fused = opened != 0;
+  eng->ar_capable = eng->ar_fused;
   if (!eng->ar_fused) tp_fused_teardown(eng);
   return MS_OK;
 }
@@ -229,6 +230,7 @@ void tp_fused_teardown(Engine *eng) {
   if (eng->ar_sym) cudaFree(eng->ar_sym);
   eng->ar_sym = nullptr;
   eng->ar_fused = false;
+  eng->ar_capable = false;
 }
 
 cudaError_t launch_ar_add_rmsnorm(Engine *eng, int which, const void *residual, const int32_t *row_index,

@@ -68,8 +68,10 @@ _SIGS = {
     "ms_engine_set_profiling": ([_P, _I32], C.c_int),
     "ms_engine_profile": ([_P, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(C.c_double),
                            C.POINTER(C.c_double)], C.c_int),
+    "ms_engine_profile_allreduce": ([_P, C.POINTER(C.c_int64), C.POINTER(C.c_double)], C.c_int),
     "ms_engine_set_graphs": ([_P, _I32], C.c_int),
     "ms_engine_tp_fused": ([_P, C.POINTER(_I32)], C.c_int),
+    "ms_engine_set_tp_fused": ([_P, _I32], C.c_int),
     "ms_engine_graph_stats": ([_P, C.POINTER(C.c_int64), C.POINTER(C.c_int64), C.POINTER(_I32)], C.c_int),
     "ms_nccl_get_unique_id": ([C.c_char_p, _I32], C.c_int),
     "ms_nccl_comm_init": ([C.POINTER(_P), _I32, C.c_char_p, _I32, _I32], C.c_int),
@@ -344,11 +346,22 @@ class Engine:
                     "profile")
         return kl.value, al.value, ms.value, by.value
 
+    def profile_allreduce(self):
+        """(all-reduce sections bracketed, their summed ms) under tensor parallelism."""
+        n, ms = C.c_int64(), C.c_double()
+        self._check(self.lib.ms_engine_profile_allreduce(self.h, C.byref(n), C.byref(ms)), "profile_allreduce")
+        return n.value, ms.value
+
     def tp_fused(self) -> bool:
         """True when TP all-reduces run as the fused peer-memory kernel."""
         v = _I32()
         self._check(self.lib.ms_engine_tp_fused(self.h, C.byref(v)), "tp_fused")
         return bool(v.value)
+
+    def set_tp_fused(self, on: bool):
+        """Fused peer-memory all-reduce (True, where set up) or NCCL (False) for
+        later steps; every rank of the group switches at the same step."""
+        self._check(self.lib.ms_engine_set_tp_fused(self.h, 1 if on else 0), "set_tp_fused")
 
     def set_graphs(self, on: bool):
         """Replay pure-decode steps from captured CUDA graphs (default on)."""

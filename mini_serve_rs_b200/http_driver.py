@@ -806,4 +806,5 @@ def summarize_http(results, elapsed: float) -> Dict[str, float]:
     return {"requests": len(results), "failed": len(results) - len(ok), "tokens": tokens, "elapsed_s": elapsed,
             "aggregate_tokens_per_s": tokens / elapsed if elapsed > 0 else 0.0,
             "ttft_ms_p50": pct(ttft, 0.5), "ttft_ms_p90": pct(ttft, 0.9), "ttft_ms_p99": pct(ttft, 0.99),
+            "ttft_ms_all": ttft,
             "per_request_decode_tokens_per_s_median": pct(dec, 0.5)}

@@ -20,6 +20,7 @@ from dataclasses import dataclass, field
 from typing import Deque, Dict, List, Optional
 
 from . import engine as E
+from .router import LatencyWindow, ReplicaMetrics
 
 
 @dataclass
@@ -55,6 +56,7 @@ class ServingLoop:
         self.active: List[Request] = []
         self.finished: List[Request] = []
         self.steps = 0
+        self.latency = LatencyWindow()  # scheduler.rs:543-550, read by the router
 
     def submit(self, r: Request):
         self.queue.append(r)
@@ -83,7 +85,17 @@ class ServingLoop:
         self.pages.release(r.rid)
         r.done_at = now
         r.error = error
+        if error is None:
+            self.latency.add((now - r.arrival) * 1000.0)
         self.finished.append(r)
+
+    def metrics(self) -> ReplicaMetrics:
+        """What the router reads (scheduler.rs:128-135): waiting requests that
+        have arrived, active requests, mean latency of the last 64 finished."""
+        now = self.clock()
+        waiting = sum(1 for r in self.queue if r.arrival <= now)
+        return ReplicaMetrics(queue_depth=waiting, active_count=len(self.active),
+                              avg_latency_ms=self.latency.avg_ms(), healthy=self.eng.is_healthy())
 
     def _grow(self, now: float):
         failed = []
@@ -160,6 +172,39 @@ class ServingLoop:
                 time.sleep(max(0.0, min(nxt - now, 0.01)))
         return self.clock()
 
+    def run_routed(self, link, requests: Dict[int, Request], timeout_s: float = 600.0) -> float:
+        """Serve the requests a Dispatcher routes to this replica (`link` is
+        its ReplicaLink; `requests` maps request id -> Request, with arrival
+        times on the dispatcher's clock).  The metrics go out after every step
+        and while idle.  Returns the elapsed seconds on the shared clock."""
+        t0_wall = link.start_time()
+        # clock() = wall-clock seconds since the dispatcher's t0, on this process's perf counter
+        self._t0 = time.perf_counter() - (time.time() - t0_wall)
+        last = None
+        while True:
+            for rid in link.poll():
+                self.submit(requests[rid])
+            now = self.clock()
+            if now > timeout_s:
+                raise TimeoutError("trace did not finish")
+            ran = self.step(now)
+            m = self.metrics()
+            key = (m.queue_depth, m.active_count, m.avg_latency_ms, m.healthy, link.got)
+            if key != last:  # only changes go to the store
+                link.publish(m)
+                last = key
+            if ran:
+                continue
+            if not self.queue and not self.active and link.finished():
+                late = link.poll()  # assigned between the last poll and the done mark
+                if not late:
+                    break
+                for rid in late:
+                    self.submit(requests[rid])
+                continue
+            time.sleep(0.001)
+        return self.clock()
+
 
 def summarize(reqs: List[Request], elapsed: float) -> Dict[str, float]:
     """Aggregate tokens/s and TTFT percentiles (examples/bench.rs:85-108, 189)."""
@@ -175,4 +220,5 @@ def summarize(reqs: List[Request], elapsed: float) -> Dict[str, float]:
     return {"requests": len(reqs), "failed": len(reqs) - len(ok), "tokens": tokens, "elapsed_s": elapsed,
             "aggregate_tokens_per_s": tokens / elapsed if elapsed > 0 else 0.0,
             "ttft_ms_p50": pct(ttft, 0.5), "ttft_ms_p90": pct(ttft, 0.9), "ttft_ms_p99": pct(ttft, 0.99),
+            "ttft_ms_all": ttft,
             "per_request_decode_tokens_per_s_median": pct(sorted(dec), 0.5)}

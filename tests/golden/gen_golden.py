@@ -13,7 +13,12 @@ Two independent sources pin the oracle:
    (``reference_rmsnorm``, ``reference_paged_gqa``) imported from the
    reference tree, on the cases that script runs (:132-251).
 
-Usage: python tests/golden/gen_golden.py [--ref /path/to/mini-serve-rs]
+Usage: python tests/golden/gen_golden.py [--ref /path/to/mini-serve-rs] [--cases NAME ...]
+
+The reference tree is taken from --ref, else $MS_REFERENCE_ROOT, else the
+"reference_path" of BASELINE.json at the repository root.  With --cases only
+the named model cases are (re)computed and merged into the existing
+golden.npz; every other stored array is kept as it is.
 """
 from __future__ import annotations
 
@@ -21,6 +26,7 @@ import argparse
 import importlib.util
 import json
 import math
+import os
 import sys
 from pathlib import Path
 
@@ -74,9 +80,11 @@ def logits_all(model, ids):
         return model(torch.tensor([ids], dtype=torch.long)).logits[0].to(torch.float32)
 
 
-def gen_model_cases(out):
+def gen_model_cases(out, only=None):
     meta = {}
     for case in MODEL_CASES:
+        if only and case["name"] not in only:
+            continue
         cfg = case["cfg"]
         w = sin_fixture_weights(cfg) if case["weights"] == "sin" else random_weights(
             cfg, case["seed"], norm_std=case.get("norm_std", 0.0))
@@ -129,20 +137,41 @@ def gen_kernel_cases(out, ref_root: Path):
         out[f"paged_gqa/{dt_name}/ragged"] = y.to(torch.float32).numpy()
 
 
+def reference_root(arg):
+    if arg is not None:
+        return arg
+    if os.environ.get("MS_REFERENCE_ROOT"):
+        return Path(os.environ["MS_REFERENCE_ROOT"])
+    baseline = ROOT / "BASELINE.json"
+    if baseline.exists():
+        p = json.loads(baseline.read_text()).get("reference_path")
+        if p:
+            return Path(p)
+    raise SystemExit("reference tree unknown: pass --ref or set MS_REFERENCE_ROOT")
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--ref", type=Path, default=None)
+    ap.add_argument("--cases", nargs="*", default=None,
+                    help="recompute only these model cases and merge them into the existing golden.npz")
     args = ap.parse_args()
     torch.manual_seed(0)
-    out = {}
-    meta = gen_model_cases(out)
-    gen_kernel_cases(out, args.ref)
-    np.savez_compressed(HERE / "golden.npz", **out)
     import transformers
-    meta_all = {"transformers": transformers.__version__, "torch": torch.__version__,
-                "numpy": np.__version__, "model_cases": meta,
-                "sources": {"model": "transformers Qwen2/Qwen3ForCausalLM, CPU f32, eager",
-                            "kernels": "scripts/validate_cuda_kernels.py:21-46 (reference tree)"}}
+    if args.cases:
+        with np.load(HERE / "golden.npz") as z:
+            out = {k: z[k] for k in z.files}
+        meta_all = json.loads((HERE / "golden_meta.json").read_text())
+        meta_all["model_cases"].update(gen_model_cases(out, set(args.cases)))
+    else:
+        out = {}
+        meta = gen_model_cases(out)
+        gen_kernel_cases(out, reference_root(args.ref))
+        meta_all = {"transformers": transformers.__version__, "torch": torch.__version__,
+                    "numpy": np.__version__, "model_cases": meta,
+                    "sources": {"model": "transformers Qwen2/Qwen3ForCausalLM, CPU f32, eager",
+                                "kernels": "scripts/validate_cuda_kernels.py:21-46 (reference tree)"}}
+    np.savez_compressed(HERE / "golden.npz", **out)
     (HERE / "golden_meta.json").write_text(json.dumps(meta_all, indent=2, sort_keys=True) + "\n")
     print("wrote", len(out), "arrays")
 

@@ -31,6 +31,15 @@ QWEN2_SMALL = Config(vocab_size=512, hidden_size=1792, intermediate_size=512, nu
                      attention_bias=True, tie_word_embeddings=False)
 
 
+# Qwen2.5-7B's attention shape (hidden 3584, 28 query / 4 KV heads x 128, q/k/v
+# bias, untied lm_head) on two layers with a small vocabulary and MLP: shards
+# one KV head per rank at TP=4, as the 7B model does.
+QWEN2_KV4 = Config(vocab_size=512, hidden_size=3584, intermediate_size=1024, num_hidden_layers=2,
+                   num_attention_heads=28, num_key_value_heads=4, max_position_embeddings=4096,
+                   head_dim=128, rope_theta=1e6, rms_norm_eps=1e-6, qk_norm=False,
+                   attention_bias=True, tie_word_embeddings=False)
+
+
 def _prompt(seed: int, n: int, vocab: int):
     rng = np.random.Generator(np.random.PCG64(seed))
     return [int(t) for t in rng.integers(0, vocab, n)]
@@ -44,6 +53,8 @@ MODEL_CASES = [
      "decode_steps": 8},
     {"name": "qwen2_small", "cfg": QWEN2_SMALL, "weights": "random", "seed": 4321,
      "prompts": [_prompt(21, 16, 512), _prompt(22, 31, 512)], "decode_steps": 6},
+    {"name": "qwen2_kv4", "cfg": QWEN2_KV4, "weights": "random", "seed": 7007,
+     "prompts": [_prompt(31, 20, 512), _prompt(32, 37, 512), _prompt(33, 50, 512)], "decode_steps": 6},
 ]
 
 # --- kernel cases (scripts/validate_cuda_kernels.py:132-251) -----------------
