@@ -202,6 +202,9 @@ typedef struct ms_pages_stats {
   int64_t hits, misses, tokens_saved; /* record_reuse, prefix_cache.rs:359-367 */
   int64_t evictions;         /* cached chunks evicted */
   int64_t rejections;        /* admissions / block requests refused (CachePressure) */
+  int64_t reserved_blocks;   /* worst-case pages held by reservations */
+  int64_t peak_reserved_blocks;
+  int64_t reservation_rejections; /* ms_pages_reserve refused (CachePressure) */
 } ms_pages_stats;
 /* max_chunks = 0 disables the prefix cache: block ids are then exactly
  * KVCache's (LIFO stack popping 0, 1, 2, ... first). */
@@ -225,6 +228,18 @@ int ms_pages_publish(ms_pages *pm, uint64_t seq_id, const uint32_t *prompt, int3
                      int32_t *published_out);
 /* PrefixCache::lookup (prefix_cache.rs:126-157): leading cached tokens. */
 int ms_pages_lookup(ms_pages *pm, const uint32_t *prompt, int32_t prompt_len, int32_t *matched_tokens);
+/* reserve_sequence's memory budget (candle.rs:349-375, tensor_memory.rs:72-111,
+ * prefix_cache.rs:229-244) with the page pool as the budget: a request is
+ * charged its worst case, ceil((prompt_len + max_tokens) / block_size) pages.
+ * Reservations plus the pages only the prefix cache holds must fit the pool;
+ * least recently used cache-only pages are evicted to make room, and when
+ * that is not enough the call returns MS_E_PRESSURE (CachePressure) and
+ * charges nothing (the entries evicted on the way stay evicted, as in the
+ * reference).  Idempotent per seq_id (a second call returns MS_OK without
+ * a new charge); prompt_len or max_tokens <= 0 is MS_E_TOKEN_LIMIT.
+ * ms_pages_release also ends the sequence's reservation.  While every
+ * admitted sequence holds a reservation, its page requests never fail. */
+int ms_pages_reserve(ms_pages *pm, uint64_t seq_id, int64_t prompt_len, int64_t max_tokens);
 int ms_pages_stats_get(ms_pages *pm, ms_pages_stats *out);
 /* The chain keys (32 bytes each) of the full chunks of tokens; returns their
  * count, -1 on bad arguments or capacity (in keys) too small. */

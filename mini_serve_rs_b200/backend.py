@@ -4,7 +4,10 @@ Mirrors ``trait ModelBackend`` (src/backends/traits.rs:15-50) as
 CandleBackend implements it (src/backends/candle.rs:304-705), with the
 forward step running in the sm_100a engine:
 
-* ``reserve_sequence`` -- idempotent per id (candle.rs:349-375).
+* ``reserve_sequence`` -- idempotent per id (candle.rs:349-375): the request's
+  worst-case KV pages, ceil((prompt + max_tokens) / 16), are charged against
+  the engine's page pool (the B200 path's tensor-memory budget, see
+  ``Pages.reserve``); ``CachePressure`` when they do not fit.
 * ``step_batch`` -- one token per sequence in input order; sequences not yet
   prefilled get their prompt run and ``is_prefilled`` set (candle.rs:431-433);
   the others decode their last output token.  Block ids come from the
@@ -23,7 +26,7 @@ from typing import Dict, List, Sequence, Set
 
 import numpy as np
 
-from .engine import BackendError, Engine, NoHealthyWorkers, TokenLimitExceeded
+from .engine import BackendError, Engine, NoHealthyWorkers, Pages, TokenLimitExceeded
 
 
 @dataclass
@@ -36,11 +39,17 @@ class StepToken:
 
 
 class CudaBackend:
-    def __init__(self, engine: Engine, name: str = "ms-b200", eos_ids: Sequence[int] = ()):
+    def __init__(self, engine: Engine, name: str = "ms-b200", eos_ids: Sequence[int] = (),
+                 budget: Pages = None):
+        """budget: the reservation ledger; by default one over the engine's
+        whole page pool (no prefix cache)."""
         self.engine = engine
         self._name = name
         self.eos: Set[int] = set(int(e) for e in eos_ids)
-        self._ids: Dict[str, int] = {}      # request id -> engine sequence id
+        self.budget = budget if budget is not None else Pages(int(engine.opts.pool_blocks),
+                                                              int(engine.opts.block_size), max_chunks=0)
+        self._ids: Dict[str, int] = {}      # request id -> engine sequence id (from its reservation on)
+        self._admitted: Set[str] = set()    # requests the engine holds
         self._pushed: Dict[str, int] = {}   # blocks already handed to the engine
         self._reserved: Set[str] = set()
         self._next = 1
@@ -56,7 +65,10 @@ class CudaBackend:
     def mark_unhealthy(self):
         self._healthy = False
         self.engine.mark_unhealthy()
+        for sid in self._ids.values():
+            self.budget.release(sid)
         self._ids.clear()
+        self._admitted.clear()
         self._pushed.clear()
         self._reserved.clear()
 
@@ -70,14 +82,24 @@ class CudaBackend:
             return
         if prompt_tokens == 0 or max_tokens == 0 or prompt_tokens + max_tokens > self.context_length():
             raise TokenLimitExceeded("Request exceeds model context or has zero tokens")
+        sid = self._ids.get(request_id)
+        if sid is None:
+            sid = self._next
+            self._next += 1
+        self.budget.reserve(sid, prompt_tokens, max_tokens)  # CachePressure: nothing is kept
+        self._ids[request_id] = sid
         self._reserved.add(request_id)
 
     def cancel_sequence(self, request_id: str):
         sid = self._ids.pop(request_id, None)
         self._pushed.pop(request_id, None)
         self._reserved.discard(request_id)
-        if sid is not None and self.engine.is_healthy():
-            self.engine.release(sid)
+        admitted = request_id in self._admitted
+        self._admitted.discard(request_id)
+        if sid is not None:
+            self.budget.release(sid)
+            if admitted and self.engine.is_healthy():
+                self.engine.release(sid)
 
     def step_batch(self, sequences: List) -> List[int]:
         """sequences: objects with request_id, prompt_tokens, output_tokens,
@@ -101,11 +123,10 @@ class CudaBackend:
         for i, s in enumerate(sequences):
             rid = s.request_id
             self.reserve_sequence(rid, len(s.prompt_tokens), s.max_tokens)
-            if rid not in self._ids:
-                sid = self._next
-                self._next += 1
+            if rid not in self._admitted:
+                sid = self._ids[rid]
                 eng.admit(sid, s.prompt_tokens, s.kv_blocks, 0)
-                self._ids[rid] = sid
+                self._admitted.add(rid)
                 self._pushed[rid] = len(s.kv_blocks)
             else:
                 for b in s.kv_blocks[self._pushed[rid]:]:

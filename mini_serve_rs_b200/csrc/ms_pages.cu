@@ -171,6 +171,8 @@ struct PageManager {
   };
   std::unordered_map<Key, Chunk, KeyHash> chunks;
   std::list<Key> lru;  // front: least recently used
+  std::unordered_map<uint64_t, int64_t> reservations;  // seq -> worst-case pages
+  int64_t reserved = 0;
   ms_pages_stats st{};
 
   int64_t blocks_needed(int64_t tokens) const { return tokens == 0 ? 1 : (tokens + bs - 1) / bs; }
@@ -199,6 +201,12 @@ struct PageManager {
       return true;
     }
     return false;
+  }
+
+  int64_t cache_only() const {
+    int64_t n = 0;
+    for (const auto &kv : chunks) n += refs[kv.second.page] == 1;
+    return n;
   }
 
   bool make_free(int64_t n) {
@@ -313,9 +321,35 @@ extern "C" int ms_pages_allocate_block(ms_pages *pm, uint64_t seq_id, int32_t *b
   return MS_OK;
 }
 
+extern "C" int ms_pages_reserve(ms_pages *pm, uint64_t seq_id, int64_t prompt_len, int64_t max_tokens) {
+  if (!pm) return MS_E_INVALID;
+  std::lock_guard<std::mutex> lk(pm->mu);
+  if (pm->reservations.count(seq_id)) return MS_OK;
+  if (prompt_len <= 0 || max_tokens <= 0 || prompt_len > INT32_MAX || max_tokens > INT32_MAX) return MS_E_TOKEN_LIMIT;
+  const int64_t need = (prompt_len + max_tokens + pm->bs - 1) / pm->bs;
+  // prefix_cache.rs:229-244: evict cached entries until the charge fits
+  int64_t only = pm->cache_only();
+  while (pm->reserved + need + only > pm->total) {
+    if (!pm->evict_one(true)) {
+      ++pm->st.reservation_rejections;
+      return MS_E_PRESSURE;
+    }
+    --only;
+  }
+  pm->reservations.emplace(seq_id, need);
+  pm->reserved += need;
+  pm->st.peak_reserved_blocks = std::max(pm->st.peak_reserved_blocks, pm->reserved);
+  return MS_OK;
+}
+
 extern "C" int ms_pages_release(ms_pages *pm, uint64_t seq_id, int32_t *released_out) {
   if (!pm) return MS_E_INVALID;
   std::lock_guard<std::mutex> lk(pm->mu);
+  auto rv = pm->reservations.find(seq_id);
+  if (rv != pm->reservations.end()) {
+    pm->reserved -= rv->second;
+    pm->reservations.erase(rv);
+  }
   auto it = pm->alloc.find(seq_id);
   int32_t n = 0;
   if (it != pm->alloc.end()) {
@@ -383,6 +417,7 @@ extern "C" int ms_pages_stats_get(ms_pages *pm, ms_pages_stats *out) {
   int64_t only = 0;
   for (const auto &kv : pm->chunks) only += pm->refs[kv.second.page] == 1;
   s.cache_only_blocks = only;
+  s.reserved_blocks = pm->reserved;
   *out = s;
   return MS_OK;
 }

@@ -46,7 +46,8 @@ class MsStepDesc(C.Structure):
 
 class MsPagesStats(C.Structure):
     _fields_ = [(n, C.c_int64) for n in ("total_blocks", "free_blocks", "cached_chunks", "cache_only_blocks",
-                                         "hits", "misses", "tokens_saved", "evictions", "rejections")]
+                                         "hits", "misses", "tokens_saved", "evictions", "rejections",
+                                         "reserved_blocks", "peak_reserved_blocks", "reservation_rejections")]
 
 
 _P = C.c_void_p
@@ -105,6 +106,7 @@ _SIGS = {
     "ms_pages_release": ([_P, C.c_uint64, C.POINTER(_I32)], C.c_int),
     "ms_pages_publish": ([_P, C.c_uint64, _P, _I32, C.POINTER(_I32)], C.c_int),
     "ms_pages_lookup": ([_P, _P, _I32, C.POINTER(_I32)], C.c_int),
+    "ms_pages_reserve": ([_P, C.c_uint64, C.c_int64, C.c_int64], C.c_int),
     "ms_pages_stats_get": ([_P, C.POINTER(MsPagesStats)], C.c_int),
     "ms_prefix_chunk_hashes": ([_P, _I32, _I32, _P, _I32], C.c_int),
     "launch_rmsnorm_f32": ([_P, _P, _P, C.c_int, C.c_int, C.c_float], C.c_int),
@@ -446,6 +448,14 @@ class Pages:
         if rc != MS_OK:
             raise error_for(rc, "ms_pages_admit")
         return out[:n.value].tolist(), cached.value
+
+    def reserve(self, seq_id: int, prompt_len: int, max_tokens: int):
+        """Charge the request's worst-case pages against the pool (idempotent per
+        id); raises CachePressure when they do not fit, TokenLimitExceeded for a
+        zero-length prompt or zero max_tokens."""
+        rc = self.lib.ms_pages_reserve(self.h, seq_id, prompt_len, max_tokens)
+        if rc != MS_OK:
+            raise error_for(rc, "Tensor memory budget exhausted" if rc == MS_E_PRESSURE else "ms_pages_reserve")
 
     def allocate_block(self, seq_id: int) -> int:
         b = _I32()

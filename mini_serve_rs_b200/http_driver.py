@@ -359,6 +359,7 @@ class ServingServer:
         r = sub.req
         if r in sl.queue:
             sl.queue.remove(r)
+            sl.pages.release(rid)  # a queued request may already hold its reservation
         elif r in sl.active:
             sl.active.remove(r)
             sl.eng.release(rid)
@@ -394,6 +395,8 @@ class ServingServer:
                     release(r.rid)
                 except Exception:  # the engine may be quarantined; pages must still be returned
                     pass
+        for r in list(sl.queue):
+            sl.pages.release(r.rid)  # reservations of queued requests
         for r in list(sl.active) + list(sl.queue):
             r.error = msg
             r.done_at = sl.clock()

@@ -2,8 +2,10 @@
 
 The caller side of the hot path, as the reference's Scheduler runs it
 (src/scheduler/scheduler.rs):
-* FIFO admission while there is room (:312-382).  A request that does not
-  get its pages (CachePressure) stays queued.
+* FIFO admission while there is room (:312-382).  Each request first reserves
+  its worst-case pages (reserve_sequence); one whose reservation or pages do
+  not fit stays queued until running requests free room (with nothing
+  running, a reservation that cannot fit fails the request).
 * One ragged ms_step per iteration over every active request (:422-449).
 * Block growth before a step (:430-431).
 * Release when a request finishes (:555) or fails (:446).
@@ -64,6 +66,19 @@ class ServingLoop:
     def _admit(self, now: float):
         while self.queue and self.queue[0].arrival <= now and len(self.active) < self.max_active:
             r = self.queue[0]
+            # reserve_sequence before the first forward (scheduler.rs:325-343): the request's
+            # worst-case pages; while they do not fit it waits for running requests to finish,
+            # and fails (as the reference's admission does) when nothing is running
+            try:
+                self.pages.reserve(r.rid, len(r.prompt), r.max_tokens)
+            except E.EngineError as e:
+                if isinstance(e, E.CachePressure) and self.active:
+                    break
+                self.queue.popleft()
+                r.error = str(e)
+                r.done_at = now
+                self.finished.append(r)
+                continue
             try:
                 r.blocks, r.cached = self.pages.admit(r.rid, r.prompt)
             except E.CachePressure:

@@ -12,6 +12,14 @@ prefix cache's LRU policy (prefix_cache.rs:126-157 lookup refresh,
 213-243 eviction under pressure, 319-321 the max_chunks cap).  Chunks are
 pages.  It follows the same rules step by step, so a trace of admissions,
 growth, publication and release yields the same block ids and counters.
+
+`reserve` restates the admission budget (CandleBackend::reserve_sequence,
+candle.rs:349-375, charging through PrefixCache::reserve_memory,
+prefix_cache.rs:229-244, against TensorMemoryBudget::try_reserve,
+tensor_memory.rs:72-88) with the pool as the budget: a request costs
+ceil((prompt + max_tokens) / block_size) pages; reservations plus cache-only
+pages must fit the pool, evicting the oldest evictable entries first; a repeat
+reservation of the same id is free (candle.rs:361-363).
 """
 from __future__ import annotations
 
@@ -47,6 +55,8 @@ class PagesRef:
         # key -> [page, parent key or None, children]; order = LRU (first = oldest)
         self.chunks: "OrderedDict[str, list]" = OrderedDict()
         self.hits = self.misses = self.tokens_saved = self.evictions = self.rejections = 0
+        self.reservations: Dict[int, int] = {}
+        self.peak_reserved = self.reservation_rejections = 0
 
     def blocks_needed(self, tokens: int) -> int:
         return 1 if tokens == 0 else -(-tokens // self.bs)
@@ -123,7 +133,24 @@ class PagesRef:
         self.alloc[seq].append(p)
         return p
 
+    def _cache_only(self) -> int:
+        return sum(1 for v in self.chunks.values() if self.refs[v[0]] == 1)
+
+    def reserve(self, seq: int, prompt_len: int, max_tokens: int):
+        if seq in self.reservations:
+            return
+        if prompt_len <= 0 or max_tokens <= 0:
+            raise ValueError("Request exceeds model context or has zero tokens")
+        need = -(-(prompt_len + max_tokens) // self.bs)
+        while sum(self.reservations.values()) + need + self._cache_only() > self.total:
+            if not self._evict_one(True):
+                self.reservation_rejections += 1
+                raise CachePressure("Tensor memory budget exhausted")
+        self.reservations[seq] = need
+        self.peak_reserved = max(self.peak_reserved, sum(self.reservations.values()))
+
     def release(self, seq: int) -> int:
+        self.reservations.pop(seq, None)
         pages = self.alloc.pop(seq, None)
         if pages is None:
             return 0
@@ -166,4 +193,6 @@ class PagesRef:
         return {"total_blocks": self.total, "free_blocks": len(self.free), "cached_chunks": len(self.chunks),
                 "cache_only_blocks": sum(1 for v in self.chunks.values() if self.refs[v[0]] == 1),
                 "hits": self.hits, "misses": self.misses, "tokens_saved": self.tokens_saved,
-                "evictions": self.evictions, "rejections": self.rejections}
+                "evictions": self.evictions, "rejections": self.rejections,
+                "reserved_blocks": sum(self.reservations.values()), "peak_reserved_blocks": self.peak_reserved,
+                "reservation_rejections": self.reservation_rejections}

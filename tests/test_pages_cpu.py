@@ -65,8 +65,18 @@ def test_random_trace_matches_restated_manager():
     pg, ref = E.Pages(96, 16, max_chunks=24), PagesRef(96, 16, max_chunks=24)
     live = {}
     for step in range(1500):
-        op = int(rng.integers(0, 5))
-        if op <= 1:
+        op = int(rng.integers(0, 6))
+        if op == 5:  # a reservation (for a sequence admitted now, later or never)
+            sid = step + int(rng.integers(0, 3))
+            plen, mt = int(rng.integers(1, 200)), int(rng.integers(1, 200))
+            try:
+                ref.reserve(sid, plen, mt)
+            except RefPressure:
+                with pytest.raises(E.CachePressure):
+                    pg.reserve(sid, plen, mt)
+            else:
+                pg.reserve(sid, plen, mt)
+        elif op <= 1:
             sid = step + 1
             base = prefixes[int(rng.integers(0, len(prefixes)))] if rng.random() < 0.8 else []
             prompt = base[:int(rng.integers(0, len(base) + 1))] + rng.integers(0, 50000, int(rng.integers(0, 40))).tolist()
@@ -100,6 +110,7 @@ def test_random_trace_matches_restated_manager():
         assert pg.stats() == ref.stats(), step
     st = pg.stats()
     assert st["hits"] > 50 and st["evictions"] > 0 and st["rejections"] > 0, st
+    assert st["peak_reserved_blocks"] > 0 and st["reservation_rejections"] > 0, st
 
 
 def test_reference_prefix_cache_tests_in_page_form():
