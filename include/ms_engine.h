@@ -328,6 +328,14 @@ int ms_debug_logits(ms_engine *eng, float *out, int64_t count);
  * "act" [T, I], "last_norm" [num_seqs, H] (model dtype), "row_ctx" /
  * "row_table" / "positions" [T] (int32).  Fails if `bytes` is too small. */
 int ms_debug_buffer(ms_engine *eng, const char *name, void *out, int64_t bytes);
+/* Debugging, for per-layer parity checks: layer >= 0 makes later steps stop
+ * after that layer's MLP down projection (no residual add after it, no final
+ * norm, lm_head or sampling), so ms_debug_buffer returns that layer's "attn"
+ * (attention output), "x_resid" (residual after attention), "x_norm"
+ * (post-attention RMSNorm) and "x_tmp" (MLP output); -1 turns it off.  Such a
+ * step leaves its sequences' later layers without K/V: release them after.
+ * Eager steps only; not with the fused TP all-reduce. */
+int ms_debug_stop_after_layer(ms_engine *eng, int32_t layer);
 /* Device address of layer `layer`'s K (which = 0) or V (which = 1) page pool,
  * laid out [pool_blocks, num_kv_heads_local, block_size, head_dim]. */
 int ms_debug_pool_ptr(ms_engine *eng, int32_t layer, int32_t which, void **ptr);
@@ -403,6 +411,20 @@ int ms_prefill_tiles(const int32_t *seq_row0, const int32_t *seq_ntok, const int
                      const int32_t *seq_table_row, int32_t num_seqs, int32_t num_heads,
                      int32_t num_kv_heads, int32_t *tiles_out, int32_t capacity);
 
+/* Status of the kernels launched without an engine on `device`: the
+ * prototype-compatible launchers below, and ms_launch_paged_attention /
+ * ms_launch_paged_prefill (which use it when their own status word is NULL).
+ * Synchronises the device, returns the OR of the kernels' status bits since
+ * the last call (1 = a bounded wait ran out and the kernel returned without
+ * writing its output, 2 = an index out of range) and clears them.  No
+ * counterpart in the reference, whose kernels do not wait on barriers. */
+int ms_kernel_status(int32_t device, uint32_t *status_out);
+/* Test hook: polls > 0 limits every page-loop wait of the decode-attention
+ * kernels launched afterwards to that many polls (0 restores the default of
+ * 4M polls), so a test can make a wait run out while every copy it started
+ * still lands (the drain after a failed wait keeps the default limit). */
+int ms_test_set_attention_wait_limit(int32_t polls);
+
 /* K6b on-device sampling over f32 logits [rows, vocab]: for each row with
  * temperature[row] >= 1e-7 the token is drawn as candle-transformers'
  * LogitsProcessor draws it (softmax of logits / temperature, top-p nucleus
@@ -422,7 +444,9 @@ int ms_launch_argmax(const float *logits, int32_t rows, int32_t vocab, int32_t *
  * Same signatures and argument checks as the reference's prototype C ABI
  * (docs/colab_cuda_kernels/mini_serve_kernels.cu:247-296): default stream,
  * asynchronous, cudaError_t as int, block size 16, head_dim 128.  They run
- * this library's kernels. */
+ * this library's kernels.  The return value covers the launch only; a
+ * failure inside the kernel (a bounded wait that ran out) sets a bit of the
+ * device's status word, which ms_kernel_status returns. */
 int launch_rmsnorm_f32(const float *d_x, const float *d_w, float *d_out, int num_rows,
                        int hidden_size, float eps);
 int launch_rmsnorm_f16(const void *d_x, const void *d_w, void *d_out, int num_rows,
@@ -453,10 +477,13 @@ int launch_paged_gqa_decode_tiled_bf16(const void *d_q, const void *d_k_pool,
  * fixed 16 MiB buffer inside the library, which every GPU that loads the
  * library holds until exit.  A call whose scratch would exceed 16 MiB
  * (batch_size * num_heads * partitions * 520 bytes) returns
- * cudaErrorMemoryAllocation without launching anything.  The first call on a
- * device looks the buffer's address up (make it before any stream capture).
- * Calls share the buffer: calls that may overlap on the GPU race and must be
- * serialised by the caller. */
+ * cudaErrorMemoryAllocation without launching anything.  The CUDA runtime
+ * reserves the 16 MiB on a device when it loads the buffer's module there --
+ * under CUDA's default lazy module loading, at the first call on that device
+ * -- so make one call per device before the caller's allocator claims its
+ * HBM, and before any stream capture.  Calls share the buffer: calls that may
+ * overlap on the GPU race and must be serialised by the caller.  A bounded
+ * wait that ran out inside the kernel is reported by ms_kernel_status. */
 int launch_paged_gqa_decode_tiled_bf16_noalloc(const void *d_q, const void *d_k_pool,
                                                const void *d_v_pool, const int *d_block_tables,
                                                const int *d_seq_lens, void *d_out, int batch_size,

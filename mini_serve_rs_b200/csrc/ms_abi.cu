@@ -275,6 +275,14 @@ extern "C" int ms_engine_profile_allreduce(ms_engine *eng, int64_t *calls, doubl
   return MS_OK;
 }
 
+extern "C" int ms_debug_stop_after_layer(ms_engine *eng, int32_t layer) {
+  if (!eng || layer < -1 || layer >= eng->L) return MS_E_INVALID;
+  if (eng->pending) return eng->fail(MS_E_INVALID, "ms_debug_stop_after_layer between launch and wait");
+  if (layer >= 0 && eng->ar_fused) return eng->fail(MS_E_INVALID, "not available with the fused TP all-reduce");
+  eng->debug_stop_layer = layer;
+  return MS_OK;
+}
+
 extern "C" int ms_debug_buffer(ms_engine *eng, const char *name, void *out, int64_t bytes) {
   if (!eng || !name || !out) return MS_E_INVALID;
   if (eng->pending) return eng->fail(MS_E_INVALID, "step in flight");

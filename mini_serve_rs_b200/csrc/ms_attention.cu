@@ -18,6 +18,7 @@
 // warps merge in shared memory, partitions merge in a second kernel by
 // log-sum-exp.
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "ms_attention_common.cuh"
@@ -162,7 +163,7 @@ __global__ void __launch_bounds__(kWarps * 32) paged_attention_kernel(Params p) 
     const int s = k % NSTAGE;
     const uint32_t parity = (k / NSTAGE) & 1;
     // the whole warp agrees before leaving, so no lane is left waiting in a shuffle
-    if (!__all_sync(kFull, mbar_wait_bounded(&my_bar[s], parity))) {
+    if (!__all_sync(kFull, mbar_wait_bounded(&my_bar[s], parity, p.wait_limit))) {
       failed = true;
       kfail = k;
       break;
@@ -314,13 +315,13 @@ cudaError_t launch_t(const Params &p, int num_rows, cudaStream_t stream) {
   constexpr int NSTAGE = default_stages<T, D, G>();
   auto kern = paged_attention_kernel<T, D, G, NSTAGE>;
   const size_t smem = smem_bytes<T, D, G>();
-  static bool attr_done[64] = {false};  // per device
+  static std::atomic<bool> attr_done[64];  // per device; zero-initialised (static storage)
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 64 && !attr_done[dev]) {
+  if (dev < 64 && !attr_done[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
-    attr_done[dev] = true;
+    attr_done[dev].store(true, std::memory_order_release);  // setting twice is harmless
   }
   dim3 grid(num_rows, p.num_kv_heads, p.max_parts);
   kern<<<grid, kWarps * 32, smem, stream>>>(p);
@@ -348,10 +349,22 @@ cudaError_t dispatch_dim(const Params &p, int head_dim, int group, int num_rows,
   return cudaErrorInvalidValue;
 }
 
-// device status word for kernels launched without an engine
+// Device status word of the launches made without an engine status word
+// (the prototype-compatible launchers, ms_launch_* with a null status): the
+// kernels OR their kStatus* bits into it; ms_kernel_status reads and clears it.
 __device__ unsigned g_status_scratch;
 
+// Test hook: > 0 replaces the poll limit of the page-loop waits (ms_test_set_attention_wait_limit).
+std::atomic<int> g_test_wait_limit{0};
+
 }  // namespace attn
+
+cudaError_t standalone_status_word(unsigned **out) {
+  void *sp = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&sp, attn::g_status_scratch);
+  if (e == cudaSuccess) *out = static_cast<unsigned *>(sp);
+  return e;
+}
 
 int choose_partition_blocks(int num_rows, int num_kv_heads, int max_ctx, long long total_blocks) {
   // Aim for >= ~16 CTAs per SM in total while keeping >= 2 pages per warp.
@@ -400,12 +413,12 @@ cudaError_t launch_paged_attention(const AttnArgs &a, cudaStream_t stream) {
   p.max_parts = (max_blk + a.part_blocks - 1) / a.part_blocks;
   if (p.max_parts > 65535) return cudaErrorInvalidValue;
   p.qscale = a.scale * attn::kLog2e;
+  const int test_limit = attn::g_test_wait_limit.load(std::memory_order_relaxed);
+  p.wait_limit = test_limit > 0 ? test_limit : attn::kWaitLimit;
   p.status = a.status;
   if (p.status == nullptr) {
-    void *sp = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&sp, attn::g_status_scratch);
+    cudaError_t e = standalone_status_word(&p.status);
     if (e != cudaSuccess) return e;
-    p.status = static_cast<unsigned *>(sp);
   }
   p.ws_o = nullptr;
   p.ws_ml = nullptr;
@@ -549,4 +562,26 @@ extern "C" int launch_paged_gqa_decode_tiled_bf16(const void *d_q, const void *d
                                                   int max_blocks_per_seq, float scale) {
   return proto_attention(d_q, d_k_pool, d_v_pool, d_block_tables, d_seq_lens, d_out, batch_size,
                          num_heads, num_kv_heads, max_blocks_per_seq, scale, MS_DTYPE_BF16);
+}
+
+extern "C" int ms_kernel_status(int32_t device, uint32_t *out) {
+  if (!out || device < 0) return MS_E_INVALID;
+  int prev = 0;
+  cudaError_t e = cudaGetDevice(&prev);
+  if (e == cudaSuccess) e = cudaSetDevice(device);
+  if (e != cudaSuccess) return MS_E_DEVICE;
+  unsigned v = 0, zero = 0;
+  e = cudaDeviceSynchronize();  // every launch made before this call has finished
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, ms::attn::g_status_scratch, sizeof(v));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(ms::attn::g_status_scratch, &zero, sizeof(zero));
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return MS_E_DEVICE;
+  *out = v;
+  return MS_OK;
+}
+
+extern "C" int ms_test_set_attention_wait_limit(int32_t polls) {
+  if (polls < 0) return MS_E_INVALID;
+  ms::attn::g_test_wait_limit.store(polls, std::memory_order_relaxed);
+  return MS_OK;
 }

@@ -33,7 +33,8 @@ struct Params {
   int num_kv_heads;
   int part_blocks;  // pages per partition
   int max_parts;
-  float qscale;  // softmax scale * log2(e)
+  float qscale;    // softmax scale * log2(e)
+  int wait_limit;  // polls before a wait in the page loop gives up (the drain after it uses kWaitLimit)
 };
 
 // ---- PTX wrappers ------------------------------------------------------------------
@@ -80,8 +81,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 // Polls with an iteration limit; returns false when it gave up.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
-  for (int i = 0; i < kWaitLimit; ++i)
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int limit = kWaitLimit) {
+  for (int i = 0; i < limit; ++i)
     if (mbar_try_wait(bar, parity)) return true;
   return false;
 }

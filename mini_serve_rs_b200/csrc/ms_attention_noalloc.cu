@@ -10,18 +10,26 @@
 // kernel with its split-K scratch in a fixed buffer that is part of the
 // library image.
 //
-// The buffer is a file-scope __device__ array of kScratchBytes (16 MiB): every
-// GPU on which the library is loaded holds those 16 MiB until the process
-// exits.  Host code cannot use the array's name as a device address, so the
-// first call on each device (with that device current) asks the runtime for
-// the address with cudaGetSymbolAddress and keeps it; make that first call
-// before any stream capture.  All calls share the one buffer and it keeps the
+// The buffer is a file-scope __device__ array of kScratchBytes (16 MiB).  The
+// CUDA runtime reserves it on a device when it loads this file's module
+// there: with CUDA's default lazy module loading that is the first call of
+// this entry point on the device (or an earlier use of the symbol), with
+// CUDA_MODULE_LOADING=EAGER it is when the library's first CUDA call
+// initialises the device.  It stays reserved until the process exits.  A
+// caller whose allocator claims nearly all of HBM must therefore make one
+// call per device before that (any small batch will do), or the load itself
+// can fail with an out-of-memory error; make that first call before any
+// stream capture as well.  Host code cannot use the array's name as a device
+// address: every call asks the runtime for the current device's address with
+// cudaGetSymbolAddress (cheap once loaded, and never stale after a context is
+// torn down and recreated).  All calls share the one buffer and it keeps the
 // last call's contents: calls that can overlap on the GPU (different streams
 // without ordering between them) race on it and must be serialised by the
 // caller.  Nothing in the buffer has to start at zero: each call writes every
-// partial result it later reads.
+// partial result it later reads.  A kernel-side failure (a bounded wait that
+// ran out) is recorded in the per-device status word that ms_kernel_status
+// reads and clears.
 #include <algorithm>
-#include <mutex>
 
 #include "ms_common.cuh"
 #include "ms_internal.h"
@@ -30,9 +38,6 @@ namespace {
 
 constexpr size_t kScratchBytes = size_t(16) << 20;
 __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
-
-std::mutex g_setup_mu;
-void *g_scratch_addr[64] = {};  // device address of g_noalloc_scratch, per device
 
 }  // namespace
 
@@ -52,21 +57,10 @@ extern "C" int launch_paged_gqa_decode_tiled_bf16_noalloc(const void *d_q, const
   const int64_t need = ms::attention_workspace_bytes(batch_size, num_heads, max_ctx, part);
   if (need > int64_t(kScratchBytes)) return int(cudaErrorMemoryAllocation);  // beyond the fixed scratch
 
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return int(e);
-  if (dev < 0 || dev >= 64) return int(cudaErrorInvalidDevice);
+  // the current device's copy of the buffer (loads this module on the first call there)
   void *scratch = nullptr;
-  {
-    std::lock_guard<std::mutex> lk(g_setup_mu);
-    if (!g_scratch_addr[dev]) {  // once per device, with that device current
-      void *p = nullptr;
-      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-      if (e != cudaSuccess) return int(e);
-      g_scratch_addr[dev] = p;
-    }
-    scratch = g_scratch_addr[dev];
-  }
+  const cudaError_t e = cudaGetSymbolAddress(&scratch, g_noalloc_scratch);
+  if (e != cudaSuccess) return int(e);
   ms::AttnArgs a{};
   a.q = d_q;
   a.k_pool = d_k_pool;

@@ -23,6 +23,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 #include <mutex>
 
@@ -148,7 +149,7 @@ __global__ void __launch_bounds__(kWarps * 32)
   for (int k = 0; k < nb_w; ++k) {
     const int s = k % NSTAGE;
     // the whole warp agrees before leaving, so no lane is left waiting in a shuffle
-    if (!__all_sync(kFull, mbar_wait_bounded(&my_bar[s], (k / NSTAGE) & 1))) {
+    if (!__all_sync(kFull, mbar_wait_bounded(&my_bar[s], (k / NSTAGE) & 1, p.wait_limit))) {
       failed = true;
       kfail = k;
       break;
@@ -289,13 +290,13 @@ cudaError_t launch_tc_t(const Params &p, const CUtensorMap &km, const CUtensorMa
   constexpr size_t stage_bytes = size_t(kWarps) * NSTAGE * 2 * (D / 64) * kHalfBytes;
   const size_t merge = (size_t(kWarps) * G * D + 2 * kWarps * G) * sizeof(float);
   const size_t smem = 1024 + std::max(stage_bytes + kWarps * NSTAGE * sizeof(uint64_t), merge);
-  static bool attr_done[64] = {false};
+  static std::atomic<bool> attr_done[64];  // zero-initialised (static storage)
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+  if (dev >= 0 && dev < 64 && !attr_done[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
-    attr_done[dev] = true;
+    attr_done[dev].store(true, std::memory_order_release);  // setting twice is harmless
   }
   dim3 grid(num_rows, p.num_kv_heads, p.max_parts);
   kern<<<grid, kWarps * 32, smem, stream>>>(km, vm, p);

@@ -133,6 +133,9 @@ struct Engine {
   std::vector<cudaEvent_t> prof_ev;  // pairs: start, end
   size_t prof_used = 0;              // events in use (2 per bracketed launch)
   double prof_bytes = 0.0;
+  // debugging: >= 0 ends the layer loop after that layer's MLP down
+  // projection (no lm_head, no sampling), so the activation buffers hold it
+  int debug_stop_layer = -1;
   // tensor parallelism: pairs around each all-reduce + residual add + RMSNorm
   // (the fused kernel, or NCCL all-reduce + K4)
   std::vector<cudaEvent_t> prof_ar_ev;

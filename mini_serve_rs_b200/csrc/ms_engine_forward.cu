@@ -217,6 +217,7 @@ int enqueue_forward(Engine *eng, const StepPlan &plan) {
       continue;
     }
     MS_BLAS_TRY(linear(eng, w.w_down, eng->act, eng->x_tmp, eng->H, T, eng->I));
+    if (l == eng->debug_stop_layer) break;
     MS_CUDA_TRY(prof_ar_mark(eng));
     if (eng->tp > 1 && nccl_allreduce_sum(eng->x_tmp, size_t(T) * eng->H, dt, eng->comm, st) != 0)
       return eng->fail(MS_E_DEVICE, "NCCL all-reduce after down_proj failed");
@@ -229,6 +230,13 @@ int enqueue_forward(Engine *eng, const StepPlan &plan) {
                                      eng->last_norm, S, eng->H, eps, dt, st));
     }
     MS_CUDA_TRY(prof_ar_mark(eng));
+  }
+  if (eng->debug_stop_layer >= 0 && eng->debug_stop_layer < eng->L && !eng->ar_fused) {
+    // debugging stop: no lm_head or sampling; the step still returns (stale) tokens and the status
+    eng->last_launches = 0;
+    MS_CUDA_TRY(cudaMemcpyAsync(eng->h_next, eng->d_next, size_t(S) * 4, cudaMemcpyDeviceToHost, st));
+    MS_CUDA_TRY(cudaMemcpyAsync(eng->h_status, eng->d_status, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+    return MS_OK;
   }
   // lm_head in f32 output, greedy argmax, tokens back to the host
   MS_BLAS_TRY(linear(eng, eng->lm_head, eng->last_norm, eng->logits, eng->V, S, eng->H, true));

@@ -214,7 +214,8 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
   // Eligible: one token per sequence (so the decode rows are the packed rows
   // and there are no prefill tiles), at most S block-table deltas, no
   // collectives, no per-launch profiling events.
-  const bool graph_ok = eng->graphs_enabled && eng->tp == 1 && !eng->profiling && T == S && nd <= S &&
+  const bool graph_ok = eng->graphs_enabled && eng->tp == 1 && !eng->profiling && eng->debug_stop_layer < 0 &&
+                        T == S && nd <= S &&
                         (!sp.split || (sp.n_dec == S && sp.n_tiles == 0));
   Engine::StepGraph *g = nullptr;
   bool capture = false;

@@ -46,6 +46,9 @@ struct AttnArgs {
 bool encode_pool_tensor_map(void *map_out, const void *pool, int dtype, int head_dim, int64_t pool_tiles);
 
 cudaError_t launch_paged_attention(const AttnArgs &a, cudaStream_t stream);
+// The current device's status word for kernels launched without an engine
+// (see ms_kernel_status); looked up on every call.
+cudaError_t standalone_status_word(unsigned **out);
 
 // K3p: ragged causal prefill over the paged pool (16-bit, tensor cores).
 // tiles [num_tiles][4] = (first packed row, rows, position of the first row,

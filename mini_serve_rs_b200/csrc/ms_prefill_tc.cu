@@ -12,6 +12,7 @@
 // skipped by that warp.  Stale keys past the sequence's length in its last
 // page are masked in S and their V fragments zeroed in registers.
 #include <algorithm>
+#include <atomic>
 #include <array>
 #include <vector>
 #include <mutex>
@@ -254,13 +255,13 @@ cudaError_t launch_prefill_t(const PrefillParams &p, const CUtensorMap &km, cons
   constexpr int NSTAGE = 3;
   auto kern = paged_prefill_tc_kernel<T, D, G, NSTAGE>;
   const size_t smem = 1024 + size_t(NSTAGE) * 2 * (D / 64) * kHalfBytes + NSTAGE * sizeof(uint64_t);
-  static bool attr_done[64] = {false};
+  static std::atomic<bool> attr_done[64];  // zero-initialised (static storage)
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+  if (dev >= 0 && dev < 64 && !attr_done[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
-    attr_done[dev] = true;
+    attr_done[dev].store(true, std::memory_order_release);  // setting twice is harmless
   }
   dim3 grid(num_tiles, p.num_kv_heads);
   kern<<<grid, kWarps * 32, smem, stream>>>(km, vm, p);
@@ -281,7 +282,6 @@ cudaError_t prefill_group(const PrefillParams &p, const CUtensorMap &km, const C
 }
 
 }  // namespace
-__device__ unsigned g_prefill_status;
 // tcgen05 build (ms_prefill_tc5.cu)
 bool prefill_tc5_enabled();
 int prefill_tc5_tokens_per_tile(int group);
@@ -306,10 +306,8 @@ cudaError_t launch_paged_prefill(const PrefillArgs &a, cudaStream_t stream) {
   if (!attn::attention_tc_supported(a.dtype, a.head_dim, group)) return cudaErrorInvalidValue;
   unsigned *status = a.status;
   if (!status) {
-    void *sp = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&sp, attn::g_prefill_status);
+    cudaError_t e = standalone_status_word(&status);
     if (e != cudaSuccess) return e;
-    status = static_cast<unsigned *>(sp);
   }
   if (attn::prefill_tc5_enabled())
     return attn::launch_prefill_tc5(a.q, a.out, a.block_tables, a.max_blocks_per_seq, a.tiles, a.num_tiles,

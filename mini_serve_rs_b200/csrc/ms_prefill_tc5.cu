@@ -44,6 +44,7 @@
 // on expiry the CTA records kStatusWaitTimeout, drains its MMAs and copies
 // (bounded), frees TMEM and returns.
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 #include <mutex>
 #include <type_traits>
@@ -689,13 +690,13 @@ template <typename T, int D, int G>
 cudaError_t launch_t5(const Prefill5Params &p, int num_tiles, cudaStream_t stream) {
   auto kern = paged_prefill_tc5_kernel<T, D, G>;
   const size_t smem = Ring5<D>::kSmem;
-  static bool attr_done[64] = {false};
+  static std::atomic<bool> attr_done[64];  // zero-initialised (static storage)
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+  if (dev >= 0 && dev < 64 && !attr_done[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
     if (e != cudaSuccess) return e;
-    attr_done[dev] = true;
+    attr_done[dev].store(true, std::memory_order_release);  // setting twice is harmless
   }
   if (num_tiles > 65535) return cudaErrorInvalidValue;
   dim3 grid(p.num_kv_heads, num_tiles);
@@ -1152,13 +1153,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads6, 1)
 template <typename T, int G>
 cudaError_t launch_pair(const Prefill5Params &p, int num_tiles, cudaStream_t stream) {
   auto kern = paged_prefill_pair_kernel<T, G>;
-  static bool attr_done[64] = {false};
+  static std::atomic<bool> attr_done[64];  // zero-initialised (static storage)
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+  if (dev >= 0 && dev < 64 && !attr_done[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem6);
     if (e != cudaSuccess) return e;
-    attr_done[dev] = true;
+    attr_done[dev].store(true, std::memory_order_release);  // setting twice is harmless
   }
   if (num_tiles > 65535) return cudaErrorInvalidValue;
   dim3 grid(2 * p.num_kv_heads, num_tiles);  // x: (kv head, half) pairs = the clusters' two CTAs

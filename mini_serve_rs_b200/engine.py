@@ -86,6 +86,7 @@ _SIGS = {
     "ms_debug_logits": ([_P, C.POINTER(C.c_float), C.c_int64], C.c_int),
     "ms_debug_pool_ptr": ([_P, _I32, _I32, C.POINTER(_P)], C.c_int),
     "ms_debug_buffer": ([_P, C.c_char_p, _P, C.c_int64], C.c_int),
+    "ms_debug_stop_after_layer": ([_P, _I32], C.c_int),
     "ms_launch_pack": ([_P, _P, _P, _I32, _P, _P, _P, _I32, _P, _I32, _I32, _P, _P, _P, _P, _P, _P], C.c_int),
     "ms_launch_add_rmsnorm": ([_P, _P, _P, _P, _P, _P, _I32, _I32, C.c_float, _I32, _P], C.c_int),
     "ms_launch_qk_norm_rope_append": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I32,
@@ -99,6 +100,8 @@ _SIGS = {
     "ms_launch_silu_mul": ([_P, _P, _I32, _I32, _I32, _P], C.c_int),
     "ms_launch_argmax": ([_P, _I32, _I32, _P, _P], C.c_int),
     "ms_launch_sample": ([_P, _I32, _I32, _P, _P, _P, _P, _P], C.c_int),
+    "ms_kernel_status": ([_I32, C.POINTER(C.c_uint32)], C.c_int),
+    "ms_test_set_attention_wait_limit": ([_I32], C.c_int),
     "ms_pages_create": ([C.c_int64, _I32, _I32, C.POINTER(_P)], C.c_int),
     "ms_pages_destroy": ([_P], C.c_int),
     "ms_pages_admit": ([_P, C.c_uint64, _P, _I32, _P, _I32, C.POINTER(_I32), C.POINTER(_I32)], C.c_int),
@@ -411,6 +414,10 @@ class Engine:
                     f"buffer {name}")
         return out
 
+    def stop_after_layer(self, layer: int):
+        """Later steps end after `layer`'s MLP (-1: off); see ms_debug_stop_after_layer."""
+        self._check(self.lib.ms_debug_stop_after_layer(self.h, layer), "stop_after_layer")
+
     def pool_ptr(self, layer: int, which: int) -> int:
         p = C.c_void_p()
         self._check(self.lib.ms_debug_pool_ptr(self.h, layer, which, C.byref(p)), "pool_ptr")
@@ -511,6 +518,16 @@ def chunk_hashes(tokens, chunk_size: int = 16):
     if n < 0:
         raise ValueError("ms_prefix_chunk_hashes")
     return [bytes(out[32 * i:32 * i + 32]).hex() for i in range(n)]
+
+
+def kernel_status(device: int = 0) -> int:
+    """Status bits of kernels launched without an engine on `device` since the
+    last call (ms_kernel_status); clears them."""
+    v = C.c_uint32()
+    rc = lib().ms_kernel_status(device, C.byref(v))
+    if rc != MS_OK:
+        raise error_for(rc, "ms_kernel_status")
+    return v.value
 
 
 def nccl_unique_id() -> bytes:

@@ -258,6 +258,11 @@ class QwenRef:
         self.w = {k: v.to(dtype) for k, v in weights.items()}
         self.cos, self.sin = rope_tables(cfg, dtype, max_pos=min(cfg.max_position_embeddings, 65536))
         self.lm_head = self.w.get("lm_head.weight", self.w["model.embed_tokens.weight"])
+        # per-layer activations, filled by forward() when set to a dict:
+        # ("attn", l) attention output before o_proj, ("x_norm", l) the
+        # post-attention RMSNorm, ("x_resid", l) the residual after attention,
+        # "last_norm" the final norm of the last position
+        self.capture: Optional[Dict] = None
 
     # ---- one decoder layer, q_len tokens of a single request (qwen2.rs:279-347, 414-428)
     def _attn(self, l: int, xs: torch.Tensor, state: SeqState, offset: int) -> torch.Tensor:
@@ -293,6 +298,8 @@ class QwenRef:
             mask[:, offset:] = torch.where(i < j, torch.tensor(float("-inf")), torch.tensor(0.0)).to(att.dtype)
             att = softmax_last(att + mask)
             out = torch.matmul(att, vr).transpose(0, 1).reshape(t, hq * d)
+        if self.capture is not None:
+            self.capture[("attn", l)] = out
         return linear(out, w[p + "o_proj.weight"])
 
     def _mlp(self, l: int, xs: torch.Tensor) -> torch.Tensor:
@@ -313,6 +320,9 @@ class QwenRef:
         xs = h + residual
         residual = xs
         h = rms_norm(xs, w[p + "post_attention_layernorm.weight"], eps)
+        if self.capture is not None:
+            self.capture[("x_resid", l)] = xs
+            self.capture[("x_norm", l)] = h
         h = self._mlp(l, h)
         return residual + h
 
@@ -323,6 +333,8 @@ class QwenRef:
         for l in range(self.cfg.num_hidden_layers):
             xs = self._layer(l, xs, state, offset)
         xs = rms_norm(xs, self.w["model.norm.weight"], self.cfg.rms_norm_eps)
+        if self.capture is not None:
+            self.capture["last_norm"] = xs[-1]
         return linear(xs[-1:], self.lm_head)[0].to(torch.float32)
 
     def step_decode_batch(self, states: List[SeqState], ids: Sequence[int],
