@@ -26,8 +26,9 @@ thread of the engine's process (BackgroundHttp) or in a process of its own
 process's interpreter: one pipe message per engine step carries every new
 token, and the reference's single tokio process has no such contention.
 
-Client: CompletionStream restates the reference's incremental SSE parser
-(src/sse.rs:1-131); stream_completion measures one request as
+Client: CompletionStream checks a streamed completion against the rules the
+reference's client parser enforces (listed below, src/sse.rs); stream_completion
+measures one request as
 examples/bench.rs:61-110 does (TTFT = first token event, decode rate over
 the events after it), and run_trace replays a trace with real arrival times.
 """
@@ -49,119 +50,167 @@ MAX_EVENT_BYTES = 1024 * 1024
 
 
 # ---------------------------------------------------------------------------------------
-# client-side SSE parsing (src/sse.rs)
+# client-side parsing of a streamed completion
+#
+# What the trace client accepts, as rules (the reference's client, src/sse.rs,
+# enforces the same ones):
+#   framing   - text/event-stream: lines end in LF or CR LF; the values of the
+#               "data" fields of an event (one leading space dropped) are joined
+#               by LF; a blank line ends the event; comments and other fields
+#               are ignored; a line is decoded as UTF-8 once it is complete;
+#               an event may hold at most 1 MiB of line bytes;
+#   payloads  - every event but the closing "[DONE]" is a JSON object; one
+#               with an "error" member fails the stream;
+#   tokens    - a chunk has exactly one choice with a string "text"; without a
+#               finish_reason it is one generated-token event;
+#   finish    - a non-empty string finish_reason ends the generation: after it
+#               only a usage-only chunk (empty choices) or "[DONE]" may come;
+#   usage     - usage.completion_tokens, when present, is a non-negative
+#               integer that never changes and is the authoritative count;
+#               it may not be smaller than the token events seen;
+#   close     - "[DONE]" needs a finish_reason before it and ends the stream:
+#               nothing may follow, and a stream that never got it, or ends
+#               inside an event, is incomplete.
+MAX_EVENT_BYTES = 1024 * 1024
+
+
 class SseError(ValueError):
-    pass
+    """The stream breaks one of the rules above (`rule` names it)."""
+
+    def __init__(self, rule: str, detail: str):
+        super().__init__(f"{rule}: {detail}")
+        self.rule = rule
+
+
+class EventFramer:
+    """Bytes in, complete event payloads out (the framing rule)."""
+
+    def __init__(self, limit: int = MAX_EVENT_BYTES):
+        self.limit = limit
+        self.partial = bytearray()   # the current line, not yet terminated
+        self.fields: List[str] = []  # data values of the event being built
+        self.size = 0                # line bytes of the event being built
+
+    def idle(self) -> bool:
+        """No line or event is half received."""
+        return not self.partial and not self.fields
+
+    def feed(self, chunk: bytes) -> List[str]:
+        events: List[str] = []
+        *complete, tail = bytes(chunk).split(b"\n")
+        for seg in complete:
+            self._grow(len(seg))
+            self.partial += seg
+            line, self.partial = bytes(self.partial), bytearray()
+            if line.endswith(b"\r"):
+                line = line[:-1]
+            try:
+                text = line.decode("utf-8")
+            except UnicodeDecodeError:
+                raise SseError("framing", "a line is not valid UTF-8") from None
+            if text == "":
+                if self.fields:  # trailing empty data lines add nothing
+                    events.append("\n".join(self.fields).rstrip("\n"))
+                self.fields, self.size = [], 0
+                continue
+            name, _, value = text.partition(":")
+            if name == "data" and ":" in text:
+                self.fields.append(value[1:] if value.startswith(" ") else value)
+        self._grow(len(tail))
+        self.partial += tail
+        return events
+
+    def _grow(self, n: int):
+        self.size += n
+        if self.size > self.limit:
+            raise SseError("framing", f"an event is longer than {self.limit} bytes")
 
 
 class CompletionStream:
-    """Incremental completion SSE parser with the reference's rules:
-    complete byte lines are decoded as UTF-8, events are bounded to 1 MiB,
-    a chunk with a finish_reason is not a token event, [DONE] needs a finish
-    reason first, nothing may follow [DONE], an "error" payload fails the
-    stream, and the server's usage.completion_tokens is authoritative."""
+    """A streamed /v1/completions response, checked against the rules above
+    while it arrives.  push() takes bytes as they come (any split); finish()
+    returns the completion-token count of a complete stream.  After any broken
+    rule the stream stays failed."""
+
+    GENERATING, FINISHED, CLOSED, BROKEN = "generating", "finished", "closed", "broken"
 
     def __init__(self):
-        self._line = bytearray()
-        self._data: List[str] = []
-        self._event_bytes = 0
+        self.framer = EventFramer()
+        self.phase = self.GENERATING
         self.text = ""
         self.token_events = 0
         self.completion_tokens: Optional[int] = None
         self.finish_reason: Optional[str] = None
-        self._done = False
-        self._failed = False
 
     def push(self, data: bytes):
-        if self._failed:
-            raise SseError("SSE parser already failed")
+        if self.phase == self.BROKEN:
+            raise SseError("state", "the stream already failed")
         try:
-            self._push(data)
+            for payload in self.framer.feed(data):
+                self._take(payload)
         except SseError:
-            self._failed = True
+            self.phase = self.BROKEN
             raise
 
-    def _push(self, data: bytes):
-        pos, n = 0, len(data)
-        while pos < n:
-            nl = data.find(b"\n", pos)
-            end = n if nl < 0 else nl
-            self._event_bytes += end - pos  # line bytes count toward the event bound, newlines do not
-            if self._event_bytes > MAX_EVENT_BYTES:
-                raise SseError("SSE event exceeds 1 MiB")
-            self._line += data[pos:end]
-            if nl < 0:
-                return
-            pos = nl + 1
-            if self._line and self._line[-1] == 0x0D:
-                self._line.pop()
-            try:
-                line = bytes(self._line).decode("utf-8")
-            except UnicodeDecodeError:
-                raise SseError("Invalid SSE UTF-8") from None
-            self._line.clear()
-            if not line:
-                if self._data:
-                    payload = "".join(self._data)
-                    self._data = []
-                    self._event(payload.rstrip("\n"))
-                self._event_bytes = 0
-            elif line.startswith("data:"):
-                v = line[5:]
-                self._data.append((v[1:] if v.startswith(" ") else v) + "\n")
-            # comments and other fields carry no completion semantics
+    def finish(self) -> int:
+        if self.phase != self.CLOSED or not self.framer.idle():
+            raise SseError("close", f"the stream is incomplete (phase {self.phase})")
+        if self.completion_tokens is None:
+            return self.token_events
+        if self.completion_tokens < self.token_events:
+            raise SseError("usage", "usage counts fewer tokens than the stream carried")
+        return self.completion_tokens
 
-    def _event(self, data: str):
-        if self._done:
-            raise SseError("SSE data after [DONE]")
-        if data == "[DONE]":
-            if self.finish_reason is None:
-                raise SseError("SSE [DONE] without finish reason")
-            self._done = True
+    # -- one event payload
+    def _take(self, payload: str):
+        if self.phase == self.CLOSED:
+            raise SseError("close", "an event arrived after [DONE]")
+        if payload == "[DONE]":
+            if self.phase != self.FINISHED:
+                raise SseError("close", "[DONE] before any finish_reason")
+            self.phase = self.CLOSED
             return
         try:
-            value = json.loads(data)
+            chunk = json.loads(payload)
         except json.JSONDecodeError as e:
-            raise SseError(f"Invalid SSE JSON: {e}") from None
-        if not isinstance(value, dict):
-            raise SseError("Invalid SSE JSON object")
-        if value.get("error") is not None:
-            raise SseError("Server returned an SSE error")
-        usage = value.get("usage")
-        if usage is not None:
-            n = usage.get("completion_tokens") if isinstance(usage, dict) else None
-            if not isinstance(n, int) or isinstance(n, bool) or n < 0:
-                raise SseError("Invalid completion token usage")
-            if self.completion_tokens is not None and self.completion_tokens != n:
-                raise SseError("Conflicting SSE token usage")
-            self.completion_tokens = n
-        choices = value.get("choices")
+            raise SseError("payloads", f"not JSON ({e})") from None
+        if not isinstance(chunk, dict):
+            raise SseError("payloads", "not a JSON object")
+        if "error" in chunk:
+            raise SseError("payloads", "the server sent an error")
+        self._usage(chunk.get("usage"))
+        choices = chunk.get("choices")
         if not isinstance(choices, list):
-            raise SseError("Missing SSE choices")
-        if not choices and self.finish_reason is not None and self.completion_tokens is not None:
+            raise SseError("tokens", "no choices list")
+        if self.phase == self.FINISHED:
+            # after the finish only a usage-only chunk is allowed
+            if choices or self.completion_tokens is None:
+                raise SseError("finish", "a chunk with choices after the finish_reason")
             return
-        if len(choices) != 1 or self.finish_reason is not None:
-            raise SseError("Unexpected SSE choices or repeated finish")
-        choice = choices[0]
-        text = choice.get("text") if isinstance(choice, dict) else None
+        if len(choices) != 1 or not isinstance(choices[0], dict):
+            raise SseError("tokens", f"{len(choices)} choices in one chunk")
+        text = choices[0].get("text")
         if not isinstance(text, str):
-            raise SseError("Missing completion text")
-        reason = choice.get("finish_reason")
+            raise SseError("tokens", "a choice without text")
+        reason = choices[0].get("finish_reason")
         if isinstance(reason, str):
-            if not reason:
-                raise SseError("Empty SSE finish reason")
+            if reason == "":
+                raise SseError("finish", "an empty finish_reason")
             self.finish_reason = reason
+            self.phase = self.FINISHED
         else:
             self.token_events += 1
         self.text += text
 
-    def finish(self) -> int:
-        if self._failed or not self._done or self._line or self._data:
-            raise SseError("Failed or incomplete SSE stream")
-        count = self.completion_tokens if self.completion_tokens is not None else self.token_events
-        if count < self.token_events:
-            raise SseError("Usage is smaller than generated token events")
-        return count
+    def _usage(self, usage):
+        if usage is None:
+            return
+        n = usage.get("completion_tokens") if isinstance(usage, dict) else None
+        if isinstance(n, bool) or not isinstance(n, int) or n < 0:
+            raise SseError("usage", "completion_tokens is not a non-negative integer")
+        if self.completion_tokens is not None and n != self.completion_tokens:
+            raise SseError("usage", "completion_tokens changed within the stream")
+        self.completion_tokens = n
 
 
 # ---------------------------------------------------------------------------------------
@@ -718,9 +767,9 @@ async def stream_completion(session, url: str, model: str, prompt, max_tokens: i
             "model": model, "prompt": prompt, "max_tokens": max_tokens, "temperature": temperature,
             "top_p": top_p, "stream": True}) as resp:
         if resp.status >= 400:
-            raise SseError(f"HTTP {resp.status}: {await resp.text()}")
+            raise SseError("http", f"HTTP {resp.status}: {await resp.text()}")
         if not resp.headers.get("Content-Type", "").startswith("text/event-stream"):
-            raise SseError("Expected text/event-stream")
+            raise SseError("http", "the response is not text/event-stream")
         parser = CompletionStream()
         first = last = None
         async for data in resp.content.iter_any():
@@ -734,7 +783,7 @@ async def stream_completion(session, url: str, model: str, prompt, max_tokens: i
     tokens = parser.finish()
     elapsed = time.perf_counter() - started
     if first is None:
-        raise SseError("No generated-token event in completed stream")
+        raise SseError("tokens", "the completed stream carried no generated token")
     decode = last - first
     return StreamResult(tokens, first * 1000.0, elapsed * 1000.0, tokens / elapsed,
                         (tokens - 1) / decode if tokens > 1 and decode > 0 else None,

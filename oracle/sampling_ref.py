@@ -120,3 +120,36 @@ def sample_like_kernel(logits, temperature: float, top_p: float | None, seed: in
     race = (z - np.log(E).astype(np.float32)).astype(np.float32)
     score = np.where(keep, race, np.float32(-np.inf))
     return int(np.argmax(score))  # first index among equal maxima
+
+
+def explains_mismatch(logits, temperature: float, top_p: float | None, seed: int, got: int,
+                      ulps: float = 16.0) -> bool:
+    """True when a kernel draw `got` that differs from sample_like_kernel can
+    only come from the last-bit differences between the device's expf / logf
+    and numpy's exp / log (the restatement cannot reproduce those bits):
+
+    * both tokens are in the restated nucleus and their race scores are within
+      `ulps` f32 ulps of each other (a near tie of the race), or
+    * `got` sits at the edge of the restated nucleus: the fixed-point mass
+      ranked up to it is within 1e-5 of ceil(top_p * W), so a weight a few
+      ulps off moves the edge."""
+    want = sample_like_kernel(logits, temperature, top_p, seed)
+    if want is None or got == want or not (0 <= got < len(logits)):
+        return got == want
+    z = scaled(logits, temperature)
+    u = splitmix64_uniform(seed, np.arange(len(z)))
+    race = (z - np.log((-np.log(u)).astype(np.float32)).astype(np.float32)).astype(np.float32)
+    keep = kept_mask(logits, temperature, top_p)
+    tol = ulps * float(np.spacing(np.float32(max(abs(race[got]), abs(race[want])))))
+    if keep[got] and abs(float(race[got]) - float(race[want])) <= tol:
+        return True
+    if _nucleus(top_p):
+        e, w = kernel_weights(logits, temperature)
+        W = float(w.sum(dtype=np.uint64))
+        target = np.ceil(_f32(top_p) * W)
+        order = np.lexsort((np.arange(len(e)), -e.astype(np.float64)))
+        cum = np.cumsum(w[order], dtype=np.uint64).astype(np.float64)
+        rank = int(np.nonzero(order == got)[0][0])
+        before = cum[rank - 1] if rank > 0 else 0.0
+        return min(abs(before - target), abs(cum[rank] - target)) <= 1e-5 * W
+    return False

@@ -19,7 +19,7 @@ from scipy.stats import chi2
 
 from mini_serve_rs_b200 import engine as E
 from oracle.qwen_ref import random_weights
-from oracle.sampling_ref import candle_probs, sample_like_kernel
+from oracle.sampling_ref import explains_mismatch, candle_probs, sample_like_kernel
 from tests.golden.golden_cases import MODEL_CASES
 from tests.gpu_util import need_gpu
 
@@ -58,8 +58,12 @@ def test_kernel_draws_equal_restatement():
         if want is None:
             assert out[r] == -7, r
             agree += 1
+        elif out[r] == want:
+            agree += 1
         else:
-            agree += int(out[r] == want)
+            # the device's expf/logf differ from numpy's in the last bits; a row may
+            # differ only where that decides it (a race near-tie or the nucleus edge)
+            assert explains_mismatch(x[r], temps[r], float(tops[r]), int(seeds[r]), int(out[r])), r
     assert agree >= rows - 1, (agree, rows)
 
 
@@ -72,7 +76,12 @@ def test_kernel_small_top_p_takes_the_radix_path_and_still_agrees():
     x = (rng.standard_normal((rows, V)) * 0.1).astype(np.float32)
     seeds = rng.integers(0, 2 ** 63, rows, dtype=np.uint64)
     out = _launch(x, np.ones(rows, np.float32), np.full(rows, 0.05, np.float32), seeds, np.zeros(rows, np.int32))
-    agree = sum(int(out[r] == sample_like_kernel(x[r], 1.0, 0.05, int(seeds[r]))) for r in range(rows))
+    agree = 0
+    for r in range(rows):
+        if out[r] == sample_like_kernel(x[r], 1.0, 0.05, int(seeds[r])):
+            agree += 1
+        else:  # only where the device's expf/logf last bits decide it
+            assert explains_mismatch(x[r], 1.0, 0.05, int(seeds[r]), int(out[r])), r
     assert agree >= rows - 1, agree
 
 

@@ -1,8 +1,9 @@
-"""The trace client's SSE parser (http_driver.CompletionStream) against the
-rules of the reference's parser, src/sse.rs, and its tests (:119-173):
-arbitrary byte boundaries keep UTF-8 text, token events and usage; truncated
-or invalid streams never succeed; the finish chunk is not a token event and
-usage is authoritative."""
+"""The trace client's completion-stream checker (http_driver.CompletionStream)
+against the acceptance rules listed in http_driver.py, which are the rules the
+reference's client parser enforces, on the vectors of its tests
+(src/sse.rs:119-173): arbitrary byte boundaries keep UTF-8 text, token events
+and usage; truncated or invalid streams never succeed; the finish chunk is
+not a token event and usage is authoritative."""
 import json
 
 import pytest
@@ -68,3 +69,40 @@ def test_terminal_chunk_is_not_a_token_and_usage_is_authoritative():
            b"data: [DONE]\n\n")
     assert p.token_events == 1
     assert p.finish() == 2
+
+
+def test_each_rule_is_enforced():
+    def stream(*events):
+        return b"".join(b"data: " + e + b"\n\n" for e in events)
+
+    tok = b'{"choices":[{"text":"a","finish_reason":null}]}'
+    fin = b'{"choices":[{"text":"","finish_reason":"length"}]}'
+    usage_only = b'{"choices":[],"usage":{"completion_tokens":1}}'
+    ok = CompletionStream()
+    ok.push(stream(tok, fin, usage_only, b"[DONE]"))
+    assert ok.finish() == 1 and ok.finish_reason == "length"
+    bad = {
+        "payloads": [stream(b'{"error":null}'), stream(b"[1, 2]")],
+        "tokens": [stream(b'{"choices":[{"text":"a"},{"text":"b"}]}'), stream(b'{"choices":[{"text":5}]}')],
+        "finish": [stream(tok, fin, tok), stream(tok, b'{"choices":[{"text":"","finish_reason":""}]}'),
+                   stream(tok, fin, b'{"choices":[]}')],
+        "usage": [stream(b'{"choices":[{"text":"a"}],"usage":{"completion_tokens":-1}}'),
+                  stream(b'{"choices":[{"text":"a"}],"usage":{"completion_tokens":true}}'),
+                  stream(b'{"choices":[{"text":"a"}],"usage":{"completion_tokens":1}}',
+                         b'{"choices":[{"text":"b"}],"usage":{"completion_tokens":2}}')],
+        "close": [stream(tok, b"[DONE]"), stream(tok, fin, b"[DONE]", tok)],
+        "framing": [b"data: \xff\n\n"],
+    }
+    for rule, cases in bad.items():
+        for data in cases:
+            p = CompletionStream()
+            with pytest.raises(SseError) as e:
+                p.push(data)
+            assert e.value.rule == rule, (rule, data, e.value)
+            with pytest.raises(SseError):
+                p.push(b"")  # a failed stream stays failed
+    p = CompletionStream()
+    p.push(stream(b'{"choices":[{"text":"a"}],"usage":{"completion_tokens":0}}', fin, b"[DONE]"))
+    with pytest.raises(SseError) as e:
+        p.finish()  # usage below the token events
+    assert e.value.rule == "usage"
