@@ -355,17 +355,19 @@ int ms_launch_pack(const int32_t *seq_row, const int32_t *seq_ntok, const int32_
                    int32_t *row_ctx, void *stream);
 
 /* K4: fused residual add + RMSNorm (qwen2.rs:68-75 with the adds of
- * qwen2.rs:420-427).  resid_out = x + r (r may be NULL: plain copy),
- * norm_out = (resid_out / sqrt(mean(resid_out^2) + eps)).to(dtype) * w.
- * row_index (may be NULL) gathers input rows; outputs are compact. */
+ * qwen2.rs:420-427).  With s = x + r in f32 (r may be NULL: s = x):
+ * resid_out = s and norm_out = s / sqrt(mean(s^2) + eps) * w, each computed
+ * in f32 and rounded once to the dtype.  row_index (may be NULL) gathers
+ * input rows; outputs are compact.  resid_out may be NULL. */
 int ms_launch_add_rmsnorm(const void *x, const void *r, const int32_t *row_index,
                           const void *w, void *resid_out, void *norm_out, int32_t rows,
                           int32_t hidden, float eps, int32_t dtype, void *stream);
 
 /* K5 + K2: per-head q/k RMSNorm (optional), rotate-half RoPE at positions[t]
- * with the cos/sin tables, q written to q_out [T, Hq, D]; k and v written
- * into the paged pools at slot_mapping[t] (qwen2.rs:287-313).  qkv is
- * [T, (Hq + 2 Hkv) * D]; bias (may be NULL) is added first. */
+ * with the cos/sin tables (f32 [max_pos, D/2] for every dtype), q written to
+ * q_out [T, Hq, D]; k and v written into the paged pools at slot_mapping[t]
+ * (qwen2.rs:287-313).  qkv is [T, (Hq + 2 Hkv) * D]; bias (may be NULL) is
+ * added first.  Arithmetic is f32; each output is rounded once. */
 int ms_launch_qk_norm_rope_append(const void *qkv, const void *bias, const void *q_norm_w,
                                   const void *k_norm_w, const void *cos_table,
                                   const void *sin_table, const int32_t *positions,
@@ -419,10 +421,11 @@ int ms_prefill_tiles(const int32_t *seq_row0, const int32_t *seq_ntok, const int
  * writing its output, 2 = an index out of range) and clears them.  No
  * counterpart in the reference, whose kernels do not wait on barriers. */
 int ms_kernel_status(int32_t device, uint32_t *status_out);
-/* Test hook: polls > 0 limits every page-loop wait of the decode-attention
- * kernels launched afterwards to that many polls (0 restores the default of
- * 4M polls), so a test can make a wait run out while every copy it started
- * still lands (the drain after a failed wait keeps the default limit). */
+/* Test hook: polls >= 0 limits every page-loop wait of the decode-attention
+ * kernels launched afterwards to that many polls -- 0 makes the first wait
+ * give up at once -- and polls < 0 restores the default of 4M polls.  A test
+ * can so make a wait run out while every copy the kernel started still lands
+ * (the drain after a failed wait keeps the default limit). */
 int ms_test_set_attention_wait_limit(int32_t polls);
 
 /* K6b on-device sampling over f32 logits [rows, vocab]: for each row with

@@ -354,8 +354,8 @@ cudaError_t dispatch_dim(const Params &p, int head_dim, int group, int num_rows,
 // kernels OR their kStatus* bits into it; ms_kernel_status reads and clears it.
 __device__ unsigned g_status_scratch;
 
-// Test hook: > 0 replaces the poll limit of the page-loop waits (ms_test_set_attention_wait_limit).
-std::atomic<int> g_test_wait_limit{0};
+// Test hook: >= 0 replaces the poll limit of the page-loop waits (ms_test_set_attention_wait_limit).
+std::atomic<int> g_test_wait_limit{-1};
 
 }  // namespace attn
 
@@ -414,7 +414,7 @@ cudaError_t launch_paged_attention(const AttnArgs &a, cudaStream_t stream) {
   if (p.max_parts > 65535) return cudaErrorInvalidValue;
   p.qscale = a.scale * attn::kLog2e;
   const int test_limit = attn::g_test_wait_limit.load(std::memory_order_relaxed);
-  p.wait_limit = test_limit > 0 ? test_limit : attn::kWaitLimit;
+  p.wait_limit = test_limit >= 0 ? test_limit : attn::kWaitLimit;
   p.status = a.status;
   if (p.status == nullptr) {
     cudaError_t e = standalone_status_word(&p.status);
@@ -581,7 +581,6 @@ extern "C" int ms_kernel_status(int32_t device, uint32_t *out) {
 }
 
 extern "C" int ms_test_set_attention_wait_limit(int32_t polls) {
-  if (polls < 0) return MS_E_INVALID;
-  ms::attn::g_test_wait_limit.store(polls, std::memory_order_relaxed);
+  ms::attn::g_test_wait_limit.store(polls < 0 ? -1 : polls, std::memory_order_relaxed);
   return MS_OK;
 }

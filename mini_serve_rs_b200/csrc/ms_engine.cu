@@ -36,15 +36,6 @@ static size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
 static size_t dtype_size(int dt) { return dt == MS_DTYPE_F32 ? 4 : 2; }
 
-// f32 -> bf16 / f16 on the host (round to nearest even), for the RoPE tables.
-static uint16_t f32_to_bf16(float f) {
-  uint32_t u;
-  std::memcpy(&u, &f, 4);
-  if ((u & 0x7fffffffu) > 0x7f800000u) return uint16_t((u >> 16) | 0x40);  // NaN
-  u += 0x7fffu + ((u >> 16) & 1u);
-  return uint16_t(u >> 16);
-}
-
 // ---------------------------------------------------------------------------
 // creation
 
@@ -158,7 +149,7 @@ int create_impl(const ms_model_cfg *cfg, const ms_engine_opts *opts, Engine *eng
   }
 
   // ---- RoPE tables (qwen2.rs:91-108): inv_freq = 1f32 / theta.powf(i/dim) as f32,
-  // freqs = t * inv_freq in f32, sin/cos in f32, cast to the model dtype ----
+  // freqs = t * inv_freq in f32, sin/cos in f32 (kept in f32 for every model dtype) ----
   eng->rope_len = cfg->max_position_embeddings;
   if (eng->rope_len <= 0) return eng->fail(MS_E_INVALID, "max_position_embeddings must be positive");
   {
@@ -174,17 +165,11 @@ int create_impl(const ms_model_cfg *cfg, const ms_engine_opts *opts, Engine *eng
         c[size_t(t) * half + i] = std::cos(f);
         s[size_t(t) * half + i] = std::sin(f);
       }
-    MS_CUDA_TRY(cudaMalloc(&eng->cos_t, n * es));
-    MS_CUDA_TRY(cudaMalloc(&eng->sin_t, n * es));
-    if (eng->dtype == MS_DTYPE_F32) {
-      MS_CUDA_TRY(cudaMemcpy(eng->cos_t, c.data(), n * 4, cudaMemcpyHostToDevice));
-      MS_CUDA_TRY(cudaMemcpy(eng->sin_t, s.data(), n * 4, cudaMemcpyHostToDevice));
-    } else {
-      std::vector<uint16_t> cb(n), sb(n);
-      for (size_t i = 0; i < n; ++i) { cb[i] = f32_to_bf16(c[i]); sb[i] = f32_to_bf16(s[i]); }
-      MS_CUDA_TRY(cudaMemcpy(eng->cos_t, cb.data(), n * 2, cudaMemcpyHostToDevice));
-      MS_CUDA_TRY(cudaMemcpy(eng->sin_t, sb.data(), n * 2, cudaMemcpyHostToDevice));
-    }
+    // f32 tables in every mode (K5 computes in f32 and rounds each output once)
+    MS_CUDA_TRY(cudaMalloc(&eng->cos_t, n * 4));
+    MS_CUDA_TRY(cudaMalloc(&eng->sin_t, n * 4));
+    MS_CUDA_TRY(cudaMemcpy(eng->cos_t, c.data(), n * 4, cudaMemcpyHostToDevice));
+    MS_CUDA_TRY(cudaMemcpy(eng->sin_t, s.data(), n * 4, cudaMemcpyHostToDevice));
   }
 
   // ---- paged KV pool ----

@@ -181,9 +181,6 @@ int enqueue_forward(Engine *eng, const StepPlan &plan) {
       pf.scale = 1.0f / std::sqrt(float(eng->D));
       pf.dtype = dt;
       pf.status = eng->d_status;
-      pf.k_map = &eng->kmaps[l];
-      pf.v_map = &eng->vmaps[l];
-      pf.pool_tiles = pool_tiles;
       MS_CUDA_TRY(launch_paged_prefill(pf, st));
     }
     // o_proj, residual add + post-attention norm

@@ -69,9 +69,6 @@ struct PrefillArgs {
   float scale;
   int dtype;
   unsigned *status = nullptr;
-  const void *k_map = nullptr;
-  const void *v_map = nullptr;
-  int64_t pool_tiles = 0;
 };
 cudaError_t launch_paged_prefill(const PrefillArgs &a, cudaStream_t stream);
 // true when the 16-bit tensor-core decode / prefill kernels serve this shape

@@ -2,10 +2,13 @@
 //
 // K4 restates RmsNorm::forward (src/backends/qwen2.rs:68-75) fused with the
 // residual adds of DecoderLayer::forward (qwen2.rs:420-427) and of the batched
-// decode (qwen2.rs:751-756): the sum is rounded to the model dtype, the
-// variance is taken in f32 from the rounded sum, the row is divided by
-// sqrt(var + eps), rounded, then multiplied by the weight and rounded again.
-// One CTA per row, 16-byte vector loads, warp-shuffle + shared-memory reduce.
+// decode (qwen2.rs:751-756).  All arithmetic is f32 and every stored value is
+// rounded once: the residual output is the rounded sum, and the norm is taken
+// from the unrounded f32 sum, y = round(s * (1 / sqrt(mean(s^2) + eps)) * w),
+// so a 16-bit output is within half a unit in its last place of the f32
+// reference's value computed from the same inputs.  In f32 mode the division
+// is the reference's x / norm.  One CTA (or one warp) per row, 16-byte
+// vector loads, warp-shuffle (+ shared-memory) reduce.
 #include <type_traits>
 
 #include "ms_common.cuh"
@@ -53,6 +56,15 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
   return t;
 }
 
+// x / norm * w with one rounding at the store: f32 keeps the reference's
+// division; 16-bit outputs multiply by the row's reciprocal norm (its error is
+// far below the output's rounding).
+template <typename T>
+__device__ __forceinline__ float norm_weight(float x, float norm, float rn, float w) {
+  if constexpr (std::is_same<T, float>::value) return (x / norm) * w;
+  return x * rn * w;
+}
+
 template <typename T>
 __global__ void add_rmsnorm_kernel(const T *__restrict__ x, const T *__restrict__ r,
                                    const int32_t *__restrict__ row_index, const T *__restrict__ w,
@@ -72,19 +84,20 @@ __global__ void add_rmsnorm_kernel(const T *__restrict__ x, const T *__restrict_
       float rr[N];
       V16<T>::load(r + src * hidden + c * N, rr);
 #pragma unroll
-      for (int i = 0; i < N; ++i) s[i] = round_to<T>(s[i] + rr[i]);
+      for (int i = 0; i < N; ++i) s[i] += rr[i];
     }
-    if (resid_out) V16<T>::store(resid_out + size_t(row) * hidden + c * N, s);
+    if (resid_out) V16<T>::store(resid_out + size_t(row) * hidden + c * N, s);  // rounds once
 #pragma unroll
     for (int i = 0; i < N; ++i) sq = fmaf(s[i], s[i], sq);
   }
   const float total = block_sum(sq, red);
   const float norm = sqrtf(total / float(hidden) + eps);
+  const float rn = 1.0f / norm;
   if (active) {
     float ww[N], y[N];
     V16<T>::load(w + c * N, ww);
 #pragma unroll
-    for (int i = 0; i < N; ++i) y[i] = round_to<T>(round_to<T>(s[i] / norm) * ww[i]);
+    for (int i = 0; i < N; ++i) y[i] = norm_weight<T>(s[i], norm, rn, ww[i]);
     V16<T>::store(norm_out + size_t(row) * hidden + c * N, y);
   }
 }
@@ -94,8 +107,7 @@ __global__ void add_rmsnorm_kernel(const T *__restrict__ x, const T *__restrict_
 // a warp issues every load of its row at once (x, r: CPL 16-byte chunks per
 // lane), reduces with shuffles only, and a CTA of 4 warps covers 4 rows, so a
 // config-3 batch (8192 rows of 1024) fits one wave of resident warps.  The
-// rounded sums stay packed in registers.  Same rounding points as
-// add_rmsnorm_kernel.
+// f32 sums stay in registers between the reduction and the output.
 template <typename T, int CPL>
 __global__ void __launch_bounds__(128) add_rmsnorm_warp_kernel(const T *__restrict__ x, const T *__restrict__ r,
                                                                const int32_t *__restrict__ row_index,
@@ -120,36 +132,24 @@ __global__ void __launch_bounds__(128) add_rmsnorm_warp_kernel(const T *__restri
       if (rr) rv[k] = __ldg(rr + c);
     }
   }
-  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+  float f[CPL][N];  // the f32 sums
   float sq = 0.f;
 #pragma unroll
   for (int k = 0; k < CPL; ++k) {
     const int c = lane + 32 * k;
     if (c < chunks) {
-      if constexpr (kBf16) {  // packed adds, exact f32 squares in element order
-        if (rr)
+      R::unpack(sv[k], f[k]);
+      if (rr) {
+        float b[N];
+        R::unpack(rv[k], b);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) u4_set(sv[k], j, bf2_add(u4_get(sv[k], j), u4_get(rv[k], j)));
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t v = u4_get(sv[k], j);
-          sq = fmaf(bf_lo(v), bf_lo(v), sq);
-          sq = fmaf(bf_hi(v), bf_hi(v), sq);
-        }
-      } else {
-        float s[N];
-        R::unpack(sv[k], s);
-        if (rr) {
-          float b[N];
-          R::unpack(rv[k], b);
-#pragma unroll
-          for (int i = 0; i < N; ++i) s[i] = round_to<T>(s[i] + b[i]);
-          sv[k] = R::pack(s);
-        }
-#pragma unroll
-        for (int i = 0; i < N; ++i) sq = fmaf(s[i], s[i], sq);
+        for (int i = 0; i < N; ++i) f[k][i] += b[i];
+        if (resid_out) reinterpret_cast<uint4 *>(resid_out + size_t(row) * hidden)[c] = R::pack(f[k]);
+      } else if (resid_out) {
+        reinterpret_cast<uint4 *>(resid_out + size_t(row) * hidden)[c] = sv[k];
       }
-      if (resid_out) reinterpret_cast<uint4 *>(resid_out + size_t(row) * hidden)[c] = sv[k];
+#pragma unroll
+      for (int i = 0; i < N; ++i) sq = fmaf(f[k][i], f[k][i], sq);
     }
   }
   sq = warp_sum(sq);
@@ -161,23 +161,11 @@ __global__ void __launch_bounds__(128) add_rmsnorm_warp_kernel(const T *__restri
   for (int k = 0; k < CPL; ++k) {
     const int c = lane + 32 * k;
     if (c < chunks) {
-      const uint4 wv = __ldg(wr + c);
-      if constexpr (kBf16) {
-        uint4 y;
+      float ww[N], y[N];
+      R::unpack(__ldg(wr + c), ww);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t v = u4_get(sv[k], j);
-          u4_set(y, j, bf2_mul(bf2_pack(div_by(bf_lo(v), norm, rn), div_by(bf_hi(v), norm, rn)), u4_get(wv, j)));
-        }
-        out[c] = y;
-      } else {
-        float s[N], ww[N], y[N];
-        R::unpack(sv[k], s);
-        R::unpack(wv, ww);
-#pragma unroll
-        for (int i = 0; i < N; ++i) y[i] = round_to<T>(round_to<T>(s[i] / norm) * ww[i]);
-        out[c] = R::pack(y);
-      }
+      for (int i = 0; i < N; ++i) y[i] = norm_weight<T>(f[k][i], norm, rn, ww[i]);
+      out[c] = R::pack(y);
     }
   }
 }
@@ -199,7 +187,8 @@ cudaError_t launch_add_rmsnorm_warp(const void *x, const void *r, const int32_t 
   return go(add_rmsnorm_warp_kernel<T, 8>);
 }
 
-// act = silu(gate).to(dtype) * up, gate_up = [gate | up] per row (qwen2.rs:169-174).
+// act = silu(gate) * up (qwen2.rs:169-174) in f32, rounded once; gate_up =
+// [gate | up] per row.
 template <typename T>
 __global__ void silu_mul_kernel(const T *__restrict__ gu, T *__restrict__ out, int rows, int inter) {
   constexpr int N = V16<T>::N;
@@ -213,10 +202,7 @@ __global__ void silu_mul_kernel(const T *__restrict__ gu, T *__restrict__ out, i
     V16<T>::load(gu + row * 2 * inter + c * N, g);
     V16<T>::load(gu + row * 2 * inter + inter + c * N, u);
 #pragma unroll
-    for (int k = 0; k < N; ++k) {
-      const float a = round_to<T>(g[k] / (1.0f + expf(-g[k])));
-      y[k] = round_to<T>(a * u[k]);
-    }
+    for (int k = 0; k < N; ++k) y[k] = g[k] / (1.0f + expf(-g[k])) * u[k];  // one rounding, at the store
     V16<T>::store(out + row * inter + c * N, y);
   }
 }

@@ -716,490 +716,7 @@ cudaError_t t5_group(const Prefill5Params &p, int group, int num_tiles, cudaStre
   }
 }
 
-// ======================================================================================
-// Opt-in (MS_PREFILL_PAIR=1) build for D = 128 on SM pairs: the CTAs of a 2-CTA cluster hold the two query halves of a tile and
-// run one M = 256 MMA per K step (tcgen05.mma.cta_group::2).  Operand A (Q, or P from TMEM)
-// is split by rows: each CTA holds its own 128.  Operand B is split by N: for S = Q K^T rank r
-// holds keys [64 r, 64 r + 64) of the 128-key group, all dims; for O += P V rank r holds
-// dims [64 r, 64 r + 64) of V, all 128 keys.  Each CTA gets its rows of the accumulators in
-// its own TMEM, so S is double-buffered at N = 128 (S0, S1, O = 384 columns) and the
-// softmax of group g+1 need not wait for PV(g).  One thread of rank 0 issues every MMA (a
-// quarter of the instructions of the single-SM build per unit of work) and commits to both
-// CTAs' barriers at once (multicast).  Rank 1's copies and both halves' P reach rank 0 by
-// remote mbarrier arrives.
-// Tile i of the ring order K0 K1 V0 K2 V1 ... K(n-1) V(n-2) V(n-1), the order the MMA
-// thread consumes them (S(g+1) before PV(g)); returns the group, sets is_v.
-__device__ __forceinline__ int ring_tile(int i, int n, bool &is_v) {
-  if (i == 0) { is_v = false; return 0; }
-  if (i == 2 * n - 1) { is_v = true; return n - 1; }
-  if (i & 1) { is_v = false; return (i + 1) >> 1; }
-  is_v = true;
-  return (i - 2) >> 1;
-}
-
-constexpr int kThreads6 = 192;        // 4 softmax warps, the MMA (rank 0) / relay (rank 1) warp, the copy warp
-constexpr int kKeys6 = 128;           // keys per group
-constexpr int kSlots6 = 8;            // ring slots of 16 KiB
-constexpr int kHalf6 = 64 * 128;      // 64 rows x 128 B
-constexpr int kTile6 = 2 * kHalf6;    // K half-tile: 64 keys x 128 dims; V half-tile: 128 keys x 64 dims
-constexpr int kSmem6 = 1024 + 2 * kRows * 128 + kSlots6 * kTile6;
-
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// shared::cluster address of `local` (a shared::cta address) in CTA `rank` of the cluster
-__device__ __forceinline__ uint32_t mapa_rank(uint32_t local, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait_cl(uint64_t *bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded cluster-scope wait that gives up early once this CTA's abort flag is set.
-__device__ __forceinline__ bool wait_cl(uint64_t *bar, uint32_t parity, volatile int *abort) {
-  for (int i = 0; i < kWaitLimit; ++i) {
-    if (mbar_try_wait_cl(bar, parity)) return true;
-    if ((i & 63) == 63 && *abort) return false;
-  }
-  return false;
-}
-__device__ __forceinline__ void umma2(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
-}
-__device__ __forceinline__ void umma2_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate));
-}
-// arrive on `bar` in both CTAs of the pair once every MMA issued so far by this thread completed
-__device__ __forceinline__ void umma2_commit_both(uint64_t *bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
-          smem_addr(bar)),
-      "h"((unsigned short)3)
-      : "memory");
-}
-
-template <typename T, int G>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads6, 1)
-    paged_prefill_pair_kernel(Prefill5Params p) {
-  constexpr int D = 128;
-  constexpr int RPT = RowsPerTok5<G>::value;
-  constexpr int TPH = kRows / RPT;     // tokens per query half
-  constexpr int QHALF = kRows * 128;   // one 64-dim half of this CTA's Q rows
-  constexpr int NSLOT = kSlots6, TILE = kTile6, HALF = kHalf6;
-  constexpr int TMEM_COLS = 512;       // S0 [0, 128), S1 [128, 256) (P over their first 64), O [256, 384)
-
-  extern __shared__ unsigned char smem_dyn[];
-  unsigned char *smem =
-      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-  unsigned char *sq = smem;  // this CTA's Q rows: two 64-dim halves of 128 rows x 128 B
-  unsigned char *ring = smem + 2 * QHALF;
-  // same offsets in both CTAs (the pair MMA reads each operand at one shared address in each CTA)
-  __shared__ uint64_t full[NSLOT], empty[NSLOT], peer_full[NSLOT], s_full[2], p_ready[2], pv_done, drain;
-  __shared__ uint32_t tmem_base;
-  __shared__ volatile int abort_s;
-  __shared__ int landed_s, issued_s;
-
-  const uint32_t rank = cluster_ctarank();  // the query half this CTA holds
-  const int kvh = blockIdx.x >> 1, tile = blockIdx.y;
-  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const int row0 = p.tiles[tile * 4 + 0], nrows = p.tiles[tile * 4 + 1];
-  const int pos0 = p.tiles[tile * 4 + 2], trow = p.tiles[tile * 4 + 3];
-  const int32_t *table = p.block_tables + size_t(trow) * p.max_blocks_per_seq;
-  const int kv_len = pos0 + nrows;
-  const int npages = (kv_len + kBS - 1) / kBS;
-  const int ngroups = (kv_len + kKeys6 - 1) / kKeys6;
-  const int ntiles = 2 * ngroups;  // ring order K0 K1 V0 K2 V1 ... (ring_tile)
-
-  if (t == 0) {
-    for (int i = 0; i < NSLOT; ++i) {
-      mbar_init(&full[i], 32);  // this CTA's copy lanes
-      mbar_init(&empty[i], 1);  // the pair's MMA commit
-      mbar_init(&peer_full[i], 1);  // (rank 0) rank 1's relay
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&p_ready[b], 8);  // (rank 0) 4 softmax warps of each CTA
-    }
-    mbar_init(&pv_done, 1);
-    mbar_init(&drain, 1);
-    abort_s = 0;
-    landed_s = 0;
-    issued_s = 0;
-    fence_barrier_init();
-  }
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
-                 "r"(TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::);
-  }
-  // softmax thread t (< 128): row t of this half, TMEM lane t
-  const int rt = t & (kRows - 1);
-  const int tok = int(rank) * TPH + rt / RPT, head = rt % RPT;
-  const bool rvalid = warp < 4 && head < G && tok < nrows;
-  const bool half_live = nrows > int(rank) * TPH;  // rank 1's half may be empty
-  if (warp < 4) {
-    const T *qr = static_cast<const T *>(p.q) +
-                  ((size_t(row0) + (rvalid ? tok : 0)) * p.num_kv_heads * G + size_t(kvh) * G + (rvalid ? head : 0)) * D;
-#pragma unroll
-    for (int dh = 0; dh < 2; ++dh)
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 v = rvalid ? reinterpret_cast<const uint4 *>(qr + dh * 64)[c] : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4 *>(sq + dh * QHALF + rt * 128 + ((c ^ (rt & 7)) << 4)) = v;
-      }
-  }
-  fence_proxy_async();
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync_all();  // both CTAs' barriers are initialised and TMEM allocated
-  tc_fence_after();
-  const uint32_t tmem = tmem_base;
-  const uint32_t p_ready0 = mapa_rank(smem_addr(&p_ready[0]), 0);  // rank 0's barriers
-  const uint32_t peer_full0 = mapa_rank(smem_addr(&peer_full[0]), 0);
-
-  float l_run = 0.f;
-  if (warp < 4) {
-    // ---- softmax: row rt of half `rank` ----
-    const uint32_t lane_off = uint32_t(warp * 32) << 16;
-    const uint32_t tm_o = tmem + 2 * kKeys6;
-    const int pos_first = pos0 + int(rank) * TPH;
-    const int pos = rvalid ? pos0 + tok : pos_first;  // padding rows copy the half's first row mask
-    const float c = p.qscale;
-    float m_run = -INFINITY;
-    for (int g = 0; g < ngroups; ++g) {
-      const uint32_t tm_s = tmem + (g & 1) * kKeys6;
-      if (!__all_sync(kFull, wait_cl(&s_full[g & 1], (g >> 1) & 1, &abort_s))) {
-        abort_s = 1;
-        break;
-      }
-      tc_fence_after();
-      const int key0 = g * kKeys6;
-      if (half_live) {
-        float sv[kKeys6];
-        {
-          uint32_t(&sr)[4][32] = *reinterpret_cast<uint32_t(*)[4][32]>(sv);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) tmem_ld32_async(tm_s + lane_off + 32 * k, sr[k]);
-          tmem_wait_ld();
-        }
-        if (key0 + kKeys6 - 1 > pos_first) {  // causal mask only where the group reaches past the half's start
-#pragma unroll
-          for (int i = 0; i < kKeys6; ++i) sv[i] = key0 + i <= pos ? sv[i] : -INFINITY;
-        }
-        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int i = 0; i < kKeys6 / 2; ++i) mx[i & 3] = max3f(mx[i & 3], sv[2 * i], sv[2 * i + 1]);
-        const float mts = fmaxf(max3f(mx[0], mx[1], mx[2]), mx[3]) * c;
-        const bool grow = mts > m_run + kRescale;  // m_run = -inf: any finite max
-        float alpha = 1.f;
-        if (grow) {
-          alpha = ex2_approx(m_run - mts);
-          m_run = mts;
-        }
-        if (g > 0 && __any_sync(kFull, grow)) {
-          // O is being accumulated by PV(g - 1): wait for it, then rescale this warp's rows
-          if (!__all_sync(kFull, wait_cl(&pv_done, (g - 1) & 1, &abort_s))) {
-            abort_s = 1;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int c0 = 0; c0 < D; c0 += 32) {
-            float o[32];
-            tmem_ld32(tm_o + lane_off + c0, o);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(tm_o + lane_off + c0, o);
-          }
-        }
-        const float negm = -m_run;
-        float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {  // P: 64 columns of value pairs, stored 32 at a time
-          uint32_t pk[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float x0, x1, a, b;
-            ffma2(x0, x1, sv[64 * h2 + 2 * i], sv[64 * h2 + 2 * i + 1], c, negm);
-            if ((i & 7) < kExp2OnFma) {
-              exp2_poly2(a, b, x0, x1);
-            } else {
-              a = ex2_approx(x0);
-              b = ex2_approx(x1);
-            }
-            fadd2(ps[2 * (i & 3)], ps[2 * (i & 3) + 1], a, b);
-            pk[i] = pack_pair<T>(a, b);
-          }
-          tmem_st32u(tm_s + lane_off + 32 * h2, pk);
-        }
-        l_run = l_run * alpha + (((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7])));
-      }
-      // this CTA's V rows past the sequence in the last group (stale, or pages never loaded) -> 0;
-      // both CTAs hold V (by dims), so both zero theirs
-      const int vk = kv_len - key0;
-      if (g == ngroups - 1 && vk < kKeys6) {
-        const int iv = ntiles - 1;
-        if (!__all_sync(kFull, wait_or_abort(&full[iv % NSLOT], (iv / NSLOT) & 1, &abort_s))) {
-          abort_s = 1;
-          break;
-        }
-        unsigned char *vst = ring + (iv % NSLOT) * TILE;
-        for (int i = rt; i < (kKeys6 - vk) * 8; i += kRows)
-          *reinterpret_cast<uint4 *>(vst + (vk + i / 8) * 128 + (i % 8) * 16) = make_uint4(0, 0, 0, 0);
-        fence_proxy_async();
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        if (rank == 0) mbar_arrive(&p_ready[g & 1]);  // own barrier: CTA-scope release suffices
-        else mbar_arrive_remote(p_ready0 + 8 * (g & 1));
-      }
-    }
-  } else if (warp == 4) {
-    if (lane == 0 && rank == 0) {
-      // ---- MMA issue for the pair, in ring order: S(g) on K(g), PV(g) on V(g) ----
-      const uint32_t id_s = umma_idesc<T>(256, kKeys6, 0), id_o = umma_idesc<T>(256, D, 1);
-      const uint64_t dq = umma_desc_sw128(smem_addr(sq), 16, 1024);      // Q, K-major
-      const uint64_t dk = umma_desc_sw128(smem_addr(ring), 16, 1024);    // K half-tiles, K-major
-      const uint64_t dv = umma_desc_sw128(smem_addr(ring), HALF, 1024);  // V half-tiles, MN-major
-      int landed = 0;
-      for (int i = 0; i < ntiles; ++i) {
-        bool is_v;
-        const int grp = ring_tile(i, ngroups, is_v);
-        const int slot = i % NSLOT;
-        const uint32_t ph = (i / NSLOT) & 1;
-        if (is_v && !wait_cl(&p_ready[grp & 1], (grp >> 1) & 1, &abort_s)) {
-          abort_s = 1;
-          break;
-        }
-        if (!wait_or_abort(&full[slot], ph, &abort_s) || !wait_cl(&peer_full[slot], ph, &abort_s)) {
-          abort_s = 1;
-          break;
-        }
-        landed = i + 1;
-        fence_proxy_async();  // the copies were generic-proxy writes
-        tc_fence_after();
-        const uint64_t soff = uint64_t((slot * TILE) >> 4);
-        if (!is_v) {
-          const uint32_t d = tmem + (grp & 1) * kKeys6;
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t offq = ((kk >> 2) * QHALF + (kk & 3) * 32) >> 4;
-            const uint32_t offk = ((kk >> 2) * HALF + (kk & 3) * 32) >> 4;
-            umma2(d, dq + offq, dk + soff + offk, id_s, kk > 0);
-          }
-          umma2_commit_both(&s_full[grp & 1]);
-        } else {
-          const uint32_t a = tmem + (grp & 1) * kKeys6;
-          const uint32_t acc0 = grp > 0 ? 1u : 0u;
-#pragma unroll
-          for (int kk = 0; kk < kKeys6 / 16; ++kk)
-            umma2_ts(tmem + 2 * kKeys6, a + kk * 8, dv + soff + uint64_t((kk * 2048) >> 4), id_o, kk > 0 ? 1u : acc0);
-          umma2_commit_both(&pv_done);
-        }
-        umma2_commit_both(&empty[slot]);
-      }
-      landed_s = landed;
-    } else if (lane == 0) {
-      // ---- relay (rank 1): each of this CTA's landed tiles -> rank 0's peer_full ----
-      int relayed = 0;
-      for (int i = 0; i < ntiles; ++i) {
-        if (!wait_or_abort(&full[i % NSLOT], (i / NSLOT) & 1, &abort_s)) {
-          abort_s = 1;
-          break;
-        }
-        relayed = i + 1;
-        fence_proxy_async();
-        mbar_arrive_remote(peer_full0 + 8 * (i % NSLOT));
-      }
-      landed_s = relayed;
-    }
-  } else {
-    // ---- copies: this CTA's half of every K and V tile, ring order, 16 bytes per lane ----
-    // K(g): keys [128 g + 64 rank, +64), all 128 dims (pages 8 g + 4 rank + j, j < 4);
-    // V(g): all 128 keys (pages 8 g + j, j < 8), dims [64 rank, +64).  Page ids of the
-    // current 32-page window of each stream sit one per lane, the next window prefetched.
-    auto table_at = [&](int i) { return i < npages ? table[i] : 0; };
-    int kw = 0, vw = 0;
-    int kcur = table_at(lane), vcur = kcur, knxt = table_at(32 + lane), vnxt = knxt;
-    int issued = 0;
-    for (int i = 0; i < ntiles; ++i) {
-      const int slot = i % NSLOT;
-      if (i >= NSLOT && !__all_sync(kFull, wait_cl(&empty[slot], ((i / NSLOT) - 1) & 1, &abort_s))) {
-        abort_s = 1;
-        break;
-      }
-      bool is_v;
-      const int grp = ring_tile(i, ngroups, is_v);
-      const int first = grp * (kKeys6 / kBS) + (is_v ? 0 : 4 * int(rank));
-      const int np = is_v ? 8 : 4;
-      const int n = min(np, npages - first);
-      const int w = first >> 5;
-      int &cw = is_v ? vw : kw, &cur = is_v ? vcur : kcur, &nxt = is_v ? vnxt : knxt;
-      if (w != cw) {  // groups advance one at a time, so w == cw + 1
-        cur = nxt;
-        cw = w;
-        nxt = table_at(32 * (w + 1) + lane);
-      }
-      const T *pool = static_cast<const T *>(is_v ? p.v_pool : p.k_pool);
-      unsigned char *dst = ring + slot * TILE;
-      if (!is_v) {  // 16 chunks per 256-byte row: lane -> chunk lane % 16, rows lane / 16 + 2 k
-        const int cc = lane & 15, dh = cc >> 3, ch = cc & 7, r0 = lane >> 4;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int pid = __shfl_sync(kFull, cur, (first & 31) + j);
-          if (j < n) {
-            const T *src = pool + (size_t(pid) * p.num_kv_heads + kvh) * (kBS * D) + cc * 8;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const int r = r0 + 2 * k, kr = j * kBS + r;
-              cp_async16(dst + dh * HALF + kr * 128 + ((ch ^ (kr & 7)) << 4), src + r * D);
-            }
-          }
-        }
-      } else {  // 8 chunks of this CTA's 64 dims per row: lane -> chunk lane % 8, rows lane / 8 + 4 k
-        const int ch = lane & 7, r0 = lane >> 3;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int pid = __shfl_sync(kFull, cur, (first & 31) + j);
-          if (j < n) {
-            const T *src = pool + (size_t(pid) * p.num_kv_heads + kvh) * (kBS * D) + 64 * int(rank) + ch * 8;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int r = r0 + 4 * k, kr = j * kBS + r;
-              cp_async16(dst + kr * 128 + ((ch ^ (kr & 7)) << 4), src + r * D);
-            }
-          }
-        }
-      }
-      cp_async_arrive_on(&full[slot]);
-      issued = i + 1;
-    }
-    cp_async_wait_all();
-    if (lane == 0) issued_s = issued;
-  }
-
-  // join: every role left its loop; then drain the pair's MMAs and this CTA's copies
-  __syncthreads();
-  bool ok_end = !abort_s;
-  if (warp == 4 && lane == 0) {
-    if (rank == 0) umma2_commit_both(&drain);
-    bool drained = false;  // rank 0's commit arrives in both CTAs: cluster-scope wait
-    for (int i = 0; i < kWaitLimit && !drained; ++i) drained = mbar_try_wait_cl(&drain, 0);
-    if (!drained) ok_end = false;
-  } else if (warp == 5 && lane == 0) {
-    // the copies are complete (cp.async.wait_all); their barrier arrives must land before the CTA exits
-    for (int i = landed_s; i < issued_s; ++i)
-      if (!mbar_wait_bounded(&full[i % NSLOT], (i / NSLOT) & 1)) ok_end = false;
-  }
-  tc_fence_before();
-  const bool all_ok = __syncthreads_and(ok_end);
-  tc_fence_after();
-  if (all_ok) {
-    if (warp < 4 && half_live) {
-      const uint32_t lane_off = uint32_t(warp * 32) << 16;
-      const uint32_t tm_o = tmem + 2 * kKeys6;
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      T *orow = static_cast<T *>(p.out) +
-                ((size_t(row0) + (rvalid ? tok : 0)) * p.num_kv_heads * G + size_t(kvh) * G + (rvalid ? head : 0)) * D;
-#pragma unroll
-      for (int c0 = 0; c0 < D; c0 += 32) {
-        float o[32];
-        tmem_ld32(tm_o + lane_off + c0, o);
-        if (rvalid) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 w;
-            w.x = pack_pair<T>(o[i] * inv, o[i + 1] * inv);
-            w.y = pack_pair<T>(o[i + 2] * inv, o[i + 3] * inv);
-            w.z = pack_pair<T>(o[i + 4] * inv, o[i + 5] * inv);
-            w.w = pack_pair<T>(o[i + 6] * inv, o[i + 7] * inv);
-            *reinterpret_cast<uint4 *>(orow + c0 + i) = w;
-          }
-        }
-      }
-    }
-  } else if (t == 0) {
-    atomicOr(p.status, kStatusWaitTimeout);
-  }
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync_all();  // neither CTA frees TMEM or exits while the pair still reads its memory
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
-}
-
-template <typename T, int G>
-cudaError_t launch_pair(const Prefill5Params &p, int num_tiles, cudaStream_t stream) {
-  auto kern = paged_prefill_pair_kernel<T, G>;
-  static std::atomic<bool> attr_done[64];  // zero-initialised (static storage)
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev].load(std::memory_order_acquire)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem6);
-    if (e != cudaSuccess) return e;
-    attr_done[dev].store(true, std::memory_order_release);  // setting twice is harmless
-  }
-  if (num_tiles > 65535) return cudaErrorInvalidValue;
-  dim3 grid(2 * p.num_kv_heads, num_tiles);  // x: (kv head, half) pairs = the clusters' two CTAs
-  kern<<<grid, kThreads6, kSmem6, stream>>>(p);
-  return cudaGetLastError();
-}
-
-template <typename T>
-cudaError_t pair_group(const Prefill5Params &p, int group, int num_tiles, cudaStream_t stream) {
-  switch (group) {
-    case 1: return launch_pair<T, 1>(p, num_tiles, stream);
-    case 2: return launch_pair<T, 2>(p, num_tiles, stream);
-    case 4: return launch_pair<T, 4>(p, num_tiles, stream);
-    case 7: return launch_pair<T, 7>(p, num_tiles, stream);
-    case 8: return launch_pair<T, 8>(p, num_tiles, stream);
-    default: return cudaErrorInvalidValue;
-  }
-}
-
 }  // namespace
-
-// Whether the tcgen05 build runs prefill tiles (MS_PREFILL_TC5=0 selects the
-// mma.sync build); the tile size (tokens per tile) depends on it.
-bool prefill_tc5_enabled() {
-  static const bool on = [] {
-    const char *e = std::getenv("MS_PREFILL_TC5");
-    return !(e && e[0] == '0');
-  }();
-  return on;
-}
-
-// MS_PREFILL_PAIR=1 runs D = 128 tiles on SM pairs (paged_prefill_pair_kernel): correct, but
-// slower than the single-SM kernel on the measured workloads.
-static bool prefill_pair_enabled() {
-  static const bool on = [] {
-    const char *e = std::getenv("MS_PREFILL_PAIR");
-    return e && e[0] == '1';
-  }();
-  return on;
-}
 
 int prefill_tc5_tokens_per_tile(int group) {
   const int rpt = group <= 1 ? 1 : group <= 2 ? 2 : group <= 4 ? 4 : 8;
@@ -1223,11 +740,9 @@ cudaError_t launch_prefill_tc5(const void *q, void *out, const int32_t *block_ta
   p.num_kv_heads = num_kv_heads;
   p.qscale = scale * kLog2e;
   if (dtype == MS_DTYPE_BF16) {
-    if (head_dim == 128 && prefill_pair_enabled()) return pair_group<__nv_bfloat16>(p, group, num_tiles, stream);
     if (head_dim == 128) return t5_group<__nv_bfloat16, 128>(p, group, num_tiles, stream);
     if (head_dim == 64) return t5_group<__nv_bfloat16, 64>(p, group, num_tiles, stream);
   } else if (dtype == MS_DTYPE_F16) {
-    if (head_dim == 128 && prefill_pair_enabled()) return pair_group<__half>(p, group, num_tiles, stream);
     if (head_dim == 128) return t5_group<__half, 128>(p, group, num_tiles, stream);
     if (head_dim == 64) return t5_group<__half, 64>(p, group, num_tiles, stream);
   }

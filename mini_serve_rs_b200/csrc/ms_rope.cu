@@ -4,11 +4,14 @@
 // (src/backends/qwen2.rs:287-313): projections arrive as one fused
 // [T, (Hq + 2 Hkv) * D] GEMM output; bias (qwen2.rs:234-248) and QK-norm
 // (qwen2.rs:297-304, the RmsNorm of :68-75 over head_dim) are applied before
-// RoPE (apply_rope, :132-142, with cos/sin tables of :91-108 stored in the
-// model dtype); the rotated K and the V rows are written straight into their
-// paged-pool slot (the append of :349-361, now into 16-token pages addressed
-// by slot_mapping), the rotated q into a dense [T, Hq, D] buffer for K3.
-// Every product and sum is rounded to the model dtype where Candle rounds.
+// RoPE (apply_rope, :132-142, with the cos/sin tables of :91-108, kept in f32
+// for every model dtype); the rotated K and the V rows are written straight
+// into their paged-pool slot (the append of :349-361, now into 16-token pages
+// addressed by slot_mapping), the rotated q into a dense [T, Hq, D] buffer
+// for K3.  All arithmetic is f32 and each stored value is rounded once, so a
+// 16-bit output is within half a unit in its last place of the f32
+// reference's value from the same inputs (f32 mode divides by the norm as the
+// reference does; 16-bit outputs multiply by its reciprocal).
 //
 // Two builds: qk_norm_rope_append_vec_kernel (16-byte aligned operands, the
 // engine's case) moves 16-byte vectors, several per thread; the general
@@ -23,10 +26,17 @@
 namespace ms {
 namespace {
 
+// x / norm * w: the reference's division in f32 mode, the reciprocal for 16-bit outputs.
+template <typename T>
+__device__ __forceinline__ float qk_scale(float x, float norm, float rn, float w) {
+  if constexpr (std::is_same<T, float>::value) return (x / norm) * w;
+  return x * rn * w;
+}
+
 template <typename T, int D>
 __global__ void qk_norm_rope_append_kernel(const T *__restrict__ qkv, const T *__restrict__ bias,
                                            const T *__restrict__ qn, const T *__restrict__ kn,
-                                           const T *__restrict__ cos_t, const T *__restrict__ sin_t,
+                                           const float *__restrict__ cos_t, const float *__restrict__ sin_t,
                                            const int32_t *__restrict__ positions,
                                            const int64_t *__restrict__ slot_mapping, T *__restrict__ q_out,
                                            T *__restrict__ k_pool, T *__restrict__ v_pool, int num_tokens,
@@ -49,7 +59,7 @@ __global__ void qk_norm_rope_append_kernel(const T *__restrict__ qkv, const T *_
     const T *bs = bias + size_t(h) * D + d0;
     if constexpr (DPL == 4) Vec4<T>::load(bs, b); else Vec2<T>::load(bs, b);
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) x[i] = round_to<T>(x[i] + b[i]);
+    for (int i = 0; i < DPL; ++i) x[i] += b[i];
   }
 
   if (h >= hq + hkv) {  // V head: straight into the pool
@@ -69,32 +79,31 @@ __global__ void qk_norm_rope_append_kernel(const T *__restrict__ qkv, const T *_
     for (int i = 0; i < DPL; ++i) ss = fmaf(x[i], x[i], ss);
     ss = warp_sum(ss);
     const float norm = sqrtf(ss / float(D) + eps);
+    const float rn = 1.0f / norm;
     float w[DPL];
     if constexpr (DPL == 4) Vec4<T>::load(nw + d0, w); else Vec2<T>::load(nw + d0, w);
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) x[i] = round_to<T>(round_to<T>(x[i] / norm) * w[i]);
+    for (int i = 0; i < DPL; ++i) x[i] = qk_scale<T>(x[i], norm, rn, w[i]);
   }
 
   // rotate-half RoPE
   const int pos = positions[t];
   const int j0 = d0 % HALF;
   float c[DPL], s[DPL];
-  const T *cp = cos_t + size_t(pos) * HALF + j0;
-  const T *sp = sin_t + size_t(pos) * HALF + j0;
-  if constexpr (DPL == 4) { Vec4<T>::load(cp, c); Vec4<T>::load(sp, s); }
-  else { Vec2<T>::load(cp, c); Vec2<T>::load(sp, s); }
+  const float *cp = cos_t + size_t(pos) * HALF + j0;
+  const float *sp = sin_t + size_t(pos) * HALF + j0;
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) {
+    c[i] = cp[i];
+    s[i] = sp[i];
+  }
   float partner[DPL];
 #pragma unroll
   for (int i = 0; i < DPL; ++i) partner[i] = __shfl_xor_sync(kFull, x[i], 16);
   const bool lower = lane < 16;
   float y[DPL];
 #pragma unroll
-  for (int i = 0; i < DPL; ++i) {
-    const float rot = lower ? -partner[i] : partner[i];
-    const float a = round_to<T>(x[i] * c[i]);
-    const float b = round_to<T>(rot * s[i]);
-    y[i] = round_to<T>(a + b);
-  }
+  for (int i = 0; i < DPL; ++i) y[i] = fmaf(x[i], c[i], (lower ? -partner[i] : partner[i]) * s[i]);
 
   if (is_q) {
     T *dst = q_out + (size_t(t) * hq + h) * D + d0;
@@ -111,18 +120,16 @@ __global__ void qk_norm_rope_append_kernel(const T *__restrict__ qkv, const T *_
 // Vectorised K5 (16-byte aligned operands, power-of-two page size): one CTA
 // per token.  An item is 16 bytes (N values) of one head; TPH = D / N
 // consecutive threads hold one head, so the QK-norm sum reduces over those
-// lanes and the rotate-half partner of item c is item c ^ TPH/2.  Thread i
-// takes items i, i + 256, ... (K at most) of its token: every load is issued
-// before any math, the token's position and slot are read once, and no index
-// needs a division.  Every lane runs the shuffles (V heads and the items past
-// the token's end compute and discard), so the warp never splits around them.
-// Rounding points as in qk_norm_rope_append_kernel; for bf16 each rounded add
-// and product is one packed bf16x2 instruction (equal to the f32-then-round
-// form) and x / norm uses one reciprocal per head.
+// lanes and the rotate-half partner of item c is item c ^ TPH/2 (the same
+// head, so the same norm).  Thread i takes items i, i + 256, ... (K at most)
+// of its token: every load is issued before any math, the token's position,
+// slot and table entries are read once, and no index needs a division.  Every
+// lane runs the shuffles (V heads and the items past the token's end compute
+// and discard), so the warp never splits around them.
 template <typename T, int D, int K>
 __global__ void __launch_bounds__(256) qk_norm_rope_append_vec_kernel(
     const T *__restrict__ qkv, const T *__restrict__ bias, const T *__restrict__ qn, const T *__restrict__ kn,
-    const T *__restrict__ cos_t, const T *__restrict__ sin_t, const int32_t *__restrict__ positions,
+    const float *__restrict__ cos_t, const float *__restrict__ sin_t, const int32_t *__restrict__ positions,
     const int64_t *__restrict__ slot_mapping, T *__restrict__ q_out, T *__restrict__ k_pool,
     T *__restrict__ v_pool, int hq, int hkv, int bs_shift, float eps) {
   using R = Raw16<T>;
@@ -130,7 +137,6 @@ __global__ void __launch_bounds__(256) qk_norm_rope_append_vec_kernel(
   constexpr int TPH = D / N;
   constexpr int HALF = D / 2;
   constexpr int HPP = 256 / TPH;  // heads per pass of the CTA
-  constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
   const int heads = hq + 2 * hkv;
   const int t = blockIdx.x;
   const int c = threadIdx.x % TPH;
@@ -148,9 +154,17 @@ __global__ void __launch_bounds__(256) qk_norm_rope_append_vec_kernel(
   const int64_t slot = __ldg(slot_mapping + t);
   const int64_t blk = slot >> bs_shift;
   const int off = int(slot & ((int64_t(1) << bs_shift) - 1));
-  const size_t tab = size_t(pos) * HALF + (d0 % HALF);
-  const uint4 cs = __ldg(reinterpret_cast<const uint4 *>(cos_t + tab));
-  const uint4 sn = __ldg(reinterpret_cast<const uint4 *>(sin_t + tab));
+  float cf[N], sf[N];  // this thread's N table entries (f32, 16-byte aligned)
+  {
+    const float4 *cp = reinterpret_cast<const float4 *>(cos_t + size_t(pos) * HALF + (d0 % HALF));
+    const float4 *sp = reinterpret_cast<const float4 *>(sin_t + size_t(pos) * HALF + (d0 % HALF));
+#pragma unroll
+    for (int q = 0; q < N / 4; ++q) {
+      const float4 a = __ldg(cp + q), b = __ldg(sp + q);
+      cf[4 * q] = a.x; cf[4 * q + 1] = a.y; cf[4 * q + 2] = a.z; cf[4 * q + 3] = a.w;
+      sf[4 * q] = b.x; sf[4 * q + 1] = b.y; sf[4 * q + 2] = b.z; sf[4 * q + 3] = b.w;
+    }
+  }
   const bool lower = c < TPH / 2;  // lower half rotates in -x2
 
 #pragma unroll
@@ -161,88 +175,38 @@ __global__ void __launch_bounds__(256) qk_norm_rope_append_vec_kernel(
     const bool is_v = hc >= hq + hkv;
     const bool is_q = hc < hq;
     const T *nw = is_v ? nullptr : (is_q ? qn : kn);
-    uint4 out;  // what this item stores
-    if constexpr (kBf16) {
-      uint4 x = xv[k];
-      if (bias) {
-        const uint4 b = __ldg(reinterpret_cast<const uint4 *>(bias + size_t(hc) * D + d0));
+    float x[N];
+    R::unpack(xv[k], x);
+    if (bias) {
+      float b[N];
+      R::unpack(__ldg(reinterpret_cast<const uint4 *>(bias + size_t(hc) * D + d0)), b);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) u4_set(x, j, bf2_add(u4_get(x, j), u4_get(b, j)));
-      }
-      float ss = 0.f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t v = u4_get(x, j);
-        ss = fmaf(bf_lo(v), bf_lo(v), ss);
-        ss = fmaf(bf_hi(v), bf_hi(v), ss);
-      }
-#pragma unroll
-      for (int o = TPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
-      uint4 y = x;
-      if (nw) {
-        const float norm = sqrtf(ss / float(D) + eps);
-        const float rn = 1.0f / norm;
-        const uint4 w = __ldg(reinterpret_cast<const uint4 *>(nw + d0));
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t v = u4_get(x, j);
-          u4_set(y, j, bf2_mul(bf2_pack(div_by(bf_lo(v), norm, rn), div_by(bf_hi(v), norm, rn)), u4_get(w, j)));
-        }
-      }
-      uint4 pv;
-      pv.x = __shfl_xor_sync(kFull, y.x, TPH / 2);
-      pv.y = __shfl_xor_sync(kFull, y.y, TPH / 2);
-      pv.z = __shfl_xor_sync(kFull, y.z, TPH / 2);
-      pv.w = __shfl_xor_sync(kFull, y.w, TPH / 2);
-      const uint32_t neg = lower ? 0x80008000u : 0u;
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        u4_set(out, j, bf2_add(bf2_mul(u4_get(y, j), u4_get(cs, j)), bf2_mul(u4_get(pv, j) ^ neg, u4_get(sn, j))));
-      if (is_v) out = x;
-    } else {
-      float x[N];
-      R::unpack(xv[k], x);
-      if (bias) {
-        float b[N];
-        R::unpack(__ldg(reinterpret_cast<const uint4 *>(bias + size_t(hc) * D + d0)), b);
-#pragma unroll
-        for (int i = 0; i < N; ++i) x[i] = round_to<T>(x[i] + b[i]);
-      }
-      float ss = 0.f;
-#pragma unroll
-      for (int i = 0; i < N; ++i) ss = fmaf(x[i], x[i], ss);
-#pragma unroll
-      for (int o = TPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
-      float y[N];
-      if (nw) {
-        const float norm = sqrtf(ss / float(D) + eps);
-        float w[N];
-        R::unpack(__ldg(reinterpret_cast<const uint4 *>(nw + d0)), w);
-#pragma unroll
-        for (int i = 0; i < N; ++i) y[i] = round_to<T>(round_to<T>(x[i] / norm) * w[i]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < N; ++i) y[i] = x[i];
-      }
-      const uint4 yv = R::pack(y);
-      uint4 pv;
-      pv.x = __shfl_xor_sync(kFull, yv.x, TPH / 2);
-      pv.y = __shfl_xor_sync(kFull, yv.y, TPH / 2);
-      pv.z = __shfl_xor_sync(kFull, yv.z, TPH / 2);
-      pv.w = __shfl_xor_sync(kFull, yv.w, TPH / 2);
-      float partner[N], cf[N], sf[N], o[N];
-      R::unpack(pv, partner);
-      R::unpack(cs, cf);
-      R::unpack(sn, sf);
-#pragma unroll
-      for (int i = 0; i < N; ++i) {
-        const float rot = lower ? -partner[i] : partner[i];
-        const float a = round_to<T>(y[i] * cf[i]);
-        const float b = round_to<T>(rot * sf[i]);
-        o[i] = round_to<T>(a + b);
-      }
-      out = is_v ? R::pack(x) : R::pack(o);
+      for (int i = 0; i < N; ++i) x[i] += b[i];
     }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) ss = fmaf(x[i], x[i], ss);
+#pragma unroll
+    for (int o = TPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
+    float y[N];
+    if (nw) {
+      const float norm = sqrtf(ss / float(D) + eps);
+      const float rn = 1.0f / norm;
+      float w[N];
+      R::unpack(__ldg(reinterpret_cast<const uint4 *>(nw + d0)), w);
+#pragma unroll
+      for (int i = 0; i < N; ++i) y[i] = qk_scale<T>(x[i], norm, rn, w[i]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < N; ++i) y[i] = x[i];
+    }
+    float o[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+      const float p = __shfl_xor_sync(kFull, y[i], TPH / 2);
+      o[i] = fmaf(y[i], cf[i], (lower ? -p : p) * sf[i]);
+    }
+    const uint4 out = is_v ? (bias ? R::pack(x) : xv[k]) : R::pack(o);
     if (!ok) continue;
     T *dst;
     if (is_q) dst = q_out + (size_t(t) * hq + hc) * D + d0;
@@ -258,9 +222,9 @@ cudaError_t launch_vec(const void *qkv, const void *bias, const void *qn, const 
                        void *v_pool, int T_, int hq, int hkv, int bs_shift, float eps, cudaStream_t st) {
   const int per_thread = ((hq + 2 * hkv) * (D / Raw16<T>::N) + 255) / 256;
   auto go = [&](auto kern) {
-    kern<<<T_, 256, 0, st>>>((const T *)qkv, (const T *)bias, (const T *)qn, (const T *)kn, (const T *)cs,
-                             (const T *)sn, positions, slots, (T *)q_out, (T *)k_pool, (T *)v_pool, hq, hkv, bs_shift,
-                             eps);
+    kern<<<T_, 256, 0, st>>>((const T *)qkv, (const T *)bias, (const T *)qn, (const T *)kn, (const float *)cs,
+                             (const float *)sn, positions, slots, (T *)q_out, (T *)k_pool, (T *)v_pool, hq, hkv,
+                             bs_shift, eps);
     return cudaGetLastError();
   };
   if (per_thread <= 1) return go(qk_norm_rope_append_vec_kernel<T, D, 1>);
@@ -294,12 +258,12 @@ cudaError_t launch_typed(const void *qkv, const void *bias, const void *qn, cons
   const long long blocks = (warps * 32 + threads - 1) / threads;
   if (D == 128) {
     qk_norm_rope_append_kernel<T, 128><<<blocks, threads, 0, st>>>(
-        (const T *)qkv, (const T *)bias, (const T *)qn, (const T *)kn, (const T *)cs, (const T *)sn, positions,
-        slots, (T *)q_out, (T *)k_pool, (T *)v_pool, T_, hq, hkv, bs, eps);
+        (const T *)qkv, (const T *)bias, (const T *)qn, (const T *)kn, (const float *)cs, (const float *)sn,
+        positions, slots, (T *)q_out, (T *)k_pool, (T *)v_pool, T_, hq, hkv, bs, eps);
   } else if (D == 64) {
     qk_norm_rope_append_kernel<T, 64><<<blocks, threads, 0, st>>>(
-        (const T *)qkv, (const T *)bias, (const T *)qn, (const T *)kn, (const T *)cs, (const T *)sn, positions,
-        slots, (T *)q_out, (T *)k_pool, (T *)v_pool, T_, hq, hkv, bs, eps);
+        (const T *)qkv, (const T *)bias, (const T *)qn, (const T *)kn, (const float *)cs, (const float *)sn,
+        positions, slots, (T *)q_out, (T *)k_pool, (T *)v_pool, T_, hq, hkv, bs, eps);
   } else {
     return cudaErrorInvalidValue;
   }

@@ -14,9 +14,9 @@
 //      rank's CTA b has done the same.  A rank's CTA b runs only after that
 //      rank's GEMM finished, so all partial sums are complete;
 //   2. one CTA per row: sum the row over ranks in rank order 0..tp-1 in f32
-//      (every rank computes the same bits), round to the model dtype (the
-//      all-reduce result), add the residual and round (K4's add), then
-//      RMSNorm as K4 does -- the rows read over NVLink once per rank.
+//      (every rank computes the same bits), add the residual in f32, store
+//      that sum rounded once as the new residual, and RMSNorm it from the f32
+//      sum as K4 does -- the rows read over NVLink once per rank.
 // Two partial-sum buffers alternate (o_proj, down_proj, o_proj, ...).  A
 // rank overwrites a buffer only after its next call's barrier, which every
 // rank passes only after finishing the previous call: the one that read it.
@@ -26,6 +26,7 @@
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <type_traits>
 #include <vector>
 
 #include "ms_common.cuh"
@@ -121,7 +122,7 @@ __global__ void __launch_bounds__(1024) ar_add_rmsnorm_kernel(ArArgs a) {
       R::unpack(rv, rr);
 #pragma unroll
       for (int e = 0; e < N; ++e) {
-        sf[e] = round_to<T>(round_to<T>(acc[e]) + rr[e]);
+        sf[e] = acc[e] + rr[e];  // f32; rounded once where it is stored
         sq = fmaf(sf[e], sf[e], sq);
       }
       if (a.resid_out) reinterpret_cast<uint4 *>(static_cast<T *>(a.resid_out) + size_t(i) * a.hidden)[c] = R::pack(sf);
@@ -135,10 +136,12 @@ __global__ void __launch_bounds__(1024) ar_add_rmsnorm_kernel(ArArgs a) {
     __syncthreads();  // red is reused by the next row
     if (active) {
       const float norm = sqrtf(tot / float(a.hidden) + a.eps);
+      const float rn = 1.0f / norm;
       float ww[N], y[N];
       R::unpack(reinterpret_cast<const uint4 *>(a.w)[c], ww);
 #pragma unroll
-      for (int e = 0; e < N; ++e) y[e] = round_to<T>(round_to<T>(sf[e] / norm) * ww[e]);
+      for (int e = 0; e < N; ++e)
+        y[e] = std::is_same<T, float>::value ? (sf[e] / norm) * ww[e] : sf[e] * rn * ww[e];
       reinterpret_cast<uint4 *>(static_cast<T *>(a.norm_out) + size_t(i) * a.hidden)[c] = R::pack(y);
     }
   }

@@ -78,6 +78,48 @@ def silu_mul(gate_up: torch.Tensor, inter: int) -> torch.Tensor:
     return act * u
 
 
+# ---- the kernels' 16-bit arithmetic: f32 inside, each stored value rounded once ----
+# (Candle's half-precision path rounds after every op instead; the kernels
+# keep f32 until the store, which puts them within half a unit in the last
+# place of the f32 reference's value from the same inputs.)
+
+
+def add_rmsnorm_once(x: torch.Tensor, r: Optional[torch.Tensor], w: torch.Tensor, eps: float):
+    """K4 in the inputs' dtype: (round(x + r), round((x + r) / norm * w)) with
+    the sum and the norm in f32."""
+    dt = x.dtype
+    s = x.to(torch.float32) + (0.0 if r is None else r.to(torch.float32))
+    norm = torch.sqrt((s * s).mean(dim=-1, keepdim=True) + eps)
+    return s.to(dt), (s / norm * w.to(torch.float32)).to(dt)
+
+
+def qk_norm_rope_once(qkv: torch.Tensor, positions: Sequence[int], cos32: torch.Tensor, sin32: torch.Tensor,
+                      num_heads: int, num_kv_heads: int, head_dim: int,
+                      q_norm_w: Optional[torch.Tensor], k_norm_w: Optional[torch.Tensor],
+                      bias: Optional[torch.Tensor], eps: float):
+    """K5 in qkv's dtype: bias, QK-norm and RoPE (f32 tables) in f32, q/k/v
+    rounded once."""
+    dt = qkv.dtype
+    f = lambda t: None if t is None else t.to(torch.float32)
+    q, k, v = qk_norm_rope(qkv.to(torch.float32), positions, cos32.to(torch.float32), sin32.to(torch.float32),
+                           num_heads, num_kv_heads, head_dim, f(q_norm_w), f(k_norm_w), f(bias), eps)
+    return q.to(dt), k.to(dt), v.to(dt)
+
+
+def silu_mul_once(gate_up: torch.Tensor, inter: int) -> torch.Tensor:
+    """K6 in gate_up's dtype: silu(g) * u in f32, rounded once."""
+    gf = gate_up[:, :inter].to(torch.float32)
+    uf = gate_up[:, inter:].to(torch.float32)
+    return (gf / (1.0 + torch.exp(-gf)) * uf).to(gate_up.dtype)
+
+
+def ulp16(ref: torch.Tensor, dtype) -> torch.Tensor:
+    """Spacing of `dtype` (bf16 / f16) at |ref|, per element."""
+    mant = 7 if dtype == torch.bfloat16 else 10
+    e = torch.floor(torch.log2(ref.abs().to(torch.float32).clamp(min=2.0 ** -14)))
+    return torch.pow(2.0, e - mant)
+
+
 def argmax_rows(logits: torch.Tensor) -> np.ndarray:
     """Row-wise first-index argmax (candle.rs:747-751)."""
     return torch.argmax(logits.to(torch.float32), dim=-1).to(torch.int32).numpy()

@@ -151,15 +151,3 @@ def test_prefill_4096_token_prompts_against_torch_fp32(group, head_dim, dt):
     # a chunk that starts past a page boundary: up to 257 key pages, ~36 tiles per sequence
     chunks = [(0, 4096), (513, 1536), (3001, 999), (16, 240)]
     assert _case_large(group, head_dim, dt, chunks, seed=group + head_dim) <= 2e-2
-
-
-def test_sm_pair_build_matches_too():
-    """The opt-in SM-pair build (MS_PREFILL_PAIR=1, tcgen05 cta_group::2) passes the same
-    parity cases; the switch is read once per process, so they run in a child process."""
-    import os
-    import subprocess
-    import sys
-    env = dict(os.environ, MS_PREFILL_PAIR="1")
-    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-p", "no:cacheprovider", __file__, "-k",
-                        "matches_fp32 or long_chunk or 4096"], env=env, capture_output=True, text=True, timeout=600)
-    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]

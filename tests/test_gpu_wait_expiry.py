@@ -2,10 +2,10 @@
 not hung on and not silently ignored.
 
 The kernels poll each K/V page's barrier a bounded number of times.  The test
-hook ms_test_set_attention_wait_limit(1) makes those page-loop waits give up
-after one poll, long before the page's copy lands; every copy the kernel
-started still lands, because the drain after a failed wait keeps the normal
-limit, so no access leaves its buffers and the context stays usable.
+hook ms_test_set_attention_wait_limit(0) makes those page-loop waits give up
+at once, before the page's copy has landed; every copy the kernel started
+still lands, because the drain after a failed wait keeps the normal limit, so
+no access leaves its buffers and the context stays usable.
 
 * standalone launcher: the status bit shows up in ms_kernel_status, which
   clears it; with the default limit the same launch is correct again;
@@ -31,7 +31,7 @@ WAIT_TIMEOUT_BIT = 1
 @pytest.fixture(autouse=True)
 def _restore_limit():
     yield
-    E.lib().ms_test_set_attention_wait_limit(0)
+    E.lib().ms_test_set_attention_wait_limit(-1)
 
 
 def _attention_case(seed=21, batch=64, mb=64, pool=4096):
@@ -61,12 +61,12 @@ def test_standalone_launcher_reports_a_wait_that_ran_out():
     E.kernel_status(0)
     good = _launch(*d)
     assert E.kernel_status(0) == 0
-    assert lib.ms_test_set_attention_wait_limit(1) == 0
+    assert lib.ms_test_set_attention_wait_limit(0) == 0
     _launch(*d)
     st = E.kernel_status(0)
     assert st & WAIT_TIMEOUT_BIT, st
     assert E.kernel_status(0) == 0  # read and cleared
-    assert lib.ms_test_set_attention_wait_limit(0) == 0
+    assert lib.ms_test_set_attention_wait_limit(-1) == 0
     again = _launch(*d)
     assert E.kernel_status(0) == 0
     assert torch.equal(again, good)
@@ -98,7 +98,7 @@ def test_engine_step_fails_and_quarantines_when_a_wait_runs_out():
 
     case, eng = _engine()
     ids, toks, pos = _admit_and_prefill(eng, case)
-    assert lib.ms_test_set_attention_wait_limit(1) == 0
+    assert lib.ms_test_set_attention_wait_limit(0) == 0
     with pytest.raises(E.BackendError) as ei:
         eng.step(ids, toks, pos)  # decode rows: the split-K kernel
     assert ei.value.code == E.MS_E_DEVICE
@@ -106,7 +106,7 @@ def test_engine_step_fails_and_quarantines_when_a_wait_runs_out():
     with pytest.raises(E.NoHealthyWorkers):
         eng.step(ids, toks, pos)
     eng.close()
-    assert lib.ms_test_set_attention_wait_limit(0) == 0
+    assert lib.ms_test_set_attention_wait_limit(-1) == 0
 
     # the context is still usable: a new engine computes the healthy result
     case, eng = _engine()
