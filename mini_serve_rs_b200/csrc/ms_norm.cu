@@ -9,6 +9,8 @@
 // reference's value computed from the same inputs.  In f32 mode the division
 // is the reference's x / norm.  One CTA (or one warp) per row, 16-byte
 // vector loads, warp-shuffle (+ shared-memory) reduce.
+#include <algorithm>
+#include <atomic>
 #include <type_traits>
 
 #include "ms_common.cuh"
@@ -103,11 +105,13 @@ __global__ void add_rmsnorm_kernel(const T *__restrict__ x, const T *__restrict_
 }
 
 // Warp-per-row K4 (the path for 16-byte aligned rows of up to 8 x 32 chunks,
-// i.e. hidden <= 2048 in 16-bit types; wider rows use add_rmsnorm_kernel):
-// a warp issues every load of its row at once (x, r: CPL 16-byte chunks per
-// lane), reduces with shuffles only, and a CTA of 4 warps covers 4 rows, so a
-// config-3 batch (8192 rows of 1024) fits one wave of resident warps.  The
-// f32 sums stay in registers between the reduction and the output.
+// i.e. hidden <= 2048 in 16-bit types; wider rows use add_rmsnorm_kernel): a
+// warp reduces its row with shuffles only.  The grid holds a few CTAs of 4
+// warps per SM and each warp walks rows warps-apart, loading its next row
+// (x, r: CPL 16-byte chunks per lane each) before it works on the current
+// one, so every SM keeps reads in flight while it writes: reads and writes of
+// different rows overlap instead of running as one read wave then one write
+// wave.  The f32 sums stay in registers between the reduction and the output.
 template <typename T, int CPL>
 __global__ void __launch_bounds__(128) add_rmsnorm_warp_kernel(const T *__restrict__ x, const T *__restrict__ r,
                                                                const int32_t *__restrict__ row_index,
@@ -116,57 +120,71 @@ __global__ void __launch_bounds__(128) add_rmsnorm_warp_kernel(const T *__restri
                                                                float eps) {
   using R = Raw16<T>;
   constexpr int N = R::N;
-  const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
-  if (row >= rows) return;  // warp-uniform
   const int lane = threadIdx.x & 31;
   const int chunks = hidden / N;
-  const size_t src = row_index ? size_t(row_index[row]) : size_t(row);
-  const uint4 *xr = reinterpret_cast<const uint4 *>(x + src * hidden);
-  const uint4 *rr = r ? reinterpret_cast<const uint4 *>(r + src * hidden) : nullptr;
-  uint4 sv[CPL], rv[CPL];
+  const int stride = gridDim.x * 4;
+  int row = blockIdx.x * 4 + (threadIdx.x >> 5);
+  uint4 nx[CPL], nr[CPL];  // the next row's x and r
+  auto fetch = [&](int rw) {
+    const size_t src = row_index ? size_t(__ldg(row_index + rw)) : size_t(rw);
+    const uint4 *xr = reinterpret_cast<const uint4 *>(x + src * hidden);
+    const uint4 *rr = r ? reinterpret_cast<const uint4 *>(r + src * hidden) : nullptr;
 #pragma unroll
-  for (int k = 0; k < CPL; ++k) {
-    const int c = lane + 32 * k;
-    if (c < chunks) {
-      sv[k] = __ldg(xr + c);
-      if (rr) rv[k] = __ldg(rr + c);
-    }
-  }
-  float f[CPL][N];  // the f32 sums
-  float sq = 0.f;
-#pragma unroll
-  for (int k = 0; k < CPL; ++k) {
-    const int c = lane + 32 * k;
-    if (c < chunks) {
-      R::unpack(sv[k], f[k]);
-      if (rr) {
-        float b[N];
-        R::unpack(rv[k], b);
-#pragma unroll
-        for (int i = 0; i < N; ++i) f[k][i] += b[i];
-        if (resid_out) reinterpret_cast<uint4 *>(resid_out + size_t(row) * hidden)[c] = R::pack(f[k]);
-      } else if (resid_out) {
-        reinterpret_cast<uint4 *>(resid_out + size_t(row) * hidden)[c] = sv[k];
+    for (int k = 0; k < CPL; ++k) {
+      const int c = lane + 32 * k;
+      if (c < chunks) {
+        nx[k] = __ldg(xr + c);
+        if (rr) nr[k] = __ldg(rr + c);
       }
-#pragma unroll
-      for (int i = 0; i < N; ++i) sq = fmaf(f[k][i], f[k][i], sq);
     }
-  }
-  sq = warp_sum(sq);
-  const float norm = sqrtf(sq / float(hidden) + eps);
-  const float rn = 1.0f / norm;
+  };
+  if (row < rows) fetch(row);
   const uint4 *wr = reinterpret_cast<const uint4 *>(w);
-  uint4 *out = reinterpret_cast<uint4 *>(norm_out + size_t(row) * hidden);
+  while (row < rows) {  // warp-uniform
+    uint4 sv[CPL], rv[CPL];
 #pragma unroll
-  for (int k = 0; k < CPL; ++k) {
-    const int c = lane + 32 * k;
-    if (c < chunks) {
-      float ww[N], y[N];
-      R::unpack(__ldg(wr + c), ww);
-#pragma unroll
-      for (int i = 0; i < N; ++i) y[i] = norm_weight<T>(f[k][i], norm, rn, ww[i]);
-      out[c] = R::pack(y);
+    for (int k = 0; k < CPL; ++k) {
+      sv[k] = nx[k];
+      rv[k] = nr[k];
     }
+    const int next = row + stride;
+    if (next < rows) fetch(next);
+    float f[CPL][N];  // the f32 sums
+    float sq = 0.f;
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) {
+      const int c = lane + 32 * k;
+      if (c < chunks) {
+        R::unpack(sv[k], f[k]);
+        if (r) {
+          float b[N];
+          R::unpack(rv[k], b);
+#pragma unroll
+          for (int i = 0; i < N; ++i) f[k][i] += b[i];
+          if (resid_out) reinterpret_cast<uint4 *>(resid_out + size_t(row) * hidden)[c] = R::pack(f[k]);
+        } else if (resid_out) {
+          reinterpret_cast<uint4 *>(resid_out + size_t(row) * hidden)[c] = sv[k];
+        }
+#pragma unroll
+        for (int i = 0; i < N; ++i) sq = fmaf(f[k][i], f[k][i], sq);
+      }
+    }
+    sq = warp_sum(sq);
+    const float norm = sqrtf(sq / float(hidden) + eps);
+    const float rn = 1.0f / norm;
+    uint4 *out = reinterpret_cast<uint4 *>(norm_out + size_t(row) * hidden);
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) {
+      const int c = lane + 32 * k;
+      if (c < chunks) {
+        float ww[N], y[N];
+        R::unpack(__ldg(wr + c), ww);
+#pragma unroll
+        for (int i = 0; i < N; ++i) y[i] = norm_weight<T>(f[k][i], norm, rn, ww[i]);
+        out[c] = R::pack(y);
+      }
+    }
+    row = next;
   }
 }
 
@@ -175,8 +193,19 @@ cudaError_t launch_add_rmsnorm_warp(const void *x, const void *r, const int32_t 
                                     void *resid_out, void *norm_out, int rows, int hidden, float eps,
                                     cudaStream_t st) {
   const int per_lane = (hidden / Raw16<T>::N + 31) / 32;
-  const dim3 grid((rows + 3) / 4);
   auto go = [&](auto kern) {
+    // as many CTAs of 4 warps as are resident at once (one wave); rows beyond it are walked by the same warps
+    static std::atomic<int> resident{0};
+    int n = resident.load(std::memory_order_relaxed);
+    if (n == 0) {
+      int dev = 0, sms = 0, per_sm = 0;
+      cudaGetDevice(&dev);
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, 0);
+      n = std::max(1, per_sm * sms);
+      resident.store(n, std::memory_order_relaxed);
+    }
+    const dim3 grid(std::min((rows + 3) / 4, n));
     kern<<<grid, 128, 0, st>>>((const T *)x, (const T *)r, row_index, (const T *)w, (T *)resid_out, (T *)norm_out,
                                rows, hidden, eps);
     return cudaGetLastError();

@@ -1,9 +1,9 @@
 // K3p on the 5th-generation tensor cores: ragged paged causal prefill with
 // tcgen05.mma, accumulators in tensor memory (TMEM).
 //
-// Same contract as the mma.sync build (ms_prefill_tc.cu; the prefill branch
-// of Attention::forward, src/backends/qwen2.rs:329-345, causal mask of
-// :476-503 incl. the offset columns of a cached prefix).  A CTA takes 256
+// The prefill branch of Attention::forward (src/backends/qwen2.rs:329-345,
+// causal mask of :476-503 incl. the offset columns of a cached prefix) over
+// the paged pool; ms_prefill_tc.cu plans the tiles and launches it.  A CTA takes 256
 // query rows of one KV head in two halves of 128 (the TMEM lanes), TPH = 128
 // / RPT tokens x the G query heads each (RPT = G rounded up to 1, 2, 4 or 8;
 // padding rows are computed like the half's first row and not stored).  The
@@ -197,34 +197,6 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
-}
-// (d0, d1) = (a0, a1) * b + c, one packed f32x2 FMA (each lane rounded once, as fmaf)
-__device__ __forceinline__ void ffma2(float &d0, float &d1, float a0, float a1, float b, float c) {
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %4};\n\t"
-      "mov.b64 rc, {%5, %5};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b), "f"(c));
-}
-// (d0, d1) += (a0, a1), one packed f32x2 add
-__device__ __forceinline__ void fadd2(float &d0, float &d1, float a0, float a1) {
-  asm("{\n\t.reg .b64 ra, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rd, {%0, %1};\n\t"
-      "add.rn.f32x2 rd, rd, ra;\n\tmov.b64 {%0, %1}, rd;\n}"
-      : "+f"(d0), "+f"(d1)
-      : "f"(a0), "f"(a1));
-}
-// (d0, d1) = (a0, a1) + (b0, b1) and (d0, d1) = (a0, a1) * (b0, b1) + (c0, c1), packed f32x2
-__device__ __forceinline__ void add2(float &d0, float &d1, float a0, float a1, float b0, float b1) {
-  asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
-__device__ __forceinline__ void fma2(float &d0, float &d1, float a0, float a1, float b0, float b1, float c0,
-                                     float c1) {
-  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n}"
-      : "=f"(d0), "=f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
 }
 // 2^x for two x <= 8 on the FMA and integer pipes instead of the transcendental unit
 // (Cody and Waite's argument split): j = rint(x) by adding and subtracting 1.5 * 2^23,

@@ -117,102 +117,139 @@ __global__ void qk_norm_rope_append_kernel(const T *__restrict__ qkv, const T *_
   }
 }
 
-// Vectorised K5 (16-byte aligned operands, power-of-two page size): one CTA
-// per token.  An item is 16 bytes (N values) of one head; TPH = D / N
-// consecutive threads hold one head, so the QK-norm sum reduces over those
-// lanes and the rotate-half partner of item c is item c ^ TPH/2 (the same
-// head, so the same norm).  Thread i takes items i, i + 256, ... (K at most)
-// of its token: every load is issued before any math, the token's position,
-// slot and table entries are read once, and no index needs a division.  Every
-// lane runs the shuffles (V heads and the items past the token's end compute
-// and discard), so the warp never splits around them.
-template <typename T, int D, int K>
+// Vectorised K5 (16-byte aligned operands, power-of-two page size).  A thread
+// holds one "pair item" of a head: dims [d, d + N) and their rotate-half
+// partners [d + D/2, d + D/2 + N), so RoPE needs no exchange between threads
+// and one set of cos/sin entries serves both halves; PPH = D / 2N consecutive
+// threads hold a head and reduce its QK-norm sum with PPH-wide shuffles.  A
+// row of threads (blockDim.x, a multiple of 32) covers every pair item of one
+// token, so a warp never spans two tokens and q, k and v heads fall in
+// separate warps; the CTA's TOKY rows take TOKY tokens, and each thread takes
+// KT tokens TOKY apart, issuing all its loads before any math.  The norm
+// weights (and bias) of a thread's head are loaded once.  16-bit math runs on
+// packed f32x2 instructions.
+template <typename T, int D, int KT>
 __global__ void __launch_bounds__(256) qk_norm_rope_append_vec_kernel(
     const T *__restrict__ qkv, const T *__restrict__ bias, const T *__restrict__ qn, const T *__restrict__ kn,
     const float *__restrict__ cos_t, const float *__restrict__ sin_t, const int32_t *__restrict__ positions,
     const int64_t *__restrict__ slot_mapping, T *__restrict__ q_out, T *__restrict__ k_pool,
-    T *__restrict__ v_pool, int hq, int hkv, int bs_shift, float eps) {
+    T *__restrict__ v_pool, int num_tokens, int hq, int hkv, int bs_shift, float eps) {
   using R = Raw16<T>;
   constexpr int N = R::N;
-  constexpr int TPH = D / N;
   constexpr int HALF = D / 2;
-  constexpr int HPP = 256 / TPH;  // heads per pass of the CTA
+  constexpr int PPH = HALF / N;  // threads per head
+  constexpr bool kF32 = std::is_same<T, float>::value;
   const int heads = hq + 2 * hkv;
-  const int t = blockIdx.x;
-  const int c = threadIdx.x % TPH;
-  const int d0 = c * N;
-  const int h0 = threadIdx.x / TPH;
+  const int item = threadIdx.x;
+  const bool live = item < heads * PPH;
+  const int h = live ? item / PPH : 0;
+  const int d0 = (item % PPH) * N;
+  const bool is_v = h >= hq + hkv;
+  const bool is_q = h < hq;
+  const T *nw = is_v ? nullptr : (is_q ? qn : kn);
 
-  const uint4 *src = reinterpret_cast<const uint4 *>(qkv + size_t(t) * heads * D);
-  uint4 xv[K];
+  // tokens of this thread
+  int tok[KT];
 #pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const int h = h0 + k * HPP;
-    xv[k] = h < heads ? __ldg(src + h * TPH + c) : make_uint4(0, 0, 0, 0);
-  }
-  const int pos = __ldg(positions + t);
-  const int64_t slot = __ldg(slot_mapping + t);
-  const int64_t blk = slot >> bs_shift;
-  const int off = int(slot & ((int64_t(1) << bs_shift) - 1));
-  float cf[N], sf[N];  // this thread's N table entries (f32, 16-byte aligned)
-  {
-    const float4 *cp = reinterpret_cast<const float4 *>(cos_t + size_t(pos) * HALF + (d0 % HALF));
-    const float4 *sp = reinterpret_cast<const float4 *>(sin_t + size_t(pos) * HALF + (d0 % HALF));
+  for (int k = 0; k < KT; ++k) tok[k] = (blockIdx.x * KT + k) * blockDim.y + threadIdx.y;
+  uint4 xl[KT], xh[KT];
 #pragma unroll
-    for (int q = 0; q < N / 4; ++q) {
-      const float4 a = __ldg(cp + q), b = __ldg(sp + q);
-      cf[4 * q] = a.x; cf[4 * q + 1] = a.y; cf[4 * q + 2] = a.z; cf[4 * q + 3] = a.w;
-      sf[4 * q] = b.x; sf[4 * q + 1] = b.y; sf[4 * q + 2] = b.z; sf[4 * q + 3] = b.w;
-    }
+  for (int k = 0; k < KT; ++k) {
+    const bool ok = live && tok[k] < num_tokens;
+    const uint4 *src = reinterpret_cast<const uint4 *>(qkv + (size_t(ok ? tok[k] : 0) * heads + h) * D + d0);
+    xl[k] = ok ? __ldg(src) : make_uint4(0, 0, 0, 0);
+    xh[k] = ok ? __ldg(src + HALF / N) : make_uint4(0, 0, 0, 0);
   }
-  const bool lower = c < TPH / 2;  // lower half rotates in -x2
+  float bl[N], bh[N], wl[N], wh[N];
+  if (bias && live) {
+    R::unpack(__ldg(reinterpret_cast<const uint4 *>(bias + size_t(h) * D + d0)), bl);
+    R::unpack(__ldg(reinterpret_cast<const uint4 *>(bias + size_t(h) * D + d0 + HALF)), bh);
+  }
+  if (nw && live) {
+    R::unpack(__ldg(reinterpret_cast<const uint4 *>(nw + d0)), wl);
+    R::unpack(__ldg(reinterpret_cast<const uint4 *>(nw + d0 + HALF)), wh);
+  }
 
 #pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const int h = h0 + k * HPP;
-    const bool ok = h < heads;
-    const int hc = ok ? h : 0;
-    const bool is_v = hc >= hq + hkv;
-    const bool is_q = hc < hq;
-    const T *nw = is_v ? nullptr : (is_q ? qn : kn);
-    float x[N];
-    R::unpack(xv[k], x);
+  for (int k = 0; k < KT; ++k) {
+    if (tok[k] >= num_tokens) break;  // uniform over the row, so over each warp
+    const int t = tok[k];
+    float fl[N], fh[N];
+    R::unpack(xl[k], fl);
+    R::unpack(xh[k], fh);
     if (bias) {
-      float b[N];
-      R::unpack(__ldg(reinterpret_cast<const uint4 *>(bias + size_t(hc) * D + d0)), b);
 #pragma unroll
-      for (int i = 0; i < N; ++i) x[i] += b[i];
+      for (int i = 0; i < N; i += 2) {
+        add2(fl[i], fl[i + 1], fl[i], fl[i + 1], bl[i], bl[i + 1]);
+        add2(fh[i], fh[i + 1], fh[i], fh[i + 1], bh[i], bh[i + 1]);
+      }
     }
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < N; ++i) ss = fmaf(x[i], x[i], ss);
-#pragma unroll
-    for (int o = TPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
-    float y[N];
+    const int64_t slot = __ldg(slot_mapping + t);
+    const int64_t blk = slot >> bs_shift;
+    const int off = int(slot & ((int64_t(1) << bs_shift) - 1));
+    if (is_v) {  // V: into the pool (warp-uniform branch)
+      if (live) {
+        T *dst = v_pool + ((size_t(blk) * hkv + (h - hq - hkv)) * (size_t(1) << bs_shift) + off) * D + d0;
+        reinterpret_cast<uint4 *>(dst)[0] = bias ? R::pack(fl) : xl[k];
+        reinterpret_cast<uint4 *>(dst + HALF)[0] = bias ? R::pack(fh) : xh[k];
+      }
+      continue;
+    }
     if (nw) {
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < N; i += 2) {
+        fma2(s0, s1, fl[i], fl[i + 1], fl[i], fl[i + 1], s0, s1);
+        fma2(s0, s1, fh[i], fh[i + 1], fh[i], fh[i + 1], s0, s1);
+      }
+      float ss = s0 + s1;
+#pragma unroll
+      for (int o = PPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
       const float norm = sqrtf(ss / float(D) + eps);
-      const float rn = 1.0f / norm;
-      float w[N];
-      R::unpack(__ldg(reinterpret_cast<const uint4 *>(nw + d0)), w);
+      if constexpr (kF32) {
 #pragma unroll
-      for (int i = 0; i < N; ++i) y[i] = qk_scale<T>(x[i], norm, rn, w[i]);
-    } else {
+        for (int i = 0; i < N; ++i) {
+          fl[i] = (fl[i] / norm) * wl[i];
+          fh[i] = (fh[i] / norm) * wh[i];
+        }
+      } else {
+        const float rn = 1.0f / norm;
 #pragma unroll
-      for (int i = 0; i < N; ++i) y[i] = x[i];
+        for (int i = 0; i < N; i += 2) {
+          float a0, a1, b0, b1;
+          mul2(a0, a1, wl[i], wl[i + 1], rn, rn);
+          mul2(b0, b1, wh[i], wh[i + 1], rn, rn);
+          mul2(fl[i], fl[i + 1], fl[i], fl[i + 1], a0, a1);
+          mul2(fh[i], fh[i + 1], fh[i], fh[i + 1], b0, b1);
+        }
+      }
     }
-    float o[N];
+    // rotate-half RoPE: lo' = lo cos - hi sin, hi' = hi cos + lo sin
+    float cf[N], sf[N];
+    {
+      const float4 *cp = reinterpret_cast<const float4 *>(cos_t + size_t(__ldg(positions + t)) * HALF + d0);
+      const float4 *sp = reinterpret_cast<const float4 *>(sin_t + size_t(__ldg(positions + t)) * HALF + d0);
 #pragma unroll
-    for (int i = 0; i < N; ++i) {
-      const float p = __shfl_xor_sync(kFull, y[i], TPH / 2);
-      o[i] = fmaf(y[i], cf[i], (lower ? -p : p) * sf[i]);
+      for (int q = 0; q < N / 4; ++q) {
+        const float4 c4 = __ldg(cp + q), s4 = __ldg(sp + q);
+        cf[4 * q] = c4.x; cf[4 * q + 1] = c4.y; cf[4 * q + 2] = c4.z; cf[4 * q + 3] = c4.w;
+        sf[4 * q] = s4.x; sf[4 * q + 1] = s4.y; sf[4 * q + 2] = s4.z; sf[4 * q + 3] = s4.w;
+      }
     }
-    const uint4 out = is_v ? (bias ? R::pack(x) : xv[k]) : R::pack(o);
-    if (!ok) continue;
-    T *dst;
-    if (is_q) dst = q_out + (size_t(t) * hq + hc) * D + d0;
-    else if (is_v) dst = v_pool + ((size_t(blk) * hkv + (hc - hq - hkv)) * (size_t(1) << bs_shift) + off) * D + d0;
-    else dst = k_pool + ((size_t(blk) * hkv + (hc - hq)) * (size_t(1) << bs_shift) + off) * D + d0;
-    *reinterpret_cast<uint4 *>(dst) = out;
+    float yl[N], yh[N];
+#pragma unroll
+    for (int i = 0; i < N; i += 2) {
+      float u0, u1, v0, v1;
+      mul2(u0, u1, fh[i], fh[i + 1], sf[i], sf[i + 1]);    // hi sin
+      mul2(v0, v1, fl[i], fl[i + 1], sf[i], sf[i + 1]);    // lo sin
+      fma2(yl[i], yl[i + 1], fl[i], fl[i + 1], cf[i], cf[i + 1], -u0, -u1);
+      fma2(yh[i], yh[i + 1], fh[i], fh[i + 1], cf[i], cf[i + 1], v0, v1);
+    }
+    if (!live) continue;
+    T *dst = is_q ? q_out + (size_t(t) * hq + h) * D + d0
+                  : k_pool + ((size_t(blk) * hkv + (h - hq)) * (size_t(1) << bs_shift) + off) * D + d0;
+    reinterpret_cast<uint4 *>(dst)[0] = R::pack(yl);
+    reinterpret_cast<uint4 *>(dst + HALF)[0] = R::pack(yh);
   }
 }
 
@@ -220,17 +257,17 @@ template <typename T, int D>
 cudaError_t launch_vec(const void *qkv, const void *bias, const void *qn, const void *kn, const void *cs,
                        const void *sn, const int32_t *positions, const int64_t *slots, void *q_out, void *k_pool,
                        void *v_pool, int T_, int hq, int hkv, int bs_shift, float eps, cudaStream_t st) {
-  const int per_thread = ((hq + 2 * hkv) * (D / Raw16<T>::N) + 255) / 256;
-  auto go = [&](auto kern) {
-    kern<<<T_, 256, 0, st>>>((const T *)qkv, (const T *)bias, (const T *)qn, (const T *)kn, (const float *)cs,
-                             (const float *)sn, positions, slots, (T *)q_out, (T *)k_pool, (T *)v_pool, hq, hkv,
-                             bs_shift, eps);
-    return cudaGetLastError();
-  };
-  if (per_thread <= 1) return go(qk_norm_rope_append_vec_kernel<T, D, 1>);
-  if (per_thread <= 2) return go(qk_norm_rope_append_vec_kernel<T, D, 2>);
-  if (per_thread <= 4) return go(qk_norm_rope_append_vec_kernel<T, D, 4>);
-  return go(qk_norm_rope_append_vec_kernel<T, D, 8>);
+  constexpr int KT = 2;
+  const int items = (hq + 2 * hkv) * (D / 2 / Raw16<T>::N);
+  const int bx = (items + 31) / 32 * 32;
+  if (bx > 256) return cudaErrorInvalidValue;
+  const int by = std::max(1, 256 / bx);
+  const int tokens_per_cta = by * KT;
+  const dim3 block(bx, by), grid((T_ + tokens_per_cta - 1) / tokens_per_cta);
+  qk_norm_rope_append_vec_kernel<T, D, KT><<<grid, block, 0, st>>>(
+      (const T *)qkv, (const T *)bias, (const T *)qn, (const T *)kn, (const float *)cs, (const float *)sn, positions,
+      slots, (T *)q_out, (T *)k_pool, (T *)v_pool, T_, hq, hkv, bs_shift, eps);
+  return cudaGetLastError();
 }
 
 inline bool host_aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -242,7 +279,8 @@ cudaError_t launch_typed(const void *qkv, const void *bias, const void *qn, cons
                          cudaStream_t st) {
   int bs_shift = 0;
   while ((1 << bs_shift) < bs) ++bs_shift;
-  const bool vec = (D == 128 || D == 64) && (1 << bs_shift) == bs && (hq + 2 * hkv) * (D * int(sizeof(T)) / 16) <= 8 * 256 &&
+  // the vector build: one row of at most 256 threads holds every pair item of a token
+  const bool vec = (D == 128 || D == 64) && (1 << bs_shift) == bs && (hq + 2 * hkv) * (D / 2 / Raw16<T>::N) <= 256 &&
                    host_aligned16(qkv) && (!bias || host_aligned16(bias)) &&
                    (!qn || host_aligned16(qn)) && (!kn || host_aligned16(kn)) && host_aligned16(cs) &&
                    host_aligned16(sn) && host_aligned16(q_out) && host_aligned16(k_pool) && host_aligned16(v_pool);
