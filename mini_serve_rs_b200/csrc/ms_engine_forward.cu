@@ -125,7 +125,7 @@ int enqueue_forward(Engine *eng, const StepPlan &plan) {
     MS_BLAS_TRY(linear(eng, w.w_qkv, eng->x_norm, eng->qkv, eng->qkv_dim, T, eng->H));
     MS_CUDA_TRY(launch_qk_norm_rope_append(eng->qkv, w.b_qkv, w.q_norm, w.k_norm, eng->cos_t, eng->sin_t, eng->d_pos,
                                            eng->d_slots, eng->qbuf, kp, vp, T, eng->hq, eng->hkv, eng->D,
-                                           eng->opts.block_size, eps, dt, st));
+                                           eng->opts.block_size, eps, dt, st, eng->d_status));
     // paged attention: one-token rows through split-K decode, prompt chunks through prefill tiles
     if (plan.n_dec > 0) {
       AttnArgs a{};

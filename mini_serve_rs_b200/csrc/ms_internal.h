@@ -91,7 +91,7 @@ cudaError_t launch_qk_norm_rope_append(const void *qkv, const void *bias, const 
                                        const int64_t *slot_mapping, void *q_out, void *k_pool,
                                        void *v_pool, int num_tokens, int num_heads, int num_kv_heads,
                                        int head_dim, int block_size, float eps, int dtype,
-                                       cudaStream_t stream);
+                                       cudaStream_t stream, unsigned *status = nullptr);
 
 cudaError_t launch_silu_mul(const void *gate_up, void *out, int rows, int inter, int dtype,
                             cudaStream_t stream);

@@ -20,8 +20,10 @@
 // lane l ^ 16.
 #include <type_traits>
 
-#include "ms_common.cuh"
-#include "ms_internal.h"
+#include <algorithm>
+#include <atomic>
+
+#include "ms_attention_common.cuh"
 
 namespace ms {
 namespace {
@@ -117,29 +119,48 @@ __global__ void qk_norm_rope_append_kernel(const T *__restrict__ qkv, const T *_
   }
 }
 
-// Vectorised K5 (16-byte aligned operands, power-of-two page size).  A thread
-// holds one "pair item" of a head: dims [d, d + N) and their rotate-half
-// partners [d + D/2, d + D/2 + N), so RoPE needs no exchange between threads
-// and one set of cos/sin entries serves both halves; PPH = D / 2N consecutive
-// threads hold a head and reduce its QK-norm sum with PPH-wide shuffles.  A
-// row of threads (blockDim.x, a multiple of 32) covers every pair item of one
-// token, so a warp never spans two tokens and q, k and v heads fall in
-// separate warps; the CTA's TOKY rows take TOKY tokens, and each thread takes
-// KT tokens TOKY apart, issuing all its loads before any math.  The norm
-// weights (and bias) of a thread's head are loaded once.  16-bit math runs on
-// packed f32x2 instructions.
-template <typename T, int D, int KT>
-__global__ void __launch_bounds__(256) qk_norm_rope_append_vec_kernel(
+// Staged K5 (16-byte aligned operands, power-of-two page size, every pair
+// item of a token in one CTA of 256 threads).  The CTA is persistent over
+// tokens blockIdx.x, blockIdx.x + gridDim.x, ...: one thread streams each
+// token's whole projection row (heads x D values, 8 KB for Qwen3-0.6B) and its
+// two RoPE table rows (f32 cos / sin at the token's position) into a ring of
+// kStages shared-memory slots with bulk copies (cp.async.bulk) completing on
+// one mbarrier per slot, kStages tokens ahead of the threads that use them, so
+// each SM keeps tens of KB of loads in flight with few registers.  The
+// tokens' positions and slots are read into shared memory once at the start.
+//
+// A thread holds one "pair item" of a head: dims [d, d + N) and their
+// rotate-half partners [d + D/2, d + D/2 + N), so RoPE needs no exchange
+// between threads; PPH = D / 2N consecutive threads hold a head and reduce its
+// QK-norm sum with PPH-wide shuffles; q, k and v heads fall in separate warps.
+// The norm weights (and bias) of a thread's head are loaded once.  A slot is
+// refilled only after the CTA barrier that follows its last read.  Every wait
+// is bounded: on expiry the CTA records kStatusWaitTimeout, waits (bounded)
+// for the copies it issued and returns.
+constexpr int kStages = 4;
+constexpr int kMaxTokPerCta = 64;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(256) qk_norm_rope_append_staged_kernel(
     const T *__restrict__ qkv, const T *__restrict__ bias, const T *__restrict__ qn, const T *__restrict__ kn,
     const float *__restrict__ cos_t, const float *__restrict__ sin_t, const int32_t *__restrict__ positions,
     const int64_t *__restrict__ slot_mapping, T *__restrict__ q_out, T *__restrict__ k_pool,
-    T *__restrict__ v_pool, int num_tokens, int hq, int hkv, int bs_shift, float eps) {
+    T *__restrict__ v_pool, int num_tokens, int hq, int hkv, int bs_shift, float eps, unsigned *status) {
   using R = Raw16<T>;
   constexpr int N = R::N;
   constexpr int HALF = D / 2;
   constexpr int PPH = HALF / N;  // threads per head
-  constexpr bool kF32 = std::is_same<T, float>::value;
+  constexpr uint32_t kTab = HALF * sizeof(float);
   const int heads = hq + 2 * hkv;
+  const uint32_t row_bytes = uint32_t(heads) * D * sizeof(T);
+  extern __shared__ __align__(128) unsigned char smem5[];
+  unsigned char *rows = smem5;                                           // [kStages][row_bytes]
+  float *tabs = reinterpret_cast<float *>(smem5 + kStages * row_bytes);  // [kStages][cos | sin][HALF]
+  __shared__ uint64_t full[kStages];
+  __shared__ int pos_s[kMaxTokPerCta];
+  __shared__ int64_t slot_s[kMaxTokPerCta];
+
+  const int n_my = blockIdx.x < num_tokens ? (num_tokens - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
   const int item = threadIdx.x;
   const bool live = item < heads * PPH;
   const int h = live ? item / PPH : 0;
@@ -148,17 +169,14 @@ __global__ void __launch_bounds__(256) qk_norm_rope_append_vec_kernel(
   const bool is_q = h < hq;
   const T *nw = is_v ? nullptr : (is_q ? qn : kn);
 
-  // tokens of this thread
-  int tok[KT];
-#pragma unroll
-  for (int k = 0; k < KT; ++k) tok[k] = (blockIdx.x * KT + k) * blockDim.y + threadIdx.y;
-  uint4 xl[KT], xh[KT];
-#pragma unroll
-  for (int k = 0; k < KT; ++k) {
-    const bool ok = live && tok[k] < num_tokens;
-    const uint4 *src = reinterpret_cast<const uint4 *>(qkv + (size_t(ok ? tok[k] : 0) * heads + h) * D + d0);
-    xl[k] = ok ? __ldg(src) : make_uint4(0, 0, 0, 0);
-    xh[k] = ok ? __ldg(src + HALF / N) : make_uint4(0, 0, 0, 0);
+  for (int i = threadIdx.x; i < n_my; i += blockDim.x) {
+    const int t = blockIdx.x + i * gridDim.x;
+    pos_s[i] = __ldg(positions + t);
+    slot_s[i] = __ldg(slot_mapping + t);
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) attn::mbar_init(&full[s], 1);
+    attn::fence_barrier_init();
   }
   float bl[N], bh[N], wl[N], wh[N];
   if (bias && live) {
@@ -169,104 +187,126 @@ __global__ void __launch_bounds__(256) qk_norm_rope_append_vec_kernel(
     R::unpack(__ldg(reinterpret_cast<const uint4 *>(nw + d0)), wl);
     R::unpack(__ldg(reinterpret_cast<const uint4 *>(nw + d0 + HALF)), wh);
   }
+  __syncthreads();
 
-#pragma unroll
-  for (int k = 0; k < KT; ++k) {
-    if (tok[k] >= num_tokens) break;  // uniform over the row, so over each warp
-    const int t = tok[k];
-    float fl[N], fh[N];
-    R::unpack(xl[k], fl);
-    R::unpack(xh[k], fh);
-    if (bias) {
-#pragma unroll
-      for (int i = 0; i < N; i += 2) {
-        add2(fl[i], fl[i + 1], fl[i], fl[i + 1], bl[i], bl[i + 1]);
-        add2(fh[i], fh[i + 1], fh[i], fh[i + 1], bh[i], bh[i + 1]);
+  auto issue = [&](int i) {  // thread 0: token i of this CTA into slot i % kStages
+    const int s = i % kStages;
+    const int t = blockIdx.x + i * gridDim.x;
+    const size_t pos = size_t(pos_s[i]);
+    attn::mbar_expect_tx(&full[s], row_bytes + 2 * kTab);
+    attn::bulk_g2s(rows + size_t(s) * row_bytes, qkv + size_t(t) * heads * D, row_bytes, &full[s]);
+    attn::bulk_g2s(tabs + s * 2 * HALF, cos_t + pos * HALF, kTab, &full[s]);
+    attn::bulk_g2s(tabs + s * 2 * HALF + HALF, sin_t + pos * HALF, kTab, &full[s]);
+  };
+  int issued = 0;
+  if (threadIdx.x == 0)
+    for (; issued < min(kStages, n_my); ++issued) issue(issued);
+
+  for (int i = 0; i < n_my; ++i) {
+    const int s = i % kStages;
+    const bool ok = attn::mbar_wait_bounded(&full[s], (i / kStages) & 1);
+    if (__syncthreads_or(!ok)) {  // give up: record it, let the copies in flight land, leave
+      if (threadIdx.x == 0) {
+        if (status) atomicOr(status, kStatusWaitTimeout);
+        for (int j = i; j < issued; ++j) attn::mbar_wait_bounded(&full[j % kStages], (j / kStages) & 1);
       }
+      return;
     }
-    const int64_t slot = __ldg(slot_mapping + t);
-    const int64_t blk = slot >> bs_shift;
-    const int off = int(slot & ((int64_t(1) << bs_shift) - 1));
-    if (is_v) {  // V: into the pool (warp-uniform branch)
-      if (live) {
+    const int t = blockIdx.x + i * gridDim.x;
+    const unsigned char *row = rows + size_t(s) * row_bytes + (size_t(h) * D + d0) * sizeof(T);
+    if (live) {
+      const uint4 xl = *reinterpret_cast<const uint4 *>(row);
+      const uint4 xh = *reinterpret_cast<const uint4 *>(row + HALF * sizeof(T));
+      float fl[N], fh[N];
+      R::unpack(xl, fl);
+      R::unpack(xh, fh);
+      if (bias) {
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+          fl[k] += bl[k];
+          fh[k] += bh[k];
+        }
+      }
+      const int64_t slot = slot_s[i];
+      const int64_t blk = slot >> bs_shift;
+      const int off = int(slot & ((int64_t(1) << bs_shift) - 1));
+      if (is_v) {  // V: into the pool
         T *dst = v_pool + ((size_t(blk) * hkv + (h - hq - hkv)) * (size_t(1) << bs_shift) + off) * D + d0;
-        reinterpret_cast<uint4 *>(dst)[0] = bias ? R::pack(fl) : xl[k];
-        reinterpret_cast<uint4 *>(dst + HALF)[0] = bias ? R::pack(fh) : xh[k];
-      }
-      continue;
-    }
-    if (nw) {
-      float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-      for (int i = 0; i < N; i += 2) {
-        fma2(s0, s1, fl[i], fl[i + 1], fl[i], fl[i + 1], s0, s1);
-        fma2(s0, s1, fh[i], fh[i + 1], fh[i], fh[i + 1], s0, s1);
-      }
-      float ss = s0 + s1;
-#pragma unroll
-      for (int o = PPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
-      const float norm = sqrtf(ss / float(D) + eps);
-      if constexpr (kF32) {
-#pragma unroll
-        for (int i = 0; i < N; ++i) {
-          fl[i] = (fl[i] / norm) * wl[i];
-          fh[i] = (fh[i] / norm) * wh[i];
-        }
+        reinterpret_cast<uint4 *>(dst)[0] = bias ? R::pack(fl) : xl;
+        reinterpret_cast<uint4 *>(dst + HALF)[0] = bias ? R::pack(fh) : xh;
       } else {
-        const float rn = 1.0f / norm;
+        if (nw) {
+          float ss = 0.f;
 #pragma unroll
-        for (int i = 0; i < N; i += 2) {
-          float a0, a1, b0, b1;
-          mul2(a0, a1, wl[i], wl[i + 1], rn, rn);
-          mul2(b0, b1, wh[i], wh[i + 1], rn, rn);
-          mul2(fl[i], fl[i + 1], fl[i], fl[i + 1], a0, a1);
-          mul2(fh[i], fh[i + 1], fh[i], fh[i + 1], b0, b1);
+          for (int k = 0; k < N; ++k) ss = fmaf(fh[k], fh[k], fmaf(fl[k], fl[k], ss));
+#pragma unroll
+          for (int o = PPH / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(__activemask(), ss, o);
+          const float norm = sqrtf(ss / float(D) + eps);
+          const float rn = 1.0f / norm;
+#pragma unroll
+          for (int k = 0; k < N; ++k) {
+            fl[k] = qk_scale<T>(fl[k], norm, rn, wl[k]);
+            fh[k] = qk_scale<T>(fh[k], norm, rn, wh[k]);
+          }
         }
+        const float *cs = tabs + s * 2 * HALF + d0;
+        const float *sn = cs + HALF;
+        float yl[N], yh[N];
+#pragma unroll
+        for (int k = 0; k < N; ++k) {
+          const float c = cs[k], sv = sn[k];
+          yl[k] = fmaf(fl[k], c, -fh[k] * sv);  // lo' = lo cos - hi sin
+          yh[k] = fmaf(fh[k], c, fl[k] * sv);   // hi' = hi cos + lo sin
+        }
+        T *dst = is_q ? q_out + (size_t(t) * hq + h) * D + d0
+                      : k_pool + ((size_t(blk) * hkv + (h - hq)) * (size_t(1) << bs_shift) + off) * D + d0;
+        reinterpret_cast<uint4 *>(dst)[0] = R::pack(yl);
+        reinterpret_cast<uint4 *>(dst + HALF)[0] = R::pack(yh);
       }
     }
-    // rotate-half RoPE: lo' = lo cos - hi sin, hi' = hi cos + lo sin
-    float cf[N], sf[N];
-    {
-      const float4 *cp = reinterpret_cast<const float4 *>(cos_t + size_t(__ldg(positions + t)) * HALF + d0);
-      const float4 *sp = reinterpret_cast<const float4 *>(sin_t + size_t(__ldg(positions + t)) * HALF + d0);
-#pragma unroll
-      for (int q = 0; q < N / 4; ++q) {
-        const float4 c4 = __ldg(cp + q), s4 = __ldg(sp + q);
-        cf[4 * q] = c4.x; cf[4 * q + 1] = c4.y; cf[4 * q + 2] = c4.z; cf[4 * q + 3] = c4.w;
-        sf[4 * q] = s4.x; sf[4 * q + 1] = s4.y; sf[4 * q + 2] = s4.z; sf[4 * q + 3] = s4.w;
-      }
+    __syncthreads();  // slot s has been read by every thread
+    if (threadIdx.x == 0 && issued < n_my) {
+      attn::fence_proxy_async();  // the generic-proxy reads of the slot before its async refill
+      issue(issued++);
     }
-    float yl[N], yh[N];
-#pragma unroll
-    for (int i = 0; i < N; i += 2) {
-      float u0, u1, v0, v1;
-      mul2(u0, u1, fh[i], fh[i + 1], sf[i], sf[i + 1]);    // hi sin
-      mul2(v0, v1, fl[i], fl[i + 1], sf[i], sf[i + 1]);    // lo sin
-      fma2(yl[i], yl[i + 1], fl[i], fl[i + 1], cf[i], cf[i + 1], -u0, -u1);
-      fma2(yh[i], yh[i + 1], fh[i], fh[i + 1], cf[i], cf[i + 1], v0, v1);
-    }
-    if (!live) continue;
-    T *dst = is_q ? q_out + (size_t(t) * hq + h) * D + d0
-                  : k_pool + ((size_t(blk) * hkv + (h - hq)) * (size_t(1) << bs_shift) + off) * D + d0;
-    reinterpret_cast<uint4 *>(dst)[0] = R::pack(yl);
-    reinterpret_cast<uint4 *>(dst + HALF)[0] = R::pack(yh);
   }
 }
 
 template <typename T, int D>
-cudaError_t launch_vec(const void *qkv, const void *bias, const void *qn, const void *kn, const void *cs,
-                       const void *sn, const int32_t *positions, const int64_t *slots, void *q_out, void *k_pool,
-                       void *v_pool, int T_, int hq, int hkv, int bs_shift, float eps, cudaStream_t st) {
-  constexpr int KT = 2;
-  const int items = (hq + 2 * hkv) * (D / 2 / Raw16<T>::N);
-  const int bx = (items + 31) / 32 * 32;
-  if (bx > 256) return cudaErrorInvalidValue;
-  const int by = std::max(1, 256 / bx);
-  const int tokens_per_cta = by * KT;
-  const dim3 block(bx, by), grid((T_ + tokens_per_cta - 1) / tokens_per_cta);
-  qk_norm_rope_append_vec_kernel<T, D, KT><<<grid, block, 0, st>>>(
-      (const T *)qkv, (const T *)bias, (const T *)qn, (const T *)kn, (const float *)cs, (const float *)sn, positions,
-      slots, (T *)q_out, (T *)k_pool, (T *)v_pool, T_, hq, hkv, bs_shift, eps);
+cudaError_t launch_staged(const void *qkv, const void *bias, const void *qn, const void *kn, const void *cs,
+                          const void *sn, const int32_t *positions, const int64_t *slots, void *q_out,
+                          void *k_pool, void *v_pool, int T_, int hq, int hkv, int bs_shift, float eps,
+                          unsigned *status, cudaStream_t st) {
+  auto kern = qk_norm_rope_append_staged_kernel<T, D>;
+  const int row_bytes = (hq + 2 * hkv) * D * int(sizeof(T));
+  const int smem = kStages * (row_bytes + 2 * (D / 2) * int(sizeof(float)));
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  // per device: the shared-memory attribute set so far and the resident CTAs it allows
+  static std::atomic<int> smem_set[64], resident[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (smem > smem_set[dev].load(std::memory_order_acquire)) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    int n_sm = 0, per = 0;
+    cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kern, 256, smem);
+    resident[dev].store(std::max(1, per) * std::max(1, n_sm), std::memory_order_relaxed);
+    smem_set[dev].store(smem, std::memory_order_release);  // setting twice is harmless
+  }
+  // one resident wave of persistent CTAs, each holding at most kMaxTokPerCta tokens
+  int grid = resident[dev].load(std::memory_order_relaxed);
+  grid = std::max(grid, (T_ + kMaxTokPerCta - 1) / kMaxTokPerCta);
+  grid = std::min(grid, T_);
+  if (status == nullptr) {
+    e = standalone_status_word(&status);
+    if (e != cudaSuccess) return e;
+  }
+  kern<<<grid, 256, smem, st>>>((const T *)qkv, (const T *)bias, (const T *)qn, (const T *)kn, (const float *)cs,
+                                (const float *)sn, positions, slots, (T *)q_out, (T *)k_pool, (T *)v_pool, T_, hq,
+                                hkv, bs_shift, eps, status);
   return cudaGetLastError();
 }
 
@@ -276,20 +316,21 @@ template <typename T>
 cudaError_t launch_typed(const void *qkv, const void *bias, const void *qn, const void *kn, const void *cs,
                          const void *sn, const int32_t *positions, const int64_t *slots, void *q_out,
                          void *k_pool, void *v_pool, int T_, int hq, int hkv, int D, int bs, float eps,
-                         cudaStream_t st) {
+                         unsigned *status, cudaStream_t st) {
   int bs_shift = 0;
   while ((1 << bs_shift) < bs) ++bs_shift;
-  // the vector build: one row of at most 256 threads holds every pair item of a token
-  const bool vec = (D == 128 || D == 64) && (1 << bs_shift) == bs && (hq + 2 * hkv) * (D / 2 / Raw16<T>::N) <= 256 &&
-                   host_aligned16(qkv) && (!bias || host_aligned16(bias)) &&
-                   (!qn || host_aligned16(qn)) && (!kn || host_aligned16(kn)) && host_aligned16(cs) &&
-                   host_aligned16(sn) && host_aligned16(q_out) && host_aligned16(k_pool) && host_aligned16(v_pool);
-  if (vec) {
+  // the staged build: 16-bit types, one CTA of 256 threads holds every pair item of a token
+  const bool staged = !std::is_same<T, float>::value && (D == 128 || D == 64) && (1 << bs_shift) == bs &&
+                      (hq + 2 * hkv) * (D / 2 / Raw16<T>::N) <= 256 && host_aligned16(qkv) &&
+                      (!bias || host_aligned16(bias)) && (!qn || host_aligned16(qn)) && (!kn || host_aligned16(kn)) &&
+                      host_aligned16(cs) && host_aligned16(sn) && host_aligned16(q_out) && host_aligned16(k_pool) &&
+                      host_aligned16(v_pool);
+  if (staged) {
     if (D == 128)
-      return launch_vec<T, 128>(qkv, bias, qn, kn, cs, sn, positions, slots, q_out, k_pool, v_pool, T_, hq, hkv,
-                                bs_shift, eps, st);
-    return launch_vec<T, 64>(qkv, bias, qn, kn, cs, sn, positions, slots, q_out, k_pool, v_pool, T_, hq, hkv,
-                             bs_shift, eps, st);
+      return launch_staged<T, 128>(qkv, bias, qn, kn, cs, sn, positions, slots, q_out, k_pool, v_pool, T_, hq, hkv,
+                                   bs_shift, eps, status, st);
+    return launch_staged<T, 64>(qkv, bias, qn, kn, cs, sn, positions, slots, q_out, k_pool, v_pool, T_, hq, hkv,
+                                bs_shift, eps, status, st);
   }
   const long long warps = (long long)T_ * (hq + 2 * hkv);
   const int threads = 256;
@@ -315,22 +356,22 @@ cudaError_t launch_qk_norm_rope_append(const void *qkv, const void *bias, const 
                                        const int32_t *positions, const int64_t *slot_mapping, void *q_out,
                                        void *k_pool, void *v_pool, int num_tokens, int num_heads,
                                        int num_kv_heads, int head_dim, int block_size, float eps, int dtype,
-                                       cudaStream_t st) {
+                                       cudaStream_t st, unsigned *status) {
   if (num_tokens == 0) return cudaSuccess;
   if (num_tokens < 0 || num_heads <= 0 || num_kv_heads <= 0 || block_size <= 0) return cudaErrorInvalidValue;
   switch (dtype) {
     case MS_DTYPE_F32:
       return launch_typed<float>(qkv, bias, q_norm_w, k_norm_w, cos_table, sin_table, positions, slot_mapping,
                                  q_out, k_pool, v_pool, num_tokens, num_heads, num_kv_heads, head_dim,
-                                 block_size, eps, st);
+                                 block_size, eps, status, st);
     case MS_DTYPE_BF16:
       return launch_typed<__nv_bfloat16>(qkv, bias, q_norm_w, k_norm_w, cos_table, sin_table, positions,
                                          slot_mapping, q_out, k_pool, v_pool, num_tokens, num_heads,
-                                         num_kv_heads, head_dim, block_size, eps, st);
+                                         num_kv_heads, head_dim, block_size, eps, status, st);
     case MS_DTYPE_F16:
       return launch_typed<__half>(qkv, bias, q_norm_w, k_norm_w, cos_table, sin_table, positions, slot_mapping,
                                   q_out, k_pool, v_pool, num_tokens, num_heads, num_kv_heads, head_dim,
-                                  block_size, eps, st);
+                                  block_size, eps, status, st);
     default:
       return cudaErrorInvalidValue;
   }
@@ -347,5 +388,5 @@ extern "C" int ms_launch_qk_norm_rope_append(const void *qkv, const void *bias, 
   return int(ms::launch_qk_norm_rope_append(qkv, bias, q_norm_w, k_norm_w, cos_table, sin_table, positions,
                                             slot_mapping, q_out, k_pool, v_pool, num_tokens, num_heads,
                                             num_kv_heads, head_dim, block_size, eps, dtype,
-                                            static_cast<cudaStream_t>(stream)));
+                                            static_cast<cudaStream_t>(stream), nullptr));
 }
