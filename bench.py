@@ -13,7 +13,17 @@ of KV) are far larger than L2, so no flush is needed between steps.
 
 Multi-GPU: one process per GPU (torchrun), each rank an independent
 data-parallel replica with its own 256 sequences (weak scaling, no data-path
-collective); rank 0 prints the whole-job aggregate.
+collective); rank 0 prints the whole-job aggregate.  With N >= 2 the line
+also carries a "tp" record: BASELINE config 5 (Qwen2.5-7B architecture) under
+tensor parallelism by KV head on the same ranks (TP=2 at N=2, TP=4 at N=4, two
+TP=4 replicas at N=8) -- first the committed transformers golden case on every
+rank (fused peer-memory and NCCL all-reduce), then decode steps timed with each
+all-reduce path, with the all-reduce share of the step.
+
+CPU leg (N=1 line's cpu_baseline, and --impl reference): the oracle's
+torch-CPU f32 restatement of the reference's batched decode at batches 8, 32,
+64 and 256 (the GPU arm's), all host threads; the value is the largest batch
+that fits host memory.
 """
 from __future__ import annotations
 

@@ -141,34 +141,29 @@ __global__ void __launch_bounds__(128) add_rmsnorm_warp_kernel(const T *__restri
   if (row < rows) fetch(row);
   const uint4 *wr = reinterpret_cast<const uint4 *>(w);
   while (row < rows) {  // warp-uniform
-    uint4 sv[CPL], rv[CPL];
-#pragma unroll
-    for (int k = 0; k < CPL; ++k) {
-      sv[k] = nx[k];
-      rv[k] = nr[k];
-    }
-    const int next = row + stride;
-    if (next < rows) fetch(next);
     float f[CPL][N];  // the f32 sums
     float sq = 0.f;
 #pragma unroll
     for (int k = 0; k < CPL; ++k) {
       const int c = lane + 32 * k;
       if (c < chunks) {
-        R::unpack(sv[k], f[k]);
+        R::unpack(nx[k], f[k]);
         if (r) {
           float b[N];
-          R::unpack(rv[k], b);
+          R::unpack(nr[k], b);
 #pragma unroll
           for (int i = 0; i < N; ++i) f[k][i] += b[i];
           if (resid_out) reinterpret_cast<uint4 *>(resid_out + size_t(row) * hidden)[c] = R::pack(f[k]);
         } else if (resid_out) {
-          reinterpret_cast<uint4 *>(resid_out + size_t(row) * hidden)[c] = sv[k];
+          reinterpret_cast<uint4 *>(resid_out + size_t(row) * hidden)[c] = nx[k];
         }
 #pragma unroll
         for (int i = 0; i < N; ++i) sq = fmaf(f[k][i], f[k][i], sq);
       }
     }
+    // the current row is in registers: fetch the next one while this one is reduced and written
+    const int next = row + stride;
+    if (next < rows) fetch(next);
     sq = warp_sum(sq);
     const float norm = sqrtf(sq / float(hidden) + eps);
     const float rn = 1.0f / norm;

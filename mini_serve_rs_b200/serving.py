@@ -2,10 +2,11 @@
 
 The caller side of the hot path, as the reference's Scheduler runs it
 (src/scheduler/scheduler.rs):
-* FIFO admission while there is room (:312-382).  Each request first reserves
-  its worst-case pages (reserve_sequence); one whose reservation or pages do
-  not fit stays queued until running requests free room (with nothing
-  running, a reservation that cannot fit fails the request).
+* FIFO admission while there is room (:312-382).  With reserve=True each
+  request first reserves its worst-case pages (reserve_sequence); one whose
+  reservation or pages do not fit stays queued until running requests free
+  room (with nothing running, a reservation that cannot fit fails the
+  request).
 * One ragged ms_step per iteration over every active request (:422-449).
 * Block growth before a step (:430-431).
 * Release when a request finishes (:555) or fails (:446).
@@ -48,9 +49,14 @@ class Request:
 
 class ServingLoop:
     def __init__(self, eng: E.Engine, pages: E.Pages, max_active: int = 256, token_budget: int = 2048,
-                 block_size: int = 16):
+                 block_size: int = 16, reserve: bool = False):
+        """reserve: admit a request only once its worst-case pages (prompt +
+        max_tokens) are reserved (reserve_sequence's budget, scheduler.rs:325-343);
+        off, pages are taken as the request grows and a pool that runs dry
+        fails the growing request (scheduler.rs:430-446)."""
         self.eng = eng
         self.pages = pages
+        self.reserve = reserve
         self.max_active = max_active
         self.token_budget = token_budget
         self.bs = block_size
@@ -69,16 +75,17 @@ class ServingLoop:
             # reserve_sequence before the first forward (scheduler.rs:325-343): the request's
             # worst-case pages; while they do not fit it waits for running requests to finish,
             # and fails (as the reference's admission does) when nothing is running
-            try:
-                self.pages.reserve(r.rid, len(r.prompt), r.max_tokens)
-            except E.EngineError as e:
-                if isinstance(e, E.CachePressure) and self.active:
-                    break
-                self.queue.popleft()
-                r.error = str(e)
-                r.done_at = now
-                self.finished.append(r)
-                continue
+            if self.reserve:
+                try:
+                    self.pages.reserve(r.rid, len(r.prompt), r.max_tokens)
+                except E.EngineError as e:
+                    if isinstance(e, E.CachePressure) and self.active:
+                        break
+                    self.queue.popleft()
+                    r.error = str(e)
+                    r.done_at = now
+                    self.finished.append(r)
+                    continue
             try:
                 r.blocks, r.cached = self.pages.admit(r.rid, r.prompt)
             except E.CachePressure:

@@ -232,14 +232,19 @@ def _config3_batch(gen):
     return torch.tensor(pos[:T], dtype=torch.int32)
 
 
-@pytest.mark.parametrize("dt,qk_norm,bias", [(torch.bfloat16, True, False), (torch.float32, True, False),
-                                             (torch.bfloat16, False, True)])
-def test_qk_norm_rope_append_config3(dt, qk_norm, bias):
+@pytest.mark.parametrize("dt,qk_norm,bias,hq,hkv", [(torch.bfloat16, True, False, 16, 8),
+                                                    (torch.float32, True, False, 16, 8),
+                                                    (torch.bfloat16, False, True, 16, 8),
+                                                    (torch.bfloat16, False, True, 7, 1),
+                                                    (torch.bfloat16, True, False, 14, 2)])
+def test_qk_norm_rope_append_config3(dt, qk_norm, bias, hq, hkv):
     """BASELINE config 3's QK-norm + RoPE (theta 1e6) on 16/8 heads x 128 over a
-    packed T=8192 batch; K and V must land in exactly their slot."""
+    packed T=8192 batch; K and V must land in exactly their slot.  Also the head
+    counts one tensor-parallel rank of Qwen2.5-7B holds (7/1 at TP=4 with q/k/v
+    bias, 14/2 at TP=2), where a warp holds pair items of two kinds of head."""
     lib = E.lib()
     gen = torch.Generator().manual_seed(33)
-    T, hq, hkv, D = 8192, 16, 8, 128
+    T, D = 8192, 128
     pos = _config3_batch(gen)
     qkv = torch.randn(T, (hq + 2 * hkv) * D, generator=gen).to(dt)
     qn = (1 + 0.1 * torch.randn(D, generator=gen)).to(dt) if qk_norm else None

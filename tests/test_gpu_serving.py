@@ -27,12 +27,12 @@ def _trace(cfg, n=16):
     return reqs
 
 
-def _serve(cfg, w, reqs, max_active, budget, max_chunks):
-    eng = E.Engine(cfg, pool_blocks=160, max_seqs=8, max_tokens_per_step=512, max_blocks_per_seq=16,
+def _serve(cfg, w, reqs, max_active, budget, max_chunks, reserve=False, pool=160):
+    eng = E.Engine(cfg, pool_blocks=pool, max_seqs=8, max_tokens_per_step=512, max_blocks_per_seq=16,
                    dtype=E.MS_DTYPE_F32)
     eng.load_weights(w)
-    pages = E.Pages(160, 16, max_chunks=max_chunks)
-    loop = ServingLoop(eng, pages, max_active=max_active, token_budget=budget)
+    pages = E.Pages(pool, 16, max_chunks=max_chunks)
+    loop = ServingLoop(eng, pages, max_active=max_active, token_budget=budget, reserve=reserve)
     elapsed = loop.run(reqs, timeout_s=120.0)
     st = pages.stats()
     eng.close()
@@ -51,3 +51,22 @@ def test_serving_loop_matches_requests_served_alone():
     assert len(bad) <= 1, bad
     assert st["hits"] >= 3, st  # requests 4, 7, 10, 13, 16 reuse the shared prefix pages
     assert st["free_blocks"] + st["cache_only_blocks"] == st["total_blocks"], st
+
+
+def test_serving_loop_with_reservations_waits_for_room_and_matches():
+    """reserve=True: each request reserves its worst-case pages before
+    admission (reserve_sequence); with a pool of 24 pages that cover about
+    four requests' worst cases, requests wait in the queue for reservations to
+    free, none fails, the tokens equal those served alone, and every
+    reservation is returned."""
+    need_gpu()
+    case = MODEL_CASES[1]
+    cfg = case["cfg"]
+    w = random_weights(cfg, case["seed"], norm_std=case.get("norm_std", 0.0))
+    got, summ, st, _ = _serve(cfg, w, _trace(cfg), max_active=6, budget=40, max_chunks=32, reserve=True, pool=24)
+    want, _, _, _ = _serve(cfg, w, _trace(cfg), max_active=1, budget=0, max_chunks=0)
+    assert summ["failed"] == 0 and len(got) == 16
+    bad = [rid for rid in want if got[rid] != want[rid]]
+    assert len(bad) <= 1, bad
+    assert st["reservation_rejections"] > 0, st  # some requests had to wait for reservations
+    assert st["peak_reserved_blocks"] <= 24 and st["reserved_blocks"] == 0, st
