@@ -747,6 +747,8 @@ def run_tp(args, rank, world, local):
     import torch.distributed as dist
     from mini_serve_rs_b200 import engine as E
     tp = 2 if world == 2 or world % 4 else 4
+    if world % tp:
+        return {"skipped": f"{world} ranks do not split into tensor-parallel groups of {tp}"}
     torch.cuda.empty_cache()
     group, tp_rank, comm = tp_group_comm(rank, world, local, tp)
     try:
