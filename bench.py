@@ -922,9 +922,12 @@ def run_sample_kernel(args, local):
     topp = timed(lambda: lib.ms_launch_sample(ptr(lg), rows, V, ptr(t), ptr(p9), ptr(sd), ptr(out), sp))
     plain = timed(lambda: lib.ms_launch_sample(ptr(lg), rows, V, ptr(t), None, ptr(sd), ptr(out), sp))
     amax = timed(lambda: lib.ms_launch_argmax(ptr(lg), rows, V, ptr(out), sp))
+    peak, kind = peaks()
+    nbytes = rows * V * 4  # the logits, read once (155 MB, above the 126 MB L2)
     print(json.dumps({"workload": "256 rows x 151936 f32 logits (Qwen3 vocabulary), temperature 0.8",
-                      "logits_bytes": rows * V * 4, "ms_top_p_0.9": topp, "ms_temperature_only": plain,
-                      "ms_argmax": amax}), flush=True)
+                      "logits_bytes": nbytes, "ms_top_p_0.9": topp, "ms_temperature_only": plain,
+                      "ms_argmax": amax, "top_p_frac_of_hbm_read_once": nbytes / topp / 1e6 / peak,
+                      "peak_gbs": peak, "peak_source": kind}), flush=True)
 
 
 def run_prefill_kernel(args, local, seqs: int = 4, length: int = 4096):

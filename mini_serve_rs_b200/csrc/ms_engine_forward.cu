@@ -250,6 +250,7 @@ int enqueue_forward(Engine *eng, const StepPlan &plan) {
     sa.out = eng->d_next;
     sa.row_slot = pa.seq_row;
     sa.slot_last = eng->d_slot_last;
+    sa.status = eng->d_status;
     MS_CUDA_TRY(launch_sample(sa, st));
   }
   {

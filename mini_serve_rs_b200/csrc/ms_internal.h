@@ -106,6 +106,7 @@ struct SampleArgs {
   int32_t *out = nullptr;               // [rows]
   const int32_t *row_slot = nullptr;    // with slot_last: also record the token per slot
   int32_t *slot_last = nullptr;
+  unsigned *status = nullptr;           // kStatus* bits; null: the standalone status word
 };
 cudaError_t launch_sample(const SampleArgs &a, cudaStream_t st);
 cudaError_t launch_argmax(const float *logits, int rows, int vocab, int32_t *out,

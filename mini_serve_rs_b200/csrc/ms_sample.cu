@@ -9,8 +9,8 @@
 // the tokens before it reaches top_p -- then a draw from the remaining weights.
 // Temperatures below 1e-7 select argmax (LogitsProcessor::new).
 //
-// Here one CTA per row works in passes over the row's logits (L2-resident
-// after the first), z = x * inv_t:
+// A cluster of kCluster CTAs works on one row, in passes over its logits,
+// z = x * inv_t:
 //   1. the max m of z and an exponential race over all tokens: token i scores
 //      z_i - log(E_i) with E_i = -log(U_i) ~ Exp(1), and the largest score
 //      picks i with probability exp(z_i) / sum(exp(z)).  U_i comes from
@@ -34,16 +34,37 @@
 // The reference seeds its generator from the wall clock, so parity is the
 // sampled distribution (and, against the CPU restatement of this kernel, the
 // exact token for a given seed).
+//
+// Layout: CTA c of a row's cluster takes the contiguous slice [c S, c S + S)
+// of the row (S = ceil(V / kCluster) rounded up to 4 tokens) and, when the
+// slice fits, keeps it in shared memory for every pass, so the row crosses
+// HBM once: kChunks bulk copies (cp.async.bulk, one mbarrier each) stream it
+// in and pass 1 starts on the first piece.  Each reduction (max, race winner,
+// masses, radix histograms, tie counts) is a CTA reduction, then an exchange
+// through distributed shared memory: every CTA publishes its share, a
+// cluster barrier, and every CTA combines all shares itself, so all CTAs of
+// a row take the same branches.  Max, the (score, index) argmax and integer
+// sums do not depend on the order of combination, so the token drawn does
+// not depend on how the row is split.  A copy that never lands (a bounded
+// wait that runs out) sets kStatusWaitTimeout and leaves the row's argmax.
+#include <cooperative_groups.h>
+
+#include <atomic>
 #include <cstdint>
 
+#include "ms_attention_common.cuh"
 #include "ms_common.cuh"
 #include "ms_internal.h"
 
 namespace ms {
 namespace {
+namespace cg = cooperative_groups;
 
-constexpr int kThreads = 512;  // 2 CTAs (rows) per SM: a 256-row batch is one wave
+constexpr int kCluster = 8;      // CTAs per row (the portable cluster size)
+constexpr int kThreads = 256;    // 2 CTAs per SM with a 76 KB slice (V = 151936)
 constexpr int kWarpsPerCta = kThreads / 32;
+constexpr int kChunks = 4;               // bulk copies per staged slice
+constexpr int kMaxStaged = 48 * 1024;    // tokens of a slice kept in shared memory (192 KB)
 constexpr uint64_t kGolden = 0x9E3779B97F4A7C15ull;
 
 __device__ __forceinline__ uint64_t splitmix64_mix(uint64_t z) {
@@ -79,25 +100,27 @@ __device__ __forceinline__ uint64_t weight_of(float e) {
   return sh >= 0 ? mant << sh : (sh > -24 ? mant >> (-sh) : 0ull);
 }
 
-// Calls f(x[i], i) for every i < V owned by this thread: two 16-byte loads
-// in flight per iteration when the row is 16-byte aligned, scalar otherwise.
+// Calls f(src[k], i0 + k) for every k < n owned by this thread: two 16-byte
+// loads in flight per iteration when `vec` (src 16-byte aligned, n a multiple
+// of 4), scalar otherwise.
 template <typename F>
-__device__ __forceinline__ void for_row(const float *x, int V, F &&f) {
-  if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
-    const float4 *x4 = reinterpret_cast<const float4 *>(x);
-    const int n4 = V >> 2;
+__device__ __forceinline__ void for_range(const float *src, int i0, int n, bool vec, F &&f) {
+  if (vec) {
+    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+    const int n4 = n >> 2;
     for (int q = threadIdx.x; q < n4; q += 2 * kThreads) {
       const bool hb = q + kThreads < n4;
-      const float4 a = x4[q];
-      const float4 b = hb ? x4[q + kThreads] : make_float4(0.f, 0.f, 0.f, 0.f);
-      f(a.x, 4 * q); f(a.y, 4 * q + 1); f(a.z, 4 * q + 2); f(a.w, 4 * q + 3);
+      const float4 u = s4[q];
+      const float4 w = hb ? s4[q + kThreads] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int i = i0 + 4 * q;
+      f(u.x, i); f(u.y, i + 1); f(u.z, i + 2); f(u.w, i + 3);
       if (hb) {
-        const int qb = 4 * (q + kThreads);
-        f(b.x, qb); f(b.y, qb + 1); f(b.z, qb + 2); f(b.w, qb + 3);
+        const int j = i + 4 * kThreads;
+        f(w.x, j); f(w.y, j + 1); f(w.z, j + 2); f(w.w, j + 3);
       }
     }
   } else {
-    for (int i = threadIdx.x; i < V; i += kThreads) f(x[i], i);
+    for (int k = threadIdx.x; k < n; k += kThreads) f(src[k], i0 + k);
   }
 }
 
@@ -184,28 +207,87 @@ __device__ Best block_best(Best b, float *redf, int *redi) {
   return r;
 }
 
-__global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
-  __shared__ uint64_t hist[256];
+// One CTA's share of a cluster reduction.
+struct Share {
+  float m;
+  float score;
+  int idx;
+  unsigned flags;
+  uint64_t a, b;
+};
+
+// The shares of all CTAs of the cluster, combined.
+struct Combined {
+  float m;
+  Best best;
+  unsigned flags;
+  uint64_t a, b;
+  uint64_t a_below;  // a summed over the CTAs of lower rank
+};
+
+// Publishes this CTA's share (thread 0 writes it to slot `k & 1`) and returns
+// the combination of every CTA's share; all threads of all CTAs get the same
+// result.  Slots alternate: the slot written by reduction k + 2 was last read
+// before its readers arrived at the cluster barrier of reduction k + 1.
+__device__ Combined cluster_combine(const Share &mine, Share *slots, int &k) {
+  cg::cluster_group cl = cg::this_cluster();
+  Share *slot = slots + (k & 1);
+  ++k;
+  if (threadIdx.x == 0) *slot = mine;
+  cl.sync();  // barrier.cluster arrive (release) + wait (acquire)
+  const unsigned me = cl.block_rank();
+  Combined r{-INFINITY, Best{-INFINITY, 0x7fffffff}, 0u, 0ull, 0ull, 0ull};
+#pragma unroll
+  for (unsigned c = 0; c < unsigned(kCluster); ++c) {
+    const Share v = *cl.map_shared_rank(slot, c);
+    r.m = fmaxf(r.m, v.m);
+    take(r.best, v.score, v.idx);
+    r.flags |= v.flags;
+    r.a += v.a;
+    r.b += v.b;
+    if (c < me) r.a_below += v.a;
+  }
+  return r;
+}
+
+template <bool kStaged>
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 2)
+    sample_kernel(SampleArgs a, int slice) {
+  extern __shared__ __align__(16) float sm[];  // the staged slice: token lo + k at sm[k]
+  __shared__ uint64_t hist[2][256];            // radix pass p uses hist[p & 1]
+  __shared__ uint64_t tot[256];                // the cluster's histogram
   __shared__ uint64_t red64[kWarpsPerCta];
   __shared__ float redf[kWarpsPerCta];
   __shared__ int redi[kWarpsPerCta];
+  __shared__ Share slots[2];
+  __shared__ uint64_t chunk_full[kChunks];
   __shared__ uint64_t sel_above;
   __shared__ int sel_bin;
 
-  const int row = blockIdx.x;
+  cg::cluster_group cl = cg::this_cluster();
+  const int rank = int(cl.block_rank());
+  const int row = blockIdx.x / kCluster;
   const double temp = double(a.temperature[row]);
-  if (!(temp >= 1e-7)) return;  // argmax (LogitsProcessor::new maps these to ArgMax)
+  if (!(temp >= 1e-7)) return;  // argmax (LogitsProcessor::new maps these to ArgMax); every CTA of the row leaves here
   const int V = a.vocab;
   const float *x = a.logits + size_t(row) * V;
+  const int lo = min(V, rank * slice), n = min(V, lo + slice) - lo;
+  const bool vec = (V & 3) == 0 && aligned16(x);  // then lo, the chunks and n are multiples of 4 tokens
+  const float *src = kStaged ? sm : x + lo;       // passes after the first read the slice here
+  const bool svec = kStaged ? (n & 3) == 0 : vec;
   const float inv_t = float(1.0 / temp);
   uint64_t seed = 0;
   if (a.seeds) seed = a.seeds[row];
   else if (a.seed_lo) seed = (uint64_t(a.seed_hi[row]) << 32) | a.seed_lo[row];
-  auto finish = [&](int tok) {
-    if (threadIdx.x == 0) {
+  int red = 0;  // cluster reductions so far
+  // leave with `tok` (>= 0) as the row's token; the barrier keeps this CTA's
+  // shared memory alive until every CTA of the row has read its last share
+  auto leave = [&](int tok) {
+    if (tok >= 0 && rank == 0 && threadIdx.x == 0) {
       a.out[row] = tok;
       if (a.row_slot && a.slot_last) a.slot_last[a.row_slot[row]] = tok;
     }
+    cl.sync();
   };
 
   // 1. max of the scaled logits and the race over every token: token i
@@ -214,17 +296,73 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
   //    token's above m - 3), so the race needs no weights.
   float m = -INFINITY;
   Best best{-INFINITY, 0x7fffffff};
-  for_row(x, V, [&](float xv, int i) {
+  auto race_all = [&](float xv, int i) {
     const float z = scaled(xv, inv_t);
     m = fmaxf(m, z);
     take(best, race_score(z, splitmix_state(seed, i)), i);
-  });
+  };
+  unsigned flags = 0;
+  const int per = ((n + kChunks - 1) / kChunks + 3) & ~3;  // tokens per bulk copy
+  if constexpr (kStaged) {
+    if (vec) {
+      if (threadIdx.x == 0) {
+        for (int c = 0; c < kChunks; ++c) attn::mbar_init(&chunk_full[c], 1);
+        attn::fence_barrier_init();
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        for (int c = 0; c < kChunks; ++c) {
+          const int c0 = min(n, c * per), c1 = min(n, c0 + per);
+          if (c1 > c0) {
+            attn::mbar_expect_tx(&chunk_full[c], uint32_t(c1 - c0) * 4u);
+            attn::bulk_g2s(sm + c0, x + lo + c0, uint32_t(c1 - c0) * 4u, &chunk_full[c]);
+          } else {
+            attn::mbar_arrive(&chunk_full[c]);
+          }
+        }
+      }
+      for (int c = 0; c < kChunks; ++c) {
+        const int c0 = min(n, c * per), c1 = min(n, c0 + per);
+        if (!attn::mbar_wait_bounded(&chunk_full[c], 0)) {
+          flags |= kStatusWaitTimeout;
+          continue;
+        }
+        for_range(sm + c0, lo + c0, c1 - c0, true, race_all);
+      }
+    } else {
+      for (int k = threadIdx.x; k < n; k += kThreads) {
+        const float v = x[lo + k];
+        sm[k] = v;  // read by other threads after the block reductions below
+        race_all(v, lo + k);
+      }
+    }
+  } else {
+    for_range(x + lo, lo, n, vec, race_all);
+  }
   m = block_max(m, redf);
   best = block_best(best, redf, redi);
-  if (!(m > -INFINITY) || !(m < INFINITY) || best.idx == 0x7fffffff) return;  // all -inf / NaN: keep argmax
+  flags = __syncthreads_or(flags) ? kStatusWaitTimeout : 0u;
+  {
+    const Combined r = cluster_combine(Share{m, best.score, best.idx, flags, 0ull, 0ull}, slots, red);
+    if (r.flags) {
+      // a slice copy did not land in time: wait for this CTA's copies once more
+      // (bounded), report, and leave the row's argmax in place
+      if (kStaged && vec && threadIdx.x == 0)
+        for (int c = 0; c < kChunks; ++c) attn::mbar_wait_bounded(&chunk_full[c], 0);
+      if (rank == 0 && threadIdx.x == 0 && a.status) atomicOr(a.status, r.flags);
+      leave(-1);
+      return;
+    }
+    m = r.m;
+    best = r.best;
+  }
+  if (!(m > -INFINITY) || !(m < INFINITY) || best.idx == 0x7fffffff) {  // all -inf / NaN: keep argmax
+    leave(-1);
+    return;
+  }
   const double top_p = a.top_p ? double(a.top_p[row]) : 1.0;
   if (!(top_p > 0.0 && top_p < 1.0)) {
-    finish(best.idx);
+    leave(best.idx);
     return;
   }
 
@@ -245,7 +383,7 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
     const float zlo = iter == 0 ? -INFINITY : zj - 1e-6f * (1.0f + fabsf(zj - m));
     uint64_t w_all = 0, w_before = 0;
     Best next{-INFINITY, 0x7fffffff};
-    for_row(x, V, [&](float xv, int i) {
+    for_range(src, lo, n, svec, [&](float xv, int i) {
       const float z = scaled(xv, inv_t);
       if (z < zlo) return;
       const float e = weight_e(z, m);
@@ -256,15 +394,17 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
         take(next, race_score(z, splitmix_state(seed, i)), i);
       }
     });
-    if (iter == 0) target = uint64_t(ceil(top_p * double(block_sum_u64(w_all, red64))));
-    w_before = block_sum_u64(w_before, red64);
+    const uint64_t wa = iter == 0 ? block_sum_u64(w_all, red64) : 0ull;
+    const uint64_t wb = block_sum_u64(w_before, red64);
     next = block_best(next, redf, redi);
-    if (weight_of(ej) > 0 && w_before < target) {
-      finish(j);
+    const Combined r = cluster_combine(Share{-INFINITY, next.score, next.idx, 0u, wa, wb}, slots, red);
+    if (iter == 0) target = uint64_t(ceil(top_p * double(r.a)));
+    if (weight_of(ej) > 0 && r.b < target) {
+      leave(j);
       return;
     }
-    if (next.idx == 0x7fffffff) break;  // cannot happen: the top token is always kept
-    j = next.idx;
+    if (r.best.idx == 0x7fffffff) break;  // cannot happen: the top token is always kept
+    j = r.best.idx;
   }
 
   // 3. fallback after 8 rejected candidates (rare unless top_p is small):
@@ -275,18 +415,19 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
   {
     uint64_t above = 0;  // mass strictly above the selected key range
     uint32_t prefix = 0, pmask = 0;
-    for (int shift = 24; shift >= 0; shift -= 8) {
-      for (int b = threadIdx.x; b < 256; b += kThreads) hist[b] = 0;
+    for (int shift = 24, hp = 0; shift >= 0; shift -= 8, ++hp) {
+      uint64_t *h = hist[hp & 1];
+      for (int b = threadIdx.x; b < 256; b += kThreads) h[b] = 0;
       __syncthreads();
       // warp-aggregated: lanes that hit the same bin add their weights with
       // two 32-bit reductions (w <= 2^40 splits into 21 + 20 bits), and one
       // lane per bin issues the shared-memory atomic
-      for (int base = 0; base < V; base += kThreads) {
-        const int i = base + threadIdx.x;
+      for (int base = 0; base < n; base += kThreads) {
+        const int k = base + threadIdx.x;
         unsigned bin = 0xffffu;
         uint64_t w = 0;
-        if (i < V) {
-          const float e = weight_e(scaled(x[i], inv_t), m);
+        if (k < n) {
+          const float e = weight_e(scaled(src[k], inv_t), m);
           const uint32_t key = __float_as_uint(e);
           if ((key & pmask) == prefix) {
             w = weight_of(e);
@@ -298,24 +439,33 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
         const uint32_t hs = __reduce_add_sync(peers, uint32_t(w >> 20));
         const uint32_t ls = __reduce_add_sync(peers, uint32_t(w & 0xfffffu));
         if (bin != 0xffffu && int(threadIdx.x & 31) == __ffs(peers) - 1)
-          atomicAdd(reinterpret_cast<unsigned long long *>(&hist[bin]), (uint64_t(hs) << 20) + ls);
+          atomicAdd(reinterpret_cast<unsigned long long *>(&h[bin]), (uint64_t(hs) << 20) + ls);
+      }
+      // every CTA's histogram is complete; h[p & 1] is next cleared two passes
+      // later, after the barrier of the next pass (so after all reads below)
+      cl.sync();
+      for (int b = threadIdx.x; b < 256; b += kThreads) {
+        uint64_t sum = 0;
+#pragma unroll
+        for (int c = 0; c < kCluster; ++c) sum += cl.map_shared_rank(h, c)[b];
+        tot[b] = sum;
       }
       __syncthreads();
       if (threadIdx.x < 32) {  // scan the 256 bins from the top: lane l holds bins 255-8l .. 248-8l
         const int lane = threadIdx.x;
-        uint64_t loc[8], s = 0;
+        uint64_t loc[8], sum = 0;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) { loc[k] = hist[255 - 8 * lane - k]; s += loc[k]; }
-        uint64_t incl = s;
+        for (int k = 0; k < 8; ++k) { loc[k] = tot[255 - 8 * lane - k]; sum += loc[k]; }
+        uint64_t incl = sum;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-          const uint64_t n = __shfl_up_sync(kFull, incl, o);
-          if (lane >= o) incl += n;
+          const uint64_t v = __shfl_up_sync(kFull, incl, o);
+          if (lane >= o) incl += v;
         }
         const unsigned cross = __ballot_sync(kFull, above + incl >= target);
         const int L = cross ? __ffs(cross) - 1 : 31;
         if (lane == L) {
-          uint64_t cum = above + (incl - s);
+          uint64_t cum = above + (incl - sum);
           int sel = 255 - 8 * lane - 7;
           for (int k = 0; k < 8; ++k) {
             if (cum + loc[k] >= target && loc[k] > 0) { sel = 255 - 8 * lane - k; break; }
@@ -332,7 +482,7 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
       if (shift == 0) {
         const uint64_t w_edge = weight_of(__uint_as_float(prefix));
         if (w_edge > 0) {
-          const long long n_ties = (long long)(hist[sel_bin] / w_edge);
+          const long long n_ties = (long long)(tot[sel_bin] / w_edge);
           const uint64_t need = target > above ? target - above : 1;
           const long long c = (long long)((need + w_edge - 1) / w_edge);
           keep_ties = c >= n_ties ? -1 : c;
@@ -344,37 +494,67 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
   }
   best = Best{-INFINITY, 0x7fffffff};
   if (keep_ties < 0) {
-    for_row(x, V, [&](float xv, int i) {
+    for_range(src, lo, n, svec, [&](float xv, int i) {
       const float z = scaled(xv, inv_t);
       const float e = weight_e(z, m);
       if (__float_as_uint(e) < edge || weight_of(e) == 0) return;
       take(best, race_score(z, splitmix_state(seed, i)), i);
     });
   } else {
-    // ties at the edge are kept in index order: contiguous chunks per thread
-    const int per = (V + kThreads - 1) / kThreads;
-    const int i0 = min(V, int(threadIdx.x) * per), i1 = min(V, i0 + per);
+    // ties at the edge are kept in index order: contiguous chunks per thread,
+    // the CTAs' slices in rank order
+    const int cper = (n + kThreads - 1) / kThreads;
+    const int k0 = min(n, int(threadIdx.x) * cper), k1 = min(n, k0 + cper);
     int ties = 0;
-    for (int i = i0; i < i1; ++i) ties += __float_as_uint(weight_e(scaled(x[i], inv_t), m)) == edge;
-    int rank = block_exclusive_count(ties, redi);
-    for (int i = i0; i < i1; ++i) {
-      const float z = scaled(x[i], inv_t);
+    for (int k = k0; k < k1; ++k) ties += __float_as_uint(weight_e(scaled(src[k], inv_t), m)) == edge;
+    const int before_cta = block_exclusive_count(ties, redi);
+    const uint64_t cta_ties = block_sum_u64(uint64_t(ties), red64);
+    const Combined r = cluster_combine(Share{-INFINITY, -INFINITY, 0x7fffffff, 0u, cta_ties, 0ull}, slots, red);
+    long long tie_rank = (long long)r.a_below + before_cta;
+    for (int k = k0; k < k1; ++k) {
+      const float z = scaled(src[k], inv_t);
       const uint32_t key = __float_as_uint(weight_e(z, m));
       if (key < edge) continue;
-      if (key == edge && rank++ >= keep_ties) continue;
-      take(best, race_score(z, splitmix_state(seed, i)), i);
+      if (key == edge && tie_rank++ >= keep_ties) continue;
+      take(best, race_score(z, splitmix_state(seed, lo + k)), lo + k);
     }
   }
   best = block_best(best, redf, redi);
-  if (best.idx != 0x7fffffff) finish(best.idx);
+  const Combined r = cluster_combine(Share{-INFINITY, best.score, best.idx, 0u, 0ull, 0ull}, slots, red);
+  leave(r.best.idx != 0x7fffffff ? r.best.idx : -1);
 }
+
+// Shared memory opt-in for the staged kernel, once per device.
+std::atomic<uint64_t> g_sample_attr_done{0};
 
 }  // namespace
 
 cudaError_t launch_sample(const SampleArgs &a, cudaStream_t st) {
   if (a.rows == 0) return cudaSuccess;
   if (a.rows < 0 || a.vocab <= 0 || !a.logits || !a.temperature || !a.out) return cudaErrorInvalidValue;
-  sample_kernel<<<a.rows, kThreads, 0, st>>>(a);
+  if (a.rows > (1 << 27)) return cudaErrorInvalidValue;
+  SampleArgs b = a;
+  if (!b.status) {
+    cudaError_t e = standalone_status_word(&b.status);
+    if (e != cudaSuccess) return e;
+  }
+  const int slice = ((a.vocab + kCluster - 1) / kCluster + 3) & ~3;
+  const dim3 grid(unsigned(a.rows) * kCluster);
+  if (slice <= kMaxStaged) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = uint64_t(1) << (dev & 63);
+    if (!(g_sample_attr_done.load() & bit)) {
+      e = cudaFuncSetAttribute(sample_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kMaxStaged * int(sizeof(float)));
+      if (e != cudaSuccess) return e;
+      g_sample_attr_done.fetch_or(bit);
+    }
+    sample_kernel<true><<<grid, kThreads, size_t(slice) * sizeof(float), st>>>(b, slice);
+  } else {
+    sample_kernel<false><<<grid, kThreads, 0, st>>>(b, slice);
+  }
   return cudaGetLastError();
 }
 

@@ -7,6 +7,11 @@ engine's step) against the CPU restatements in oracle.sampling_ref.
 * Distribution: over 8192 seeds the draws follow LogitsProcessor's
   distribution (candle.rs:737-763), and no token outside its nucleus appears.
 * Greedy rows (temperature < 1e-7) keep the argmax already in `out`.
+* Row layouts: the kernel splits a row over a cluster of 8 CTAs (slices of
+  ceil(V / 8) rounded up to 4 tokens), kept in shared memory up to 48K tokens
+  per slice, read from global memory beyond; vocabularies that are not a
+  multiple of 4 take the scalar loads; ties at the nucleus edge that fall in
+  different slices are kept in index order across them.
 * In the engine, sampled rows of a step are the restatement's draw from that
   step's logits, eager and replayed from a CUDA graph alike.
 """
@@ -110,6 +115,66 @@ def test_kernel_ties_at_nucleus_edge():
     out = _launch(np.tile(row, (n, 1)), np.ones(n, np.float32), np.full(n, 0.6, np.float32),
                   np.arange(n, dtype=np.uint64), np.zeros(n, np.int32))
     assert set(np.unique(out).tolist()) == {1, 2, 3}  # top token + the first two ties in index order
+
+
+def test_kernel_ties_at_nucleus_edge_across_slices():
+    """V = 64 gives 8-token slices: the four tied tokens sit in four CTAs, and
+    the first two in index order are the kept ones."""
+    need_gpu()
+    row = np.full(64, -30.0, np.float32)
+    row[1] = 2.0
+    for i in (6, 14, 22, 30):
+        row[i] = 1.0
+    row[45] = -1.0
+    n = 4096
+    seeds = np.arange(n, dtype=np.uint64) * 3 + 5
+    out = _launch(np.tile(row, (n, 1)), np.ones(n, np.float32), np.full(n, 0.6, np.float32), seeds,
+                  np.zeros(n, np.int32))
+    assert set(np.unique(out).tolist()) == {1, 6, 14}
+    for r in range(0, n, 97):
+        assert out[r] == sample_like_kernel(row, 1.0, 0.6, int(seeds[r])), r
+
+
+def test_kernel_radix_edge_ties_cross_a_slice_boundary():
+    """Flat tokens from index 510 on (512-token slices at V = 4096) and
+    top_p 0.001: the kept set is the first four ties in index order, 510-513,
+    two in each of CTAs 0 and 1.  The candidate chain needs ~7 rejections on
+    average, so many rows reach the radix path and its cross-slice tie count."""
+    need_gpu()
+    V, n = 4096, 512
+    row = np.zeros(V, np.float32)
+    row[:510] = -30.0
+    seeds = np.arange(n, dtype=np.uint64) * 11 + 3
+    out = _launch(np.tile(row, (n, 1)), np.ones(n, np.float32), np.full(n, 0.001, np.float32), seeds,
+                  np.full(n, -1, np.int32))
+    assert set(np.unique(out).tolist()) <= {510, 511, 512, 513}
+    for r in range(0, n, 7):
+        assert out[r] == sample_like_kernel(row, 1.0, 0.001, int(seeds[r])), r
+
+
+@pytest.mark.parametrize("V", [1001, 4099, 400_000, 400_003])
+def test_kernel_row_layouts_draw_the_restatement(V):
+    """Scalar staging (V not a multiple of 4), and slices too large for shared
+    memory (V > 8 x 48K, read from global memory in every pass), vector and
+    scalar."""
+    need_gpu()
+    rng = np.random.default_rng(V)
+    rows = 6 if V > 100_000 else 24
+    x = (rng.standard_normal((rows, V)) * 2.5).astype(np.float32)
+    temps = rng.uniform(0.5, 1.2, rows).astype(np.float32)
+    tops = np.array([1.0, 0.9, 0.3, 0.02, 0.97, 0.6] * (rows // 6), np.float32)
+    seeds = rng.integers(0, 2 ** 63, rows, dtype=np.uint64)
+    out = _launch(x, temps, tops, seeds, np.full(rows, -1, np.int32))
+    agree = 0
+    for r in range(rows):
+        want = sample_like_kernel(x[r], temps[r], float(tops[r]), int(seeds[r]))
+        if out[r] == want:
+            agree += 1
+        else:
+            assert explains_mismatch(x[r], temps[r], float(tops[r]), int(seeds[r]), int(out[r])), r
+    assert agree >= rows - 1, (agree, rows)
+    st = C.c_uint32(7)
+    assert E.lib().ms_kernel_status(0, C.byref(st)) == 0 and st.value == 0
 
 
 def test_engine_step_samples_like_restatement():
