@@ -516,22 +516,24 @@ __global__ void __launch_bounds__(kThreads5, 1) paged_prefill_tc5_kernel(Prefill
         umma_commit(&empty[0]);
       }
       for (int g = 0; g < ngroups && ok; ++g) {
+        // V(g) and K(g + 1) were copied long before P(g) is ready (their slots were freed by
+        // MMAs of groups g - 2 and g - 1): take both, with the proxy fence for the copies, here
+        // rather than between p_ready and the MMAs
+        if (!wait_tile(min(2 * g + 2, ntiles - 1))) {
+          ok = false;
+          break;
+        }
 #pragma unroll
         for (int h = 0; h < kHalves && ok; ++h) {
           if (g < ng[h]) {
-            if (!wait_or_abort(&p_ready[h], g & 1, &abort_s) || !wait_tile(2 * g + 1)) {
+            if (!wait_or_abort(&p_ready[h], g & 1, &abort_s)) {
               ok = false;
               break;
             }
+            tc_fence_after();
             issue_pv(h, g);
           }
-          if (g + 1 < ng[h]) {
-            if (!wait_tile(2 * g + 2)) {
-              ok = false;
-              break;
-            }
-            issue_s(h, g + 1);
-          }
+          if (g + 1 < ng[h]) issue_s(h, g + 1);
         }
         if (!ok) break;
         umma_commit(&empty[(2 * g + 1) % NSLOT]);                      // V(g): its PVs are issued
