@@ -414,8 +414,9 @@ int ms_prefill_tiles(const int32_t *seq_row0, const int32_t *seq_ntok, const int
                      int32_t num_kv_heads, int32_t *tiles_out, int32_t capacity);
 
 /* Status of the kernels launched without an engine on `device`: the
- * prototype-compatible launchers below, and ms_launch_paged_attention /
- * ms_launch_paged_prefill (which use it when their own status word is NULL).
+ * prototype-compatible launchers below, ms_launch_sample, and
+ * ms_launch_paged_attention / ms_launch_paged_prefill (which use it when their
+ * own status word is NULL).
  * Synchronises the device, returns the OR of the kernels' status bits since
  * the last call (1 = a bounded wait ran out and the kernel returned without
  * writing its output, 2 = an index out of range) and clears them.  No
@@ -433,7 +434,10 @@ int ms_test_set_attention_wait_limit(int32_t polls);
  * LogitsProcessor draws it (softmax of logits / temperature, top-p nucleus
  * when 0 < top_p[row] < 1, ties at the nucleus edge kept in index order) from
  * a counter-based stream seeded by seeds[row]; rows below 1e-7 are left as
- * they are in out (run ms_launch_argmax first).  top_p and seeds may be NULL. */
+ * they are in out (run ms_launch_argmax first).  top_p and seeds may be NULL.
+ * Each row runs on a cluster of 8 CTAs; a staging copy that does not land in
+ * time leaves the row's out untouched and sets bit 1 of the status word that
+ * ms_kernel_status returns. */
 int ms_launch_sample(const float *logits, int32_t rows, int32_t vocab, const float *temperature,
                      const float *top_p, const uint64_t *seeds, int32_t *out, void *stream);
 
