@@ -67,20 +67,18 @@ constexpr int kChunks = 4;               // bulk copies per staged slice
 constexpr int kMaxStaged = 48 * 1024;    // tokens of a slice kept in shared memory (192 KB)
 constexpr uint64_t kGolden = 0x9E3779B97F4A7C15ull;
 
-__device__ __forceinline__ uint64_t splitmix64_mix(uint64_t z) {
-  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
-  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
-  return z ^ (z >> 31);
-}
-
-// SplitMix64 state of token i: seed + (i + 1) * golden (advanced by
-// kThreads * golden per strided iteration).
+// SplitMix64 state of token i: seed + (i + 1) * golden.
 __device__ __forceinline__ uint64_t splitmix_state(uint64_t seed, int i) { return seed + (uint64_t(i) + 1) * kGolden; }
 
 // Uniform in (0, 1): the top 24 bits of the SplitMix64 output, centred.
-__device__ __forceinline__ float uniform_open(uint64_t state) {
-  const uint64_t z = splitmix64_mix(state);
-  return (float(uint32_t(z >> 40)) + 0.5f) * (1.0f / 16777216.0f);
+// Only bits 40-63 are used, and the mix's last step (z ^= z >> 31) leaves
+// them as they are, so it is skipped.  (k + 0.5) * 2^-24 is one FMA: scaling
+// by a power of two commutes with rounding to nearest, so k * 2^-24 + 2^-25
+// rounds to the same float as (float(k) + 0.5f) * 2^-24.
+__device__ __forceinline__ float uniform_open(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return fmaf(float(uint32_t(z >> 40)), 1.0f / 16777216.0f, 1.0f / 33554432.0f);
 }
 
 // z = x * (1 / T) rounded on its own (never fused into a later add), so
