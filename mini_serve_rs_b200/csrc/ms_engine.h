@@ -192,6 +192,7 @@ struct StepPlan {
   int S = 0, T = 0, nd = 0;  // sequences, packed tokens, block-table deltas
   int n_dec = 0;             // rows run by the decode kernel (row list uploaded when tiles are used)
   int n_tiles = 0;           // prefill tiles (tensor-core path only)
+  bool nucleus = false;      // some sampled row has 0 < top_p < 1 (always set for a graph step)
   int max_ctx_dec = 0;
   long long blocks_dec = 0;  // sum over decode rows of pages read
   double ctx_dec = 0.0;      // sum over decode rows of keys read

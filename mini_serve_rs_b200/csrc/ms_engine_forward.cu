@@ -244,7 +244,7 @@ int enqueue_forward(Engine *eng, const StepPlan &plan) {
     sa.rows = S;
     sa.vocab = eng->V;
     sa.temperature = reinterpret_cast<const float *>(samp);
-    sa.top_p = reinterpret_cast<const float *>(samp + S);
+    sa.top_p = plan.nucleus ? reinterpret_cast<const float *>(samp + S) : nullptr;  // null: one pass suffices
     sa.seed_lo = reinterpret_cast<const uint32_t *>(samp + 2 * S);
     sa.seed_hi = reinterpret_cast<const uint32_t *>(samp + 3 * S);
     sa.out = eng->d_next;

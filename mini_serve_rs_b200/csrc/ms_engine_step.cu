@@ -258,6 +258,7 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
   if (g) {
     sp.graph = true;
     sp.sample = true;
+    sp.nucleus = true;  // the captured launch serves whatever top-p a replay brings
     sp.hdr = 4;
     sp.delta_cap = S;
     sp.max_ctx_launch = g->max_ctx_cap;
@@ -291,6 +292,7 @@ int step_launch_impl(Engine *eng, const ms_step_desc *desc) {
       const int o = plan[i].orig;
       temp[i] = desc->temperature ? desc->temperature[o] : 0.f;
       topp[i] = desc->top_p ? desc->top_p[o] : 1.f;
+      if (double(temp[i]) >= 1e-7 && topp[i] > 0.f && topp[i] < 1.f) sp.nucleus = true;
       const uint64_t sd = desc->seeds ? desc->seeds[o] : 0ull;
       slo[i] = uint32_t(sd);
       shi[i] = uint32_t(sd >> 32);

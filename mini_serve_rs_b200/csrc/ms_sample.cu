@@ -47,6 +47,8 @@
 // sums do not depend on the order of combination, so the token drawn does
 // not depend on how the row is split.  A copy that never lands (a bounded
 // wait that runs out) sets kStatusWaitTimeout and leaves the row's argmax.
+// A launch without top-p values has no nucleus row, so pass 1 is its only
+// pass: it runs one CTA per row over global memory, with nothing to stage.
 #include <cooperative_groups.h>
 
 #include <atomic>
@@ -227,6 +229,7 @@ struct Combined {
 // the combination of every CTA's share; all threads of all CTAs get the same
 // result.  Slots alternate: the slot written by reduction k + 2 was last read
 // before its readers arrived at the cluster barrier of reduction k + 1.
+template <int C>
 __device__ Combined cluster_combine(const Share &mine, Share *slots, int &k) {
   cg::cluster_group cl = cg::this_cluster();
   Share *slot = slots + (k & 1);
@@ -236,7 +239,7 @@ __device__ Combined cluster_combine(const Share &mine, Share *slots, int &k) {
   const unsigned me = cl.block_rank();
   Combined r{-INFINITY, Best{-INFINITY, 0x7fffffff}, 0u, 0ull, 0ull, 0ull};
 #pragma unroll
-  for (unsigned c = 0; c < unsigned(kCluster); ++c) {
+  for (unsigned c = 0; c < unsigned(C); ++c) {
     const Share v = *cl.map_shared_rank(slot, c);
     r.m = fmaxf(r.m, v.m);
     take(r.best, v.score, v.idx);
@@ -248,8 +251,11 @@ __device__ Combined cluster_combine(const Share &mine, Share *slots, int &k) {
   return r;
 }
 
-template <bool kStaged>
-__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 2)
+// C CTAs per row: kCluster with the row staged in shared memory (kStaged) or
+// read from global memory in every pass; 1 (unstaged) for launches that the
+// host knows have no nucleus row, where pass 1 is the only pass.
+template <bool kStaged, int C>
+__global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads, 2)
     sample_kernel(SampleArgs a, int slice) {
   extern __shared__ __align__(16) float sm[];  // the staged slice: token lo + k at sm[k]
   __shared__ uint64_t hist[2][256];            // radix pass p uses hist[p & 1]
@@ -264,7 +270,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 2)
 
   cg::cluster_group cl = cg::this_cluster();
   const int rank = int(cl.block_rank());
-  const int row = blockIdx.x / kCluster;
+  const int row = blockIdx.x / C;
   const double temp = double(a.temperature[row]);
   if (!(temp >= 1e-7)) return;  // argmax (LogitsProcessor::new maps these to ArgMax); every CTA of the row leaves here
   const int V = a.vocab;
@@ -341,7 +347,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 2)
   best = block_best(best, redf, redi);
   flags = __syncthreads_or(flags) ? kStatusWaitTimeout : 0u;
   {
-    const Combined r = cluster_combine(Share{m, best.score, best.idx, flags, 0ull, 0ull}, slots, red);
+    const Combined r = cluster_combine<C>(Share{m, best.score, best.idx, flags, 0ull, 0ull}, slots, red);
     if (r.flags) {
       // a slice copy did not land in time: wait for this CTA's copies once more
       // (bounded), report, and leave the row's argmax in place
@@ -395,7 +401,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 2)
     const uint64_t wa = iter == 0 ? block_sum_u64(w_all, red64) : 0ull;
     const uint64_t wb = block_sum_u64(w_before, red64);
     next = block_best(next, redf, redi);
-    const Combined r = cluster_combine(Share{-INFINITY, next.score, next.idx, 0u, wa, wb}, slots, red);
+    const Combined r = cluster_combine<C>(Share{-INFINITY, next.score, next.idx, 0u, wa, wb}, slots, red);
     if (iter == 0) target = uint64_t(ceil(top_p * double(r.a)));
     if (weight_of(ej) > 0 && r.b < target) {
       leave(j);
@@ -445,7 +451,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 2)
       for (int b = threadIdx.x; b < 256; b += kThreads) {
         uint64_t sum = 0;
 #pragma unroll
-        for (int c = 0; c < kCluster; ++c) sum += cl.map_shared_rank(h, c)[b];
+        for (int c = 0; c < C; ++c) sum += cl.map_shared_rank(h, c)[b];
         tot[b] = sum;
       }
       __syncthreads();
@@ -507,7 +513,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 2)
     for (int k = k0; k < k1; ++k) ties += __float_as_uint(weight_e(scaled(src[k], inv_t), m)) == edge;
     const int before_cta = block_exclusive_count(ties, redi);
     const uint64_t cta_ties = block_sum_u64(uint64_t(ties), red64);
-    const Combined r = cluster_combine(Share{-INFINITY, -INFINITY, 0x7fffffff, 0u, cta_ties, 0ull}, slots, red);
+    const Combined r = cluster_combine<C>(Share{-INFINITY, -INFINITY, 0x7fffffff, 0u, cta_ties, 0ull}, slots, red);
     long long tie_rank = (long long)r.a_below + before_cta;
     for (int k = k0; k < k1; ++k) {
       const float z = scaled(src[k], inv_t);
@@ -518,7 +524,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads, 2)
     }
   }
   best = block_best(best, redf, redi);
-  const Combined r = cluster_combine(Share{-INFINITY, best.score, best.idx, 0u, 0ull, 0ull}, slots, red);
+  const Combined r = cluster_combine<C>(Share{-INFINITY, best.score, best.idx, 0u, 0ull, 0ull}, slots, red);
   leave(r.best.idx != 0x7fffffff ? r.best.idx : -1);
 }
 
@@ -536,6 +542,10 @@ cudaError_t launch_sample(const SampleArgs &a, cudaStream_t st) {
     cudaError_t e = standalone_status_word(&b.status);
     if (e != cudaSuccess) return e;
   }
+  if (!a.top_p) {  // no nucleus row: one CTA per row, one pass over the logits in global memory
+    sample_kernel<false, 1><<<unsigned(a.rows), kThreads, 0, st>>>(b, (a.vocab + 3) & ~3);
+    return cudaGetLastError();
+  }
   const int slice = ((a.vocab + kCluster - 1) / kCluster + 3) & ~3;
   const dim3 grid(unsigned(a.rows) * kCluster);
   if (slice <= kMaxStaged) {
@@ -544,14 +554,14 @@ cudaError_t launch_sample(const SampleArgs &a, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     const uint64_t bit = uint64_t(1) << (dev & 63);
     if (!(g_sample_attr_done.load() & bit)) {
-      e = cudaFuncSetAttribute(sample_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      e = cudaFuncSetAttribute(sample_kernel<true, kCluster>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                kMaxStaged * int(sizeof(float)));
       if (e != cudaSuccess) return e;
       g_sample_attr_done.fetch_or(bit);
     }
-    sample_kernel<true><<<grid, kThreads, size_t(slice) * sizeof(float), st>>>(b, slice);
+    sample_kernel<true, kCluster><<<grid, kThreads, size_t(slice) * sizeof(float), st>>>(b, slice);
   } else {
-    sample_kernel<false><<<grid, kThreads, 0, st>>>(b, slice);
+    sample_kernel<false, kCluster><<<grid, kThreads, 0, st>>>(b, slice);
   }
   return cudaGetLastError();
 }

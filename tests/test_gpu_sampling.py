@@ -72,6 +72,30 @@ def test_kernel_draws_equal_restatement():
     assert agree >= rows - 1, (agree, rows)
 
 
+def test_kernel_without_top_p_runs_one_pass_and_draws_the_restatement():
+    """top_p NULL: the launch has no nucleus row, so it runs one CTA per row
+    over global memory; the draw is the race winner over every token."""
+    need_gpu()
+    rng = np.random.default_rng(8)
+    rows, V = 40, 151936
+    x = (rng.standard_normal((rows, V)) * 3).astype(np.float32)
+    temps = rng.uniform(0.3, 1.5, rows).astype(np.float32)
+    temps[::7] = 0.0  # greedy rows
+    seeds = rng.integers(0, 2 ** 63, rows, dtype=np.uint64)
+    out = _launch(x, temps, None, seeds, np.full(rows, -7, np.int32))
+    agree = 0
+    for r in range(rows):
+        want = sample_like_kernel(x[r], temps[r], None, int(seeds[r]))
+        if want is None:
+            assert out[r] == -7, r
+            agree += 1
+        elif out[r] == want:
+            agree += 1
+        else:
+            assert explains_mismatch(x[r], temps[r], None, int(seeds[r]), int(out[r])), r
+    assert agree >= rows - 1, (agree, rows)
+
+
 def test_kernel_small_top_p_takes_the_radix_path_and_still_agrees():
     """Flat rows with top_p 0.05: most rows reject 8 race candidates and fall
     back to the radix-select edge; the draw must still be the restatement's."""
@@ -177,7 +201,8 @@ def test_kernel_row_layouts_draw_the_restatement(V):
     assert E.lib().ms_kernel_status(0, C.byref(st)) == 0 and st.value == 0
 
 
-def test_engine_step_samples_like_restatement():
+@pytest.mark.parametrize("tops", [(1.0, 0.9, 0.5, 1.0), (1.0, 1.0, 1.0, 1.0)])
+def test_engine_step_samples_like_restatement(tops):
     need_gpu()
     case = MODEL_CASES[1]
     cfg = case["cfg"]
@@ -189,7 +214,7 @@ def test_engine_step_samples_like_restatement():
     for k, sid in enumerate(ids):
         eng.admit(sid, list(rng.integers(0, cfg.vocab_size, 10 + 7 * k)), list(range(8 * k, 8 * k + 8)))
     temps = np.array([0.0, 0.8, 1.2, 0.0], np.float32)
-    tops = np.array([1.0, 0.9, 0.5, 1.0], np.float32)
+    tops = np.array(tops, np.float32)  # all 1.0: eager steps launch the one-pass sampler
     checked = 0
     for step in range(12):  # prefill, an eager decode, a captured one, then graph replays
         seeds = np.array([11, 1000 + step, 2000 + step, 13], np.uint64)
