@@ -109,9 +109,11 @@ class ClockSampler:
     def __init__(self, device_index: int):
         self.dev = device_index
         self.proc = None
-        self.lines = []
+        self.lines = []  # (arrival time, csv line)
+        self.t_start = self.t_stop = 0.0
 
     def __enter__(self):
+        import time
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
@@ -120,14 +122,34 @@ class ClockSampler:
             self.t.start()
         except (OSError, FileNotFoundError):
             self.proc = None
+        # nvidia-smi takes a moment to start: wait (at most 5 s) for its first sample, so that a
+        # timed region shorter than that is still covered; samples before this point are dropped
+        deadline = time.time() + 5.0
+        while self.proc is not None and not self.lines and time.time() < deadline:
+            time.sleep(0.01)
+        self.t_start = time.time()
         return self
 
+    def begin(self):
+        """Mark the start of the timed region (after a barrier that follows __enter__)."""
+        import time
+        self.t_start = time.time()
+
     def _read(self):
+        import time
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
 
     def __exit__(self, *a):
+        import time
+        self.t_stop = time.time()
         if self.proc:
+            # a timed region can be shorter than the 100 ms interval: wait for the next sample,
+            # used only if none arrived inside the region
+            n = len(self.lines)
+            deadline = time.time() + 1.0
+            while len(self.lines) == n and time.time() < deadline:
+                time.sleep(0.005)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -137,7 +159,10 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        inside = [ln for t, ln in self.lines if self.t_start <= t <= self.t_stop]
+        if not inside:
+            inside = [ln for t, ln in self.lines if t > self.t_stop][:1]
+        for ln in inside:
             parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -322,10 +347,11 @@ def run_decode(args, rank, world, local, cfg, ctx, seed, tp_rank=0, tp_size=1, c
     # ---- value: device-resident inputs (decode tokens fed back on the device);
     # pure-decode steps replay a captured CUDA graph (captured during warm-up)
     launches0 = eng.profile()[0]
-    barrier()
-    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with ClockSampler(local) as clk:  # started before the barrier: its start-up skews no rank
+        barrier()
+        torch.cuda.synchronize()
+        clk.begin()
         e0.record(stream)
         for _ in range(K):
             eng.step_launch(ids, None, None, E.MS_STEP_TOKENS_FROM_DEVICE)
