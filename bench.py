@@ -610,6 +610,7 @@ def run_config4(args, rank, world, local):
             routing["unrouted"] = len(disp.failed)
         summ = summarize(loop.finished, elapsed)
         summ["steps"] = loop.steps
+        summ["engine_s"], summ["host_step_s"] = loop.engine_s, loop.host_s
         if world > 1:
             dist.barrier()  # the store's host (rank 0) outlives every client
         del store, dstore, master

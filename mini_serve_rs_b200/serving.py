@@ -64,6 +64,8 @@ class ServingLoop:
         self.active: List[Request] = []
         self.finished: List[Request] = []
         self.steps = 0
+        self.engine_s = 0.0  # wall time inside the engine's step call (launch + device work + wait)
+        self.host_s = 0.0    # wall time of the rest of step(): admission, page growth, bookkeeping
         self.latency = LatencyWindow()  # scheduler.rs:543-550, read by the router
 
     def submit(self, r: Request):
@@ -143,6 +145,7 @@ class ServingLoop:
 
     def step(self, now: float) -> bool:
         """One iteration at trace time `now`; False when there was nothing to run."""
+        t_in = time.perf_counter()
         self._admit(now)
         if not self.active:
             return False
@@ -152,11 +155,14 @@ class ServingLoop:
         ids = [r.rid for r in self.active]
         temps = [r.temperature for r in self.active]
         need_sampling = any(t >= 1e-7 for t in temps)
+        t_eng = time.perf_counter()
         toks, flags = self.eng.step(
             ids, flags=E.MS_STEP_TOKENS_FROM_DEVICE, token_budget=self.token_budget,
             temperature=temps if need_sampling else None,
             top_p=[r.top_p for r in self.active] if need_sampling else None,
             seeds=[(r.seed << 20) + len(r.out) for r in self.active] if need_sampling else None)
+        t_out = time.perf_counter()
+        self.engine_s += t_out - t_eng
         self.steps += 1
         t = self.clock()
         done = []
@@ -174,6 +180,7 @@ class ServingLoop:
         for r in done:
             self.active.remove(r)
             self._finish(r, t)
+        self.host_s += (t_eng - t_in) + (time.perf_counter() - t_out)
         return True
 
     # trace clock: seconds since run() started
