@@ -255,6 +255,11 @@ def test_error_paths_and_quarantine():
     eng.step([3])
     with pytest.raises(E.BackendError, match="block table too short"):
         eng.step([3], [5], [16])
+    # an empty batch is a no-op (candle.rs:381-383); a sequence listed twice is a contract error
+    toks, flags = eng.step([])
+    assert len(toks) == 0 and len(flags) == 0
+    with pytest.raises(E.BackendError, match="listed twice"):
+        eng.step([1, 1], [4, 4], [3, 3])
     assert eng.is_healthy()  # contract errors do not quarantine the engine
     # injected device-side failure (host-injected, no GPU fault): quarantine
     eng.inject_fault()
