@@ -63,8 +63,8 @@ namespace {
 namespace cg = cooperative_groups;
 
 constexpr int kCluster = 8;      // CTAs per row (the portable cluster size)
-constexpr int kThreads = 256;    // 2 CTAs per SM with a 76 KB slice (V = 151936)
-constexpr int kWarpsPerCta = kThreads / 32;
+constexpr int kThreads = 256;         // cluster launches: 2 CTAs per SM with a 76 KB slice (V = 151936)
+constexpr int kThreadsOnePass = 512;  // one CTA per row (no nucleus row in the launch)
 constexpr int kChunks = 4;               // bulk copies per staged slice
 constexpr int kMaxStaged = 48 * 1024;    // tokens of a slice kept in shared memory (192 KB)
 constexpr uint64_t kGolden = 0x9E3779B97F4A7C15ull;
@@ -103,24 +103,24 @@ __device__ __forceinline__ uint64_t weight_of(float e) {
 // Calls f(src[k], i0 + k) for every k < n owned by this thread: two 16-byte
 // loads in flight per iteration when `vec` (src 16-byte aligned, n a multiple
 // of 4), scalar otherwise.
-template <typename F>
+template <int NT, typename F>
 __device__ __forceinline__ void for_range(const float *src, int i0, int n, bool vec, F &&f) {
   if (vec) {
     const float4 *s4 = reinterpret_cast<const float4 *>(src);
     const int n4 = n >> 2;
-    for (int q = threadIdx.x; q < n4; q += 2 * kThreads) {
-      const bool hb = q + kThreads < n4;
+    for (int q = threadIdx.x; q < n4; q += 2 * NT) {
+      const bool hb = q + NT < n4;
       const float4 u = s4[q];
-      const float4 w = hb ? s4[q + kThreads] : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 w = hb ? s4[q + NT] : make_float4(0.f, 0.f, 0.f, 0.f);
       const int i = i0 + 4 * q;
       f(u.x, i); f(u.y, i + 1); f(u.z, i + 2); f(u.w, i + 3);
       if (hb) {
-        const int j = i + 4 * kThreads;
+        const int j = i + 4 * NT;
         f(w.x, j); f(w.y, j + 1); f(w.z, j + 2); f(w.w, j + 3);
       }
     }
   } else {
-    for (int k = threadIdx.x; k < n; k += kThreads) f(src[k], i0 + k);
+    for (int k = threadIdx.x; k < n; k += NT) f(src[k], i0 + k);
   }
 }
 
@@ -140,24 +140,26 @@ __device__ __forceinline__ void take(Best &b, float s, int i) {
   if (s > b.score || (s == b.score && i < b.idx)) { b.score = s; b.idx = i; }
 }
 
+template <int NT>
 __device__ float block_max(float v, float *red) {
   v = warp_max(v);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) red[warp] = v;
   __syncthreads();
-  float t = lane < kWarpsPerCta ? red[lane] : -INFINITY;
+  float t = lane < NT / 32 ? red[lane] : -INFINITY;
   t = warp_max(t);
   __syncthreads();
   return t;
 }
 
+template <int NT>
 __device__ uint64_t block_sum_u64(uint64_t v, uint64_t *red) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) red[warp] = v;
   __syncthreads();
-  uint64_t t = lane < kWarpsPerCta ? red[lane] : 0ull;
+  uint64_t t = lane < NT / 32 ? red[lane] : 0ull;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(kFull, t, o);
   __syncthreads();
@@ -165,6 +167,7 @@ __device__ uint64_t block_sum_u64(uint64_t v, uint64_t *red) {
 }
 
 // Exclusive prefix over threads (thread order) of a per-thread count.
+template <int NT>
 __device__ int block_exclusive_count(int v, int *red) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int incl = v;
@@ -176,14 +179,14 @@ __device__ int block_exclusive_count(int v, int *red) {
   if (lane == 31) red[warp] = incl;
   __syncthreads();
   if (warp == 0) {
-    const int w = lane < kWarpsPerCta ? red[lane] : 0;
+    const int w = lane < NT / 32 ? red[lane] : 0;
     int wi = w;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int n = __shfl_up_sync(kFull, wi, o);
       if (lane >= o) wi += n;
     }
-    if (lane < kWarpsPerCta) red[lane] = wi - w;
+    if (lane < NT / 32) red[lane] = wi - w;
   }
   __syncthreads();
   const int r = red[warp] + incl - v;
@@ -193,6 +196,7 @@ __device__ int block_exclusive_count(int v, int *red) {
 
 // Block argmax of (score, index), ties to the lowest index; every thread
 // returns the result.
+template <int NT>
 __device__ Best block_best(Best b, float *redf, int *redi) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) take(b, __shfl_xor_sync(kFull, b.score, o), __shfl_xor_sync(kFull, b.idx, o));
@@ -200,7 +204,7 @@ __device__ Best block_best(Best b, float *redf, int *redi) {
   if (lane == 0) { redf[warp] = b.score; redi[warp] = b.idx; }
   __syncthreads();
   Best r{-INFINITY, 0x7fffffff};
-  if (lane < kWarpsPerCta) { r.score = redf[lane]; r.idx = redi[lane]; }
+  if (lane < NT / 32) { r.score = redf[lane]; r.idx = redi[lane]; }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) take(r, __shfl_xor_sync(kFull, r.score, o), __shfl_xor_sync(kFull, r.idx, o));
   __syncthreads();
@@ -254,15 +258,15 @@ __device__ Combined cluster_combine(const Share &mine, Share *slots, int &k) {
 // C CTAs per row: kCluster with the row staged in shared memory (kStaged) or
 // read from global memory in every pass; 1 (unstaged) for launches that the
 // host knows have no nucleus row, where pass 1 is the only pass.
-template <bool kStaged, int C>
-__global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads, 2)
+template <bool kStaged, int C, int NT>
+__global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(NT, 2)
     sample_kernel(SampleArgs a, int slice) {
   extern __shared__ __align__(16) float sm[];  // the staged slice: token lo + k at sm[k]
   __shared__ uint64_t hist[2][256];            // radix pass p uses hist[p & 1]
   __shared__ uint64_t tot[256];                // the cluster's histogram
-  __shared__ uint64_t red64[kWarpsPerCta];
-  __shared__ float redf[kWarpsPerCta];
-  __shared__ int redi[kWarpsPerCta];
+  __shared__ uint64_t red64[NT / 32];
+  __shared__ float redf[NT / 32];
+  __shared__ int redi[NT / 32];
   __shared__ Share slots[2];
   __shared__ uint64_t chunk_full[kChunks];
   __shared__ uint64_t sel_above;
@@ -331,20 +335,20 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads, 2)
           flags |= kStatusWaitTimeout;
           continue;
         }
-        for_range(sm + c0, lo + c0, c1 - c0, true, race_all);
+        for_range<NT>(sm + c0, lo + c0, c1 - c0, true, race_all);
       }
     } else {
-      for (int k = threadIdx.x; k < n; k += kThreads) {
+      for (int k = threadIdx.x; k < n; k += NT) {
         const float v = x[lo + k];
         sm[k] = v;  // read by other threads after the block reductions below
         race_all(v, lo + k);
       }
     }
   } else {
-    for_range(x + lo, lo, n, vec, race_all);
+    for_range<NT>(x + lo, lo, n, vec, race_all);
   }
-  m = block_max(m, redf);
-  best = block_best(best, redf, redi);
+  m = block_max<NT>(m, redf);
+  best = block_best<NT>(best, redf, redi);
   flags = __syncthreads_or(flags) ? kStatusWaitTimeout : 0u;
   {
     const Combined r = cluster_combine<C>(Share{m, best.score, best.idx, flags, 0ull, 0ull}, slots, red);
@@ -387,7 +391,7 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads, 2)
     const float zlo = iter == 0 ? -INFINITY : zj - 1e-6f * (1.0f + fabsf(zj - m));
     uint64_t w_all = 0, w_before = 0;
     Best next{-INFINITY, 0x7fffffff};
-    for_range(src, lo, n, svec, [&](float xv, int i) {
+    for_range<NT>(src, lo, n, svec, [&](float xv, int i) {
       const float z = scaled(xv, inv_t);
       if (z < zlo) return;
       const float e = weight_e(z, m);
@@ -398,9 +402,9 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads, 2)
         take(next, race_score(z, splitmix_state(seed, i)), i);
       }
     });
-    const uint64_t wa = iter == 0 ? block_sum_u64(w_all, red64) : 0ull;
-    const uint64_t wb = block_sum_u64(w_before, red64);
-    next = block_best(next, redf, redi);
+    const uint64_t wa = iter == 0 ? block_sum_u64<NT>(w_all, red64) : 0ull;
+    const uint64_t wb = block_sum_u64<NT>(w_before, red64);
+    next = block_best<NT>(next, redf, redi);
     const Combined r = cluster_combine<C>(Share{-INFINITY, next.score, next.idx, 0u, wa, wb}, slots, red);
     if (iter == 0) target = uint64_t(ceil(top_p * double(r.a)));
     if (weight_of(ej) > 0 && r.b < target) {
@@ -421,12 +425,12 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads, 2)
     uint32_t prefix = 0, pmask = 0;
     for (int shift = 24, hp = 0; shift >= 0; shift -= 8, ++hp) {
       uint64_t *h = hist[hp & 1];
-      for (int b = threadIdx.x; b < 256; b += kThreads) h[b] = 0;
+      for (int b = threadIdx.x; b < 256; b += NT) h[b] = 0;
       __syncthreads();
       // warp-aggregated: lanes that hit the same bin add their weights with
       // two 32-bit reductions (w <= 2^40 splits into 21 + 20 bits), and one
       // lane per bin issues the shared-memory atomic
-      for (int base = 0; base < n; base += kThreads) {
+      for (int base = 0; base < n; base += NT) {
         const int k = base + threadIdx.x;
         unsigned bin = 0xffffu;
         uint64_t w = 0;
@@ -448,7 +452,7 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads, 2)
       // every CTA's histogram is complete; h[p & 1] is next cleared two passes
       // later, after the barrier of the next pass (so after all reads below)
       cl.sync();
-      for (int b = threadIdx.x; b < 256; b += kThreads) {
+      for (int b = threadIdx.x; b < 256; b += NT) {
         uint64_t sum = 0;
 #pragma unroll
         for (int c = 0; c < C; ++c) sum += cl.map_shared_rank(h, c)[b];
@@ -498,7 +502,7 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads, 2)
   }
   best = Best{-INFINITY, 0x7fffffff};
   if (keep_ties < 0) {
-    for_range(src, lo, n, svec, [&](float xv, int i) {
+    for_range<NT>(src, lo, n, svec, [&](float xv, int i) {
       const float z = scaled(xv, inv_t);
       const float e = weight_e(z, m);
       if (__float_as_uint(e) < edge || weight_of(e) == 0) return;
@@ -507,12 +511,12 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads, 2)
   } else {
     // ties at the edge are kept in index order: contiguous chunks per thread,
     // the CTAs' slices in rank order
-    const int cper = (n + kThreads - 1) / kThreads;
+    const int cper = (n + NT - 1) / NT;
     const int k0 = min(n, int(threadIdx.x) * cper), k1 = min(n, k0 + cper);
     int ties = 0;
     for (int k = k0; k < k1; ++k) ties += __float_as_uint(weight_e(scaled(src[k], inv_t), m)) == edge;
-    const int before_cta = block_exclusive_count(ties, redi);
-    const uint64_t cta_ties = block_sum_u64(uint64_t(ties), red64);
+    const int before_cta = block_exclusive_count<NT>(ties, redi);
+    const uint64_t cta_ties = block_sum_u64<NT>(uint64_t(ties), red64);
     const Combined r = cluster_combine<C>(Share{-INFINITY, -INFINITY, 0x7fffffff, 0u, cta_ties, 0ull}, slots, red);
     long long tie_rank = (long long)r.a_below + before_cta;
     for (int k = k0; k < k1; ++k) {
@@ -523,7 +527,7 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kThreads, 2)
       take(best, race_score(z, splitmix_state(seed, lo + k)), lo + k);
     }
   }
-  best = block_best(best, redf, redi);
+  best = block_best<NT>(best, redf, redi);
   const Combined r = cluster_combine<C>(Share{-INFINITY, best.score, best.idx, 0u, 0ull, 0ull}, slots, red);
   leave(r.best.idx != 0x7fffffff ? r.best.idx : -1);
 }
@@ -543,7 +547,7 @@ cudaError_t launch_sample(const SampleArgs &a, cudaStream_t st) {
     if (e != cudaSuccess) return e;
   }
   if (!a.top_p) {  // no nucleus row: one CTA per row, one pass over the logits in global memory
-    sample_kernel<false, 1><<<unsigned(a.rows), kThreads, 0, st>>>(b, (a.vocab + 3) & ~3);
+    sample_kernel<false, 1, kThreadsOnePass><<<unsigned(a.rows), kThreadsOnePass, 0, st>>>(b, (a.vocab + 3) & ~3);
     return cudaGetLastError();
   }
   const int slice = ((a.vocab + kCluster - 1) / kCluster + 3) & ~3;
@@ -554,14 +558,14 @@ cudaError_t launch_sample(const SampleArgs &a, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     const uint64_t bit = uint64_t(1) << (dev & 63);
     if (!(g_sample_attr_done.load() & bit)) {
-      e = cudaFuncSetAttribute(sample_kernel<true, kCluster>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      e = cudaFuncSetAttribute(sample_kernel<true, kCluster, kThreads>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                kMaxStaged * int(sizeof(float)));
       if (e != cudaSuccess) return e;
       g_sample_attr_done.fetch_or(bit);
     }
-    sample_kernel<true, kCluster><<<grid, kThreads, size_t(slice) * sizeof(float), st>>>(b, slice);
+    sample_kernel<true, kCluster, kThreads><<<grid, kThreads, size_t(slice) * sizeof(float), st>>>(b, slice);
   } else {
-    sample_kernel<false, kCluster><<<grid, kThreads, 0, st>>>(b, slice);
+    sample_kernel<false, kCluster, kThreads><<<grid, kThreads, 0, st>>>(b, slice);
   }
   return cudaGetLastError();
 }
